@@ -1,0 +1,417 @@
+// C-ABI entry points of libfa_b200.so (declared in include/fa_b200.h) plus
+// the host helpers the kernels share.  This is the library's only
+// translation unit: the kernel sources are included below, so the device
+// error word needs no relocatable device code.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "fa_b200.h"
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+#include "fa_fwd_kernel.cuh"
+#include "gemm_kernel.cuh"
+
+namespace fab {
+
+static_assert(FAB_OK == kOk && FAB_ERR_INVALID_ARG == kErrInvalidArg && FAB_ERR_UNSUPPORTED == kErrUnsupported &&
+                  FAB_ERR_LAUNCH == kErrLaunch && FAB_ERR_DEVICE_TIMEOUT == kErrDeviceTimeout &&
+                  FAB_ERR_CUDA == kErrCuda,
+              "public and internal return codes must agree");
+static_assert(FAB_DTYPE_F16 == kDtypeF16 && FAB_DTYPE_BF16 == kDtypeBF16 && FAB_DTYPE_F32 == kDtypeF32,
+              "public and internal dtype codes must agree");
+
+static int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+
+int ensure_smem_attr(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  const int dev = current_device();
+  if (dev < 0) return kErrCuda;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return kOk;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return kErrLaunch;
+  }
+  done.insert({kernel, dev});
+  return kOk;
+}
+
+int num_sms() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return -1;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+static bool stride_ok(int64_t stride_bytes) {
+  return stride_bytes > 0 && (stride_bytes % 16) == 0 && stride_bytes < (int64_t(1) << 40);
+}
+
+static int64_t round16(int64_t x) { return (x + 15) / 16 * 16; }
+
+int make_bhsd_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elt, int D, int S, int H, int B,
+                  int64_t s_s, int64_t s_h, int64_t s_b, int box_inner, int box_rows, CUtensorMapSwizzle swizzle) {
+  auto enc = encode_tiled_fn();
+  if (enc == nullptr) return kErrCuda;
+  if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) != 0) return kErrInvalidArg;
+  if (D <= 0 || S <= 0 || H <= 0 || B <= 0) return kErrInvalidArg;
+  // Strides of size-1 dims are never followed; give them a valid value.
+  int64_t bs = S == 1 ? round16(int64_t(D) * elt) : s_s * elt;
+  int64_t bh = H == 1 ? round16(bs * S) : s_h * elt;
+  int64_t bb = B == 1 ? round16(bh * H) : s_b * elt;
+  if (!stride_ok(bs) || !stride_ok(bh) || !stride_ok(bb)) return kErrInvalidArg;
+  cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(S), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t strides[3] = {cuuint64_t(bs), cuuint64_t(bh), cuuint64_t(bb)};
+  cuuint32_t box[4] = {cuuint32_t(box_inner), cuuint32_t(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInvalidArg;
+}
+
+int make_2d_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elt, int cols, int rows, int64_t ld,
+                int box_inner, int box_rows, CUtensorMapSwizzle swizzle) {
+  auto enc = encode_tiled_fn();
+  if (enc == nullptr) return kErrCuda;
+  if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) != 0) return kErrInvalidArg;
+  if (cols <= 0 || rows <= 0) return kErrInvalidArg;
+  const int64_t bs = rows == 1 ? round16(int64_t(cols) * elt) : ld * elt;
+  if (!stride_ok(bs)) return kErrInvalidArg;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(bs)};
+  cuuint32_t box[2] = {cuuint32_t(box_inner), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInvalidArg;
+}
+
+static int elt_size(int dtype) { return dtype == kDtypeF32 ? 4 : 2; }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Shared validation + launch for every attention entry point.
+static int attention_launch(FaLaunch L, cudaStream_t stream) {
+  if (L.dtype != kDtypeF16 && L.dtype != kDtypeBF16 && L.dtype != kDtypeF32) return kErrInvalidArg;
+  if (L.B < 0 || L.Hq < 0 || L.Hkv < 0 || L.M < 0 || L.N < 0 || L.D <= 0) return kErrInvalidArg;
+  if (L.M == 0 || L.B == 0 || L.Hq == 0) return kOk;
+  if (L.Hkv <= 0 || L.Hq % L.Hkv != 0) return kErrInvalidArg;
+  if (!(L.sm_scale > 0.f) || !std::isfinite(L.sm_scale)) return kErrUnsupported;
+  FaConfigInfo cfg;
+  int rc = fa_select_config(L.dtype, L.D, &cfg);
+  if (rc) return rc;
+  if (L.q == nullptr || L.o == nullptr) return kErrInvalidArg;
+  const int elt = elt_size(L.dtype);
+  // The epilogue stores rows with 16-byte vector stores.
+  if (!aligned16(L.o)) return kErrInvalidArg;
+  for (int64_t s : {L.o_sb, L.o_sh, L.o_ss})
+    if ((s * elt) % 16 != 0) return kErrInvalidArg;
+  if (L.lse != nullptr && (reinterpret_cast<uintptr_t>(L.lse) & 3u) != 0) return kErrInvalidArg;
+  if (L.N == 0) {
+    // No keys: the kernel only writes NaN rows; point the K/V maps at Q.
+    L.k = L.q;
+    L.v = L.q;
+    L.N = 0;
+    L.k_sb = L.q_sb;
+    L.k_sh = L.q_sh;
+    L.k_ss = L.q_ss;
+    L.v_sb = L.q_sb;
+    L.v_sh = L.q_sh;
+    L.v_ss = L.q_ss;
+    L.Hkv = L.Hq;
+  } else if (L.k == nullptr || L.v == nullptr) {
+    return kErrInvalidArg;
+  }
+  return fa_forward(L, stream);
+}
+
+}  // namespace fab
+
+using namespace fab;
+
+extern "C" {
+
+int fab_abi_version(void) { return 1; }
+
+const char* fab_error_string(int rc) {
+  switch (rc) {
+    case FAB_OK:
+      return "ok";
+    case FAB_ERR_INVALID_ARG:
+      return "invalid argument (pointer, shape, stride or alignment)";
+    case FAB_ERR_UNSUPPORTED:
+      return "unsupported configuration";
+    case FAB_ERR_LAUNCH:
+      return "kernel launch failed";
+    case FAB_ERR_DEVICE_TIMEOUT:
+      return "a kernel gave up on a bounded wait";
+    case FAB_ERR_CUDA:
+      return "CUDA runtime error";
+    default:
+      return "unknown error";
+  }
+}
+
+static int fa_basic_common(const void* q, const void* k, const void* v, void* o, float* lse, int64_t sqb,
+                           int64_t sqh, int64_t sqm, int64_t sqd, int64_t skb, int64_t skh, int64_t skn,
+                           int64_t skd, int64_t svb, int64_t svh, int64_t svn, int64_t svd, int64_t sob,
+                           int64_t soh, int64_t som, int64_t sod, int64_t slb, int64_t slh, int64_t slm, int B,
+                           int H, int M, int N, int D, float sm_scale, int causal, int has_lse, int dtype,
+                           void* stream) {
+  if (M > 0 && B > 0 && H > 0 && (sqd != 1 || sod != 1 || (N > 0 && (skd != 1 || svd != 1)))) return kErrInvalidArg;
+  if (has_lse && lse == nullptr) return kErrInvalidArg;
+  FaLaunch L{};
+  L.q = q;
+  L.k = k;
+  L.v = v;
+  L.o = o;
+  L.lse = has_lse ? lse : nullptr;
+  L.q_sb = sqb;
+  L.q_sh = sqh;
+  L.q_ss = sqm;
+  L.k_sb = skb;
+  L.k_sh = skh;
+  L.k_ss = skn;
+  L.v_sb = svb;
+  L.v_sh = svh;
+  L.v_ss = svn;
+  L.o_sb = sob;
+  L.o_sh = soh;
+  L.o_ss = som;
+  L.l_sb = slb;
+  L.l_sh = slh;
+  L.l_ss = slm;
+  L.B = B;
+  L.Hq = H;
+  L.Hkv = H;
+  L.M = M;
+  L.N = N;
+  L.D = D;
+  L.dtype = dtype;
+  L.sm_scale = sm_scale;
+  L.causal = causal ? 1 : 0;
+  return attention_launch(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_flash_attn_fwd_basic(const void* q, const void* k, const void* v, void* o, float* lse, int64_t stride_qb,
+                             int64_t stride_qh, int64_t stride_qm, int64_t stride_qd, int64_t stride_kb,
+                             int64_t stride_kh, int64_t stride_kn, int64_t stride_kd, int64_t stride_vb,
+                             int64_t stride_vh, int64_t stride_vn, int64_t stride_vd, int64_t stride_ob,
+                             int64_t stride_oh, int64_t stride_om, int64_t stride_od, int64_t stride_lb,
+                             int64_t stride_lh, int64_t stride_lm, int B, int H, int M, int N, int D,
+                             float sm_scale, int causal, int has_lse, int dtype, void* stream) {
+  return fa_basic_common(q, k, v, o, lse, stride_qb, stride_qh, stride_qm, stride_qd, stride_kb, stride_kh,
+                         stride_kn, stride_kd, stride_vb, stride_vh, stride_vn, stride_vd, stride_ob, stride_oh,
+                         stride_om, stride_od, stride_lb, stride_lh, stride_lm, B, H, M, N, D, sm_scale, causal,
+                         has_lse, dtype, stream);
+}
+
+int fab_flash_attn_fwd_optimize_shared_mem(const void* q, const void* k, const void* v, void* o, float* lse,
+                                           int64_t stride_qb, int64_t stride_qh, int64_t stride_qm,
+                                           int64_t stride_qd, int64_t stride_kb, int64_t stride_kh,
+                                           int64_t stride_kn, int64_t stride_kd, int64_t stride_vb,
+                                           int64_t stride_vh, int64_t stride_vn, int64_t stride_vd,
+                                           int64_t stride_ob, int64_t stride_oh, int64_t stride_om,
+                                           int64_t stride_od, int64_t stride_lb, int64_t stride_lh,
+                                           int64_t stride_lm, int B, int H, int M, int N, int D, float sm_scale,
+                                           int causal, int has_lse, int dtype, void* stream) {
+  return fa_basic_common(q, k, v, o, lse, stride_qb, stride_qh, stride_qm, stride_qd, stride_kb, stride_kh,
+                         stride_kn, stride_kd, stride_vb, stride_vh, stride_vn, stride_vd, stride_ob, stride_oh,
+                         stride_om, stride_od, stride_lb, stride_lh, stride_lm, B, H, M, N, D, sm_scale, causal,
+                         has_lse, dtype, stream);
+}
+
+int fab_flash_attn_fwd_block_d_nomask_contiguous(const void* q, const void* k, const void* v, void* o, int B,
+                                                 int H, int M, int N, int D, float sm_scale, int dtype,
+                                                 void* stream) {
+  const int64_t qs = D, qh = int64_t(M) * D, qb = qh * H;
+  const int64_t ks = D, kh = int64_t(N) * D, kb = kh * H;
+  return fa_basic_common(q, k, v, o, nullptr, qb, qh, qs, 1, kb, kh, ks, 1, kb, kh, ks, 1, qb, qh, qs, 1, 0, 0, 0,
+                         B, H, M, N, D, sm_scale, 0, 0, dtype, stream);
+}
+
+int fab_attention_fwd(const fab_attention_params* p, void* stream) {
+  if (p == nullptr) return kErrInvalidArg;
+  FaLaunch L{};
+  L.q = p->q;
+  L.k = p->k;
+  L.v = p->v;
+  L.o = p->o;
+  L.lse = p->lse;
+  L.q_sb = p->q_stride_b;
+  L.q_sh = p->q_stride_h;
+  L.q_ss = p->q_stride_s;
+  L.k_sb = p->k_stride_b;
+  L.k_sh = p->k_stride_h;
+  L.k_ss = p->k_stride_s;
+  L.v_sb = p->v_stride_b;
+  L.v_sh = p->v_stride_h;
+  L.v_ss = p->v_stride_s;
+  L.o_sb = p->o_stride_b;
+  L.o_sh = p->o_stride_h;
+  L.o_ss = p->o_stride_s;
+  L.l_sb = p->lse_stride_b;
+  L.l_sh = p->lse_stride_h;
+  L.l_ss = p->lse_stride_s;
+  L.B = p->batch;
+  L.Hq = p->heads_q;
+  L.Hkv = p->heads_kv;
+  L.M = p->seqlen_q;
+  L.N = p->seqlen_k;
+  L.D = p->head_dim;
+  L.dtype = p->dtype;
+  L.sm_scale = p->sm_scale;
+  L.causal = p->causal ? 1 : 0;
+  return attention_launch(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_gemm(const fab_gemm_params* p, void* stream) {
+  if (p == nullptr) return kErrInvalidArg;
+  if (p->M < 0 || p->N < 0 || p->K < 0) return kErrInvalidArg;
+  if (p->M == 0 || p->N == 0) return kOk;
+  for (int dt : {p->in_dtype, p->out_dtype})
+    if (dt != kDtypeF16 && dt != kDtypeBF16 && dt != kDtypeF32) return kErrInvalidArg;
+  if (p->c == nullptr || !aligned16(p->c)) return kErrInvalidArg;
+  const int oe = elt_size(p->out_dtype);
+  if ((p->ldc * oe) % 16 != 0 || p->ldc < p->N) return kErrInvalidArg;
+  if (p->K == 0) {
+    // Empty contraction: C = 0.
+    cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(p->N) * oe, size_t(p->M),
+                                      static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? kOk : kErrCuda;
+  }
+  if (p->lda < p->K || p->ldb < p->N) return kErrInvalidArg;
+  GemmLaunch L{};
+  L.a = p->a;
+  L.b = p->b;
+  L.c = p->c;
+  L.lda = p->lda;
+  L.ldb = p->ldb;
+  L.ldc = p->ldc;
+  L.M = p->M;
+  L.N = p->N;
+  L.K = p->K;
+  L.in_dtype = p->in_dtype;
+  L.out_dtype = p->out_dtype;
+  L.round_f16 = p->round_f16;
+  L.group_m = p->group_m;
+  return gemm_forward(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_matmul_contiguous(const void* a, const void* b, void* c, int M, int N, int K, int in_dtype, int out_dtype,
+                          int round_f16, void* stream) {
+  fab_gemm_params p{};
+  p.a = a;
+  p.b = b;
+  p.c = c;
+  p.lda = K;
+  p.ldb = N;
+  p.ldc = N;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.in_dtype = in_dtype;
+  p.out_dtype = out_dtype;
+  p.round_f16 = round_f16;
+  p.group_m = 8;
+  return fab_gemm(&p, stream);
+}
+
+int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out) {
+  if (out == nullptr) return kErrInvalidArg;
+  FaConfigInfo c;
+  int rc = fa_select_config(dtype, head_dim, &c);
+  if (rc) return rc;
+  out->head_dim_padded = c.d_pad;
+  out->q_tiles_per_cta = c.nq;
+  out->block_n = c.bn;
+  out->stages = c.stages;
+  out->threads = c.threads;
+  out->smem_bytes = c.smem_bytes;
+  out->tmem_columns = c.tmem_cols;
+  return kOk;
+}
+
+int fab_kernel_attrs_query(int which, int dtype, int head_dim, fab_kernel_attrs* out) {
+  if (out == nullptr) return kErrInvalidArg;
+  int regs = 0, smem = 0, threads = 0, rc;
+  if (which == FAB_KERNEL_ATTENTION)
+    rc = fa_kernel_attrs(dtype, head_dim, &regs, &smem, &threads);
+  else if (which == FAB_KERNEL_MATMUL)
+    rc = gemm_kernel_attrs(dtype, &regs, &smem, &threads);
+  else
+    return kErrInvalidArg;
+  if (rc) return rc;
+  out->registers_per_thread = regs;
+  out->shared_bytes = smem;
+  out->threads = threads;
+  return kOk;
+}
+
+int fab_device_limits_query(int device, fab_device_limits* out) {
+  if (out == nullptr) return kErrInvalidArg;
+  struct {
+    cudaDeviceAttr attr;
+    int* dst;
+  } q[] = {
+      {cudaDevAttrMaxSharedMemoryPerMultiprocessor, &out->shared_bytes_per_sm},
+      {cudaDevAttrMaxSharedMemoryPerBlockOptin, &out->shared_bytes_per_block_optin},
+      {cudaDevAttrMaxRegistersPerMultiprocessor, &out->registers_per_sm},
+      {cudaDevAttrWarpSize, &out->warp_size},
+      {cudaDevAttrMaxThreadsPerBlock, &out->max_threads_per_block},
+      {cudaDevAttrMultiProcessorCount, &out->multiprocessor_count},
+      {cudaDevAttrComputeCapabilityMajor, &out->cc_major},
+      {cudaDevAttrComputeCapabilityMinor, &out->cc_minor},
+  };
+  for (auto& e : q)
+    if (cudaDeviceGetAttribute(e.dst, e.attr, device) != cudaSuccess) {
+      cudaGetLastError();
+      return kErrCuda;
+    }
+  return kOk;
+}
+
+int fab_get_device_error(int* code) {
+  if (code == nullptr) return kErrInvalidArg;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fab_device_error, sizeof(int)) != cudaSuccess) return kErrCuda;
+  if (v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_fab_device_error, &zero, sizeof(int)) != cudaSuccess) return kErrCuda;
+  }
+  *code = v;
+  return kOk;
+}
+
+}  // extern "C"

@@ -1,0 +1,556 @@
+// FlashAttention forward for sm_100a: O = softmax(scale * Q K^T [+ causal mask]) V,
+// optional LSE = rowmax + log(rowsum) in natural-log units.
+//
+// Same mathematics as the reference's three Triton kernels
+// (flash_atten.py:14-133 basic, :136-258 optimize_shared_mem, :261-361
+// block_d_nomask_contiguous): online softmax over KV tiles in fp32, P rounded
+// to the input dtype before the P*V product, final O = acc / l.
+//
+// B200 structure (one CTA per SM, 128 + NQ*128 threads):
+//   warp 0      TMA producer: Q tiles once, then a ring of K and V tiles.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 4..   one 128-thread softmax group per 128-row Q tile; thread r of
+//               the group owns row r (TMEM lane r) for the whole kernel.
+// Per KV tile j and Q tile i:
+//   S_i   = Q_i K_j^T            tcgen05.mma SS, fp32 in TMEM
+//   P_i   = exp2(S_i*c - m_i)    softmax group: tcgen05.ld S, tcgen05.st P
+//                                (P overwrites the first columns of S_i)
+//   O_i  += P_i V_j              tcgen05.mma TS (A = P from TMEM)
+// With two Q tiles per CTA the tensor core computes one tile's MMAs while the
+// other tile's softmax runs.  The running max is only moved when it grows by
+// more than 2^8, so O is rescaled rarely; the final O / l is unaffected.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+namespace fab {
+
+template <int kElt, int kDP, int kNQ, int kBN, int kStages>
+struct FaCfg {
+  static constexpr int kBM = 128;                    // rows per Q tile (TMEM lanes)
+  static constexpr int kAtom = 128 / kElt;           // elements per 128-byte swizzle atom
+  static constexpr int kNumAtoms = kDP / kAtom;      // atoms across the head dim
+  static constexpr int kQAtomBytes = kBM * 128;
+  static constexpr int kQTileBytes = kQAtomBytes * kNumAtoms;
+  static constexpr int kKVAtomBytes = kBN * 128;
+  static constexpr int kKVTileBytes = kKVAtomBytes * kNumAtoms;
+  static constexpr int kKInstr = 32 / kElt;          // K extent of one MMA instruction
+  static constexpr int kThreads = 128 + kNQ * 128;
+  static constexpr int kPCols = kBN * kElt / 4;      // 32-bit TMEM columns of one P tile
+  static constexpr int kTmemUsed = kNQ * (kBN + kDP);
+  static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
+                                    : kTmemUsed <= 256 ? 256 : 512;
+  static constexpr int kNumBars = 1 + 4 * kStages + 3 * kNQ + 1;
+  static constexpr int kDataBytes = kNQ * kQTileBytes + 2 * kStages * kKVTileBytes;
+  static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
+  static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
+  static_assert(kTmemUsed <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  __host__ __device__ static constexpr int tmem_s(int i) { return i * kBN; }
+  __host__ __device__ static constexpr int tmem_o(int i) { return kNQ * kBN + i * kDP; }
+};
+
+template <typename T>
+struct ElemOps;
+
+template <>
+struct ElemOps<__nv_bfloat16> {
+  static constexpr uint32_t kFmt = kFmtBF16;
+  __device__ static uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <>
+struct ElemOps<__half> {
+  static constexpr uint32_t kFmt = kFmtF16;
+  __device__ static uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <>
+struct ElemOps<float> {
+  static constexpr uint32_t kFmt = kFmtTF32;
+  __device__ static uint32_t pack2(float a, float) { return __float_as_uint(a); }
+};
+
+// Store 32 fp32 values (already normalised) as one 32-column chunk of an O row.
+template <typename T>
+__device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int ncols) {
+  if constexpr (sizeof(T) == 2) {
+    uint32_t w[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = ElemOps<T>::pack2(v[2 * e], v[2 * e + 1]);
+    if (ncols >= 32) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+    } else {
+      const T* src = reinterpret_cast<const T*>(w);
+      for (int e = 0; e < ncols; ++e) dst[e] = src[e];
+    }
+  } else {
+    if (ncols >= 32) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d4[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    } else {
+      for (int e = 0; e < ncols; ++e) dst[e] = v[e];
+    }
+  }
+}
+
+template <typename T, int kDP, int kNQ, int kBN, int kStages>
+__global__ void __launch_bounds__(128 + kNQ * 128, 1)
+    fa_fwd_kernel(const __grid_constant__ FaKernelParams p, const __grid_constant__ CUtensorMap tm_q,
+                  const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages>;
+  constexpr float kNegInf = -INFINITY;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kNQ * C::kQTileBytes;
+  uint8_t* sV = sK + kStages * C::kKVTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * C::kKVTileBytes);
+  uint64_t* bar_q_full = bars;
+  uint64_t* bar_k_full = bars + 1;
+  uint64_t* bar_v_full = bar_k_full + kStages;
+  uint64_t* bar_k_empty = bar_v_full + kStages;
+  uint64_t* bar_v_empty = bar_k_empty + kStages;
+  uint64_t* bar_s_full = bar_v_empty + kStages;
+  uint64_t* bar_p_full = bar_s_full + kNQ;
+  uint64_t* bar_o_done = bar_p_full + kNQ;
+  uint64_t* bar_teardown = bar_o_done + kNQ;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_teardown + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work item: heads are the slow index so CTAs resident together share K/V
+  // in L2; within a head the longest (causal) row blocks start first.
+  const int bh = blockIdx.x / p.num_m_blocks;
+  const int mblk = p.num_m_blocks - 1 - (blockIdx.x % p.num_m_blocks);
+  const int b = bh / p.Hq;
+  const int h = bh % p.Hq;
+  const int hk = h / p.group;
+  const int m0 = mblk * kNQ * C::kBM;
+  int n_end = p.N;
+  if (p.causal) n_end = min(p.N, min(p.M, m0 + kNQ * C::kBM));
+  const int nt = (n_end + kBN - 1) / kBN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_k_full + s, 1);
+      mbar_init(bar_v_full + s, 1);
+      mbar_init(bar_k_empty + s, 1);
+      mbar_init(bar_v_empty + s, 1);
+    }
+    for (int i = 0; i < kNQ; ++i) {
+      mbar_init(bar_s_full + i, 1);
+      mbar_init(bar_p_full + i, C::kBM);
+      mbar_init(bar_o_done + i, 1);
+    }
+    mbar_init(bar_teardown, 1);
+    *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemAlloc);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const bool skip = *abort_flag != 0;
+
+  if (!skip && warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    mbar_arrive_expect_tx(bar_q_full, kNQ * C::kQTileBytes);
+    for (int i = 0; i < kNQ; ++i)
+      for (int a = 0; a < C::kNumAtoms; ++a)
+        tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full, a * C::kAtom,
+                    m0 + i * C::kBM, h, b);
+    int issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % kStages;
+      const uint32_t ph = (j / kStages) & 1;
+      if (!mbar_wait(bar_k_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
+      mbar_arrive_expect_tx(bar_k_full + s, C::kKVTileBytes);
+      for (int a = 0; a < C::kNumAtoms; ++a)
+        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, j * kBN,
+                    hk, b);
+      if (!mbar_wait(bar_v_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) {
+        issued = 2 * j + 1;
+        break;
+      }
+      mbar_arrive_expect_tx(bar_v_full + s, C::kKVTileBytes);
+      for (int a = 0; a < C::kNumAtoms; ++a)
+        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, j * kBN,
+                    hk, b);
+      issued = 2 * j + 2;
+    }
+    // Never leave this CTA with bulk copies still landing in its smem: wait
+    // (bounded) for the last load issued into every stage.
+    volatile int no_abort = 0;
+    mbar_wait(bar_q_full, 0, &no_abort, kDevTimeoutTeardown);
+    for (int x = max(0, issued - 2 * kStages); x < issued; ++x) {
+      const int j = x >> 1;
+      uint64_t* full = (x & 1) ? bar_v_full : bar_k_full;
+      mbar_wait(full + (j % kStages), (j / kStages) & 1, &no_abort, kDevTimeoutTeardown);
+    }
+  } else if (!skip && warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t kFmt = ElemOps<T>::kFmt;
+    constexpr uint32_t idesc_qk = umma_idesc(kFmt, C::kBM, kBN, 0, 0);
+    constexpr uint32_t idesc_pv = umma_idesc(kFmt, C::kBM, kDP, 0, 1);
+    const uint32_t sq_addr = smem_u32(sQ);
+    const uint32_t sk_addr = smem_u32(sK);
+    const uint32_t sv_addr = smem_u32(sV);
+    auto issue_qk = [&](int i, int s) {
+      const uint32_t d = tmem + C::tmem_s(i);
+#pragma unroll
+      for (int kk = 0; kk < kDP / C::kKInstr; ++kk) {
+        const int a = kk >> 2;
+        const uint32_t off = (kk & 3) * 32;
+        const uint64_t ad = umma_desc_sw128(sq_addr + i * C::kQTileBytes + a * C::kQAtomBytes + off, 16, 1024);
+        const uint64_t bd = umma_desc_sw128(sk_addr + s * C::kKVTileBytes + a * C::kKVAtomBytes + off, 16, 1024);
+        if constexpr (sizeof(T) == 4)
+          mma_ss_tf32(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        else
+          mma_ss_f16(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+      }
+    };
+    auto issue_pv = [&](int i, int s, bool acc) {
+      const uint32_t d = tmem + C::tmem_o(i);
+      const uint32_t pa = tmem + C::tmem_s(i);
+#pragma unroll
+      for (int kk = 0; kk < kBN / C::kKInstr; ++kk) {
+        const uint64_t bd = umma_desc_mn<sizeof(T)>(sv_addr + s * C::kKVTileBytes + kk * C::kKInstr * 128,
+                                                    C::kKVAtomBytes);
+        const uint32_t a_t = pa + kk * (C::kKInstr * static_cast<int>(sizeof(T)) / 4);
+        const uint32_t accum = (acc || kk > 0) ? 1u : 0u;
+        if constexpr (sizeof(T) == 4)
+          mma_ts_tf32(d, a_t, bd, idesc_pv, accum);
+        else
+          mma_ts_f16(d, a_t, bd, idesc_pv, accum);
+      }
+    };
+
+    bool ok = mbar_wait(bar_q_full, 0, abort_flag, kDevTimeoutQ);
+    bool any_issued = false;
+    if (ok && nt > 0) {
+      ok = mbar_wait(bar_k_full, 0, abort_flag, kDevTimeoutKV);
+      if (ok) {
+        tc_fence_after();
+        for (int i = 0; i < kNQ; ++i) {
+          issue_qk(i, 0);
+          mma_commit(bar_s_full + i);
+        }
+        mma_commit(bar_k_empty);
+        any_issued = true;
+      }
+      for (int j = 0; ok && j < nt; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        if (!(ok = mbar_wait(bar_v_full + s, ph, abort_flag, kDevTimeoutKV))) break;
+        for (int i = 0; i < kNQ; ++i) {
+          if (!(ok = mbar_wait(bar_p_full + i, j & 1, abort_flag, kDevTimeoutP))) break;
+          tc_fence_after();
+          issue_pv(i, s, j > 0);
+          mma_commit(bar_o_done + i);
+          if (i == kNQ - 1) mma_commit(bar_v_empty + s);
+          if (j + 1 < nt) {
+            if (i == 0 && !(ok = mbar_wait(bar_k_full + s1, ph1, abort_flag, kDevTimeoutKV))) break;
+            // S_i(j+1) reuses the TMEM columns that P_i(j) occupies: start it
+            // only after the P*V product that reads them has completed.
+            if (!(ok = mbar_wait(bar_o_done + i, j & 1, abort_flag, kDevTimeoutO))) break;
+            tc_fence_after();
+            issue_qk(i, s1);
+            mma_commit(bar_s_full + i);
+            if (i == kNQ - 1) mma_commit(bar_k_empty + s1);
+          }
+        }
+      }
+    }
+    if (any_issued) {
+      // Drain the tensor pipe before TMEM is released.
+      volatile int no_abort = 0;
+      mma_commit(bar_teardown);
+      mbar_wait(bar_teardown, 0, &no_abort, kDevTimeoutTeardown);
+    }
+  } else if (!skip && warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int i = (warp - 4) >> 2;
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const int row = m0 + i * C::kBM + r;
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + C::tmem_s(i);
+    const uint32_t t_o = tmem + lane_base + C::tmem_o(i);
+    const float c = p.scale_log2;
+    float m_run = kNegInf;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!(ok = mbar_wait_warp(bar_s_full + i, j & 1, abort_flag, kDevTimeoutS))) break;
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int cc = 0; cc < kBN / 32; ++cc) {
+        uint32_t rr[32];
+        tmem_ld32(t_s + cc * 32, rr);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[cc * 32 + e] = __uint_as_float(rr[e]);
+      }
+      tmem_wait_ld();
+      const int col0 = j * kBN;
+      const bool need_mask = (col0 + kBN > p.N) || (p.causal && col0 + kBN - 1 > row);
+      if (need_mask) {
+        const int lim = p.causal ? min(p.N, row + 1) : p.N;
+#pragma unroll
+        for (int e = 0; e < kBN; ++e)
+          if (col0 + e >= lim) s[e] = kNegInf;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int e = 1; e < kBN; ++e) mx = fmaxf(mx, s[e]);
+      const float m_cand = fmaxf(m_run, mx * c);
+      const bool rescale = m_cand > m_run + 8.0f;
+      const float m_new = rescale ? m_cand : m_run;
+      const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.0f;
+      const float m_base = (m_new == kNegInf) ? 0.f : m_new;
+      float lsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < kBN / 32; ++cc) {
+        if constexpr (sizeof(T) == 2) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(s[cc * 32 + 2 * e], c, -m_base));
+            const float p1 = ex2_approx(fmaf(s[cc * 32 + 2 * e + 1], c, -m_base));
+            lsum += p0 + p1;
+            pk[e] = ElemOps<T>::pack2(p0, p1);
+          }
+          tmem_st16(t_s + cc * 16, pk);
+        } else {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float p0 = ex2_approx(fmaf(s[cc * 32 + e], c, -m_base));
+            lsum += p0;
+            pk[e] = __float_as_uint(p0);
+          }
+          tmem_st32(t_s + cc * 32, pk);
+        }
+      }
+      tmem_wait_st();
+      if (j > 0) {
+        // O_i must hold the finished product of KV tile j-1 before it is
+        // rescaled and before P_i(j) is released to the MMA issuer.
+        if (!(ok = mbar_wait_warp(bar_o_done + i, (j - 1) & 1, abort_flag, kDevTimeoutO))) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int cc = 0; cc < kDP / 32; ++cc) {
+            uint32_t rr[32];
+            tmem_ld32(t_o + cc * 32, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+            tmem_st32(t_o + cc * 32, rr);
+          }
+          tmem_wait_st();
+        }
+      }
+      l_run = l_run * alpha + lsum;
+      m_run = m_new;
+      tc_fence_before();
+      mbar_arrive(bar_p_full + i);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sm;
+    if (ok && nt > 0) {
+      ok = mbar_wait_warp(bar_o_done + i, (nt - 1) & 1, abort_flag, kDevTimeoutO);
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l_run;
+#pragma unroll 1
+        for (int cc = 0; cc < kDP / 32; ++cc) {
+          uint32_t rr[32];
+          tmem_ld32(t_o + cc * 32, rr);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]) * inv_l;
+          const int ncols = min(32, p.D - cc * 32);
+          if (row < p.M && ncols > 0) store_o_chunk<T>(orow + cc * 32, v, ncols);
+        }
+        if (p.lse != nullptr && row < p.M) {
+          const float m_base = (m_run == kNegInf) ? 0.f : m_run;
+          p.lse[b * p.l_sb + h * p.l_sh + static_cast<int64_t>(row) * p.l_sm] =
+              (m_base + log2f(l_run)) * 0.6931471805599453f;
+        }
+      }
+    } else if (ok && nt == 0 && row < p.M) {
+      // No keys at all: 0/0 like the reference's acc / l_i.
+      for (int d = 0; d < p.D; ++d) orow[d] = static_cast<T>(NAN);
+      if (p.lse != nullptr) p.lse[b * p.l_sb + h * p.l_sh + static_cast<int64_t>(row) * p.l_sm] = kNegInf;
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemAlloc);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+template <typename T, int kDP, int kNQ, int kBN, int kStages>
+static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages>;
+  auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kStages>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (rc) return rc;
+  CUtensorMap tq, tk, tv;
+  const int elt = sizeof(T);
+  const CUtensorMapDataType dt = elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : L.dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // V is the MN-major operand of P*V: tf32 needs the 32-byte-chunk swizzle there.
+  const CUtensorMapSwizzle v_swz = elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, L.M, L.Hq, L.B, L.q_ss, L.q_sh, L.q_sb, C::kAtom, C::kBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_bhsd_map(&tk, L.k, dt, elt, L.D, L.N, L.Hkv, L.B, L.k_ss, L.k_sh, L.k_sb, C::kAtom, kBN,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_bhsd_map(&tv, L.v, dt, elt, L.D, L.N, L.Hkv, L.B, L.v_ss, L.v_sh, L.v_sb, C::kAtom, kBN, v_swz);
+  if (rc) return rc;
+  FaKernelParams kp;
+  kp.o = L.o;
+  kp.lse = L.lse;
+  kp.o_sb = L.o_sb;
+  kp.o_sh = L.o_sh;
+  kp.o_sm = L.o_ss;
+  kp.l_sb = L.l_sb;
+  kp.l_sh = L.l_sh;
+  kp.l_sm = L.l_ss;
+  kp.B = L.B;
+  kp.Hq = L.Hq;
+  kp.M = L.M;
+  kp.N = L.N;
+  kp.D = L.D;
+  kp.group = L.Hq / L.Hkv;
+  kp.scale_log2 = L.sm_scale * 1.4426950408889634f;
+  kp.causal = L.causal;
+  kp.num_m_blocks = (L.M + kNQ * C::kBM - 1) / (kNQ * C::kBM);
+  const long long grid = static_cast<long long>(kp.num_m_blocks) * L.B * L.Hq;
+  if (grid <= 0) return 0;
+  if (grid > 0x7fffffffLL) return kErrInvalidArg;
+  kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, stream>>>(kp, tq, tk, tv);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+}
+
+// Per-(dtype, padded head dim) tile table for sm_100a.  Returns the chosen
+// configuration's static facts for the tuner and the launch.
+int fa_select_config(int dtype, int D, FaConfigInfo* out) {
+  if (D <= 0) return kErrInvalidArg;
+  FaConfigInfo c{};
+  if (dtype == kDtypeF32) {
+    if (D <= 64) {
+      c = {64, 2, 128, 2, FaCfg<4, 64, 2, 128, 2>::kThreads, FaCfg<4, 64, 2, 128, 2>::kSmemBytes,
+           FaCfg<4, 64, 2, 128, 2>::kTmemAlloc};
+    } else if (D <= 128) {
+      c = {128, 1, 64, 2, FaCfg<4, 128, 1, 64, 2>::kThreads, FaCfg<4, 128, 1, 64, 2>::kSmemBytes,
+           FaCfg<4, 128, 1, 64, 2>::kTmemAlloc};
+    } else {
+      return kErrUnsupported;
+    }
+  } else if (dtype == kDtypeF16 || dtype == kDtypeBF16) {
+    if (D <= 64) {
+      c = {64, 2, 128, 3, FaCfg<2, 64, 2, 128, 3>::kThreads, FaCfg<2, 64, 2, 128, 3>::kSmemBytes,
+           FaCfg<2, 64, 2, 128, 3>::kTmemAlloc};
+    } else if (D <= 128) {
+      c = {128, 2, 128, 2, FaCfg<2, 128, 2, 128, 2>::kThreads, FaCfg<2, 128, 2, 128, 2>::kSmemBytes,
+           FaCfg<2, 128, 2, 128, 2>::kTmemAlloc};
+    } else if (D <= 256) {
+      c = {256, 1, 64, 2, FaCfg<2, 256, 1, 64, 2>::kThreads, FaCfg<2, 256, 1, 64, 2>::kSmemBytes,
+           FaCfg<2, 256, 1, 64, 2>::kTmemAlloc};
+    } else {
+      return kErrUnsupported;
+    }
+  } else {
+    return kErrInvalidArg;
+  }
+  *out = c;
+  return 0;
+}
+
+int fa_forward(const FaLaunch& L, cudaStream_t stream) {
+  FaConfigInfo c;
+  int rc = fa_select_config(L.dtype, L.D, &c);
+  if (rc) return rc;
+  if (L.dtype == kDtypeF32) {
+    if (c.d_pad == 64) return launch_fa<float, 64, 2, 128, 2>(L, stream);
+    return launch_fa<float, 128, 1, 64, 2>(L, stream);
+  }
+  if (L.dtype == kDtypeBF16) {
+    if (c.d_pad == 64) return launch_fa<__nv_bfloat16, 64, 2, 128, 3>(L, stream);
+    if (c.d_pad == 128) return launch_fa<__nv_bfloat16, 128, 2, 128, 2>(L, stream);
+    return launch_fa<__nv_bfloat16, 256, 1, 64, 2>(L, stream);
+  }
+  if (c.d_pad == 64) return launch_fa<__half, 64, 2, 128, 3>(L, stream);
+  if (c.d_pad == 128) return launch_fa<__half, 128, 2, 128, 2>(L, stream);
+  return launch_fa<__half, 256, 1, 64, 2>(L, stream);
+}
+
+int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads) {
+  FaConfigInfo c;
+  int rc = fa_select_config(dtype, D, &c);
+  if (rc) return rc;
+  cudaFuncAttributes a{};
+  cudaError_t e = cudaSuccess;
+  const void* k = nullptr;
+  if (dtype == kDtypeF32) {
+    k = c.d_pad == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<float, 64, 2, 128, 2>)
+                      : reinterpret_cast<const void*>(fa_fwd_kernel<float, 128, 1, 64, 2>);
+  } else if (dtype == kDtypeBF16) {
+    k = c.d_pad == 64    ? reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 64, 2, 128, 3>)
+        : c.d_pad == 128 ? reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 128, 2, 128, 2>)
+                         : reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 256, 1, 64, 2>);
+  } else {
+    k = c.d_pad == 64    ? reinterpret_cast<const void*>(fa_fwd_kernel<__half, 64, 2, 128, 3>)
+        : c.d_pad == 128 ? reinterpret_cast<const void*>(fa_fwd_kernel<__half, 128, 2, 128, 2>)
+                         : reinterpret_cast<const void*>(fa_fwd_kernel<__half, 256, 1, 64, 2>);
+  }
+  e = cudaFuncGetAttributes(&a, k);
+  if (e != cudaSuccess) return kErrLaunch;
+  *regs = a.numRegs;
+  *smem = c.smem_bytes;
+  *threads = c.threads;
+  return 0;
+}
+
+}  // namespace fab

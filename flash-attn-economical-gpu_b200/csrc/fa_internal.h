@@ -1,0 +1,100 @@
+// Internal (C++) declarations shared by the kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace fab {
+
+// Return codes (mirrored by the public FAB_* constants in include/fa_b200.h).
+enum : int {
+  kOk = 0,
+  kErrInvalidArg = 1,
+  kErrUnsupported = 2,
+  kErrLaunch = 3,
+  kErrDeviceTimeout = 4,
+  kErrCuda = 5,
+};
+
+enum : int { kDtypeF16 = 0, kDtypeBF16 = 1, kDtypeF32 = 2 };
+
+// What the FlashAttention kernel reads from its parameter block.
+struct FaKernelParams {
+  void* o;
+  float* lse;
+  int64_t o_sb, o_sh, o_sm;
+  int64_t l_sb, l_sh, l_sm;
+  int B, Hq, M, N, D;
+  int group;
+  float scale_log2;
+  int causal;
+  int num_m_blocks;
+};
+
+// A fully validated attention launch (element strides, unit stride on D).
+struct FaLaunch {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  int64_t q_sb, q_sh, q_ss;
+  int64_t k_sb, k_sh, k_ss;
+  int64_t v_sb, v_sh, v_ss;
+  int64_t o_sb, o_sh, o_ss;
+  int64_t l_sb, l_sh, l_ss;
+  int B, Hq, Hkv, M, N, D;
+  int dtype;
+  float sm_scale;
+  int causal;
+};
+
+struct FaConfigInfo {
+  int d_pad;
+  int nq;
+  int bn;
+  int stages;
+  int threads;
+  int smem_bytes;
+  int tmem_cols;
+};
+
+struct GemmKernelParams {
+  void* c;
+  int64_t ldc;
+  int M, N, K;
+  int group_m;
+  int round_f16;
+};
+
+struct GemmLaunch {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t lda, ldb, ldc;
+  int M, N, K;
+  int in_dtype, out_dtype;
+  int round_f16;
+  int group_m;
+};
+
+int fa_select_config(int dtype, int D, FaConfigInfo* out);
+int fa_forward(const FaLaunch& L, cudaStream_t stream);
+int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads);
+int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
+int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads);
+
+// Helpers implemented in capi.cu.
+int ensure_smem_attr(const void* kernel, int bytes);
+int num_sms();
+// 4-D [B, H, S, D] tensor map with unit stride on D, 128-byte swizzle,
+// box = {atom, rows, 1, 1}.
+int make_bhsd_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elt, int D, int S, int H, int B,
+                  int64_t s_s, int64_t s_h, int64_t s_b, int box_inner, int box_rows, CUtensorMapSwizzle swizzle);
+// 2-D [rows, cols] row-major tensor map, 128-byte swizzle, box = {inner, rows}.
+int make_2d_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elt, int cols, int rows, int64_t ld,
+                int box_inner, int box_rows, CUtensorMapSwizzle swizzle);
+
+}  // namespace fab

@@ -1,0 +1,321 @@
+// Dense matmul for sm_100a: C[M,N] = A[M,K] * B[K,N], row-major A and B,
+// fp32 accumulation in TMEM.  Same contraction and output rounding as the
+// reference's Triton `_matmul_contiguous_kernel` (mma.py:8-52): the fp32
+// accumulator is rounded to fp16 before the store when `round_f16` is set
+// (the reference always does `accumulator.to(tl.float16)`, mma.py:52), then
+// stored in C's dtype.
+//
+// B200 structure: persistent grid (one CTA per SM), 128x256 output tiles in
+// grouped order (GROUP_M rows of tiles share B in L2, as mma.py:22-30 does),
+// a 4-stage TMA ring of A (K-major) and B (N-major) tiles, one thread issuing
+// tcgen05.mma (M=128, N=256) into a double-buffered TMEM accumulator, and a
+// 128-thread epilogue that drains one accumulator while the next tile's main
+// loop runs.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "fa_internal.h"
+#include "ptx.cuh"
+
+namespace fab {
+
+template <int kElt>
+struct GemmCfg {
+  static constexpr int kBM = 128;
+  static constexpr int kBN = 256;
+  static constexpr int kBK = 128 / kElt;             // one 128-byte swizzle atom of K
+  static constexpr int kStages = 4;
+  static constexpr int kKInstr = 32 / kElt;
+  static constexpr int kABytes = kBM * 128;          // 128 rows x one atom
+  static constexpr int kBAtomN = 128 / kElt;         // N elements per B atom
+  static constexpr int kBAtomBytes = kBK * 128;      // kBK rows x 128 B
+  static constexpr int kBBytes = (kBN / kBAtomN) * kBAtomBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kThreads = 256;
+  static constexpr int kTmemCols = 512;              // 2 x 256 fp32 accumulators
+  static constexpr int kNumBars = 2 * kStages + 4 + 1;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 16;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <typename Tin>
+struct GemmFmt;
+template <>
+struct GemmFmt<__nv_bfloat16> {
+  static constexpr uint32_t kFmt = kFmtBF16;
+};
+template <>
+struct GemmFmt<__half> {
+  static constexpr uint32_t kFmt = kFmtF16;
+};
+template <>
+struct GemmFmt<float> {
+  static constexpr uint32_t kFmt = kFmtTF32;
+};
+
+__device__ __forceinline__ void gemm_tile_coords(int t, int num_pid_m, int num_pid_n, int group_m, int* pm, int* pn) {
+  const int per_group = group_m * num_pid_n;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gsize = min(num_pid_m - first_m, group_m);
+  const int local = t - g * per_group;
+  *pm = first_m + local % gsize;
+  *pn = local / gsize;
+}
+
+template <typename Tout>
+__device__ __forceinline__ void gemm_store_chunk(Tout* dst, const float (&v)[32], int ncols, bool round_f16) {
+  float w[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) w[e] = round_f16 ? __half2float(__float2half_rn(v[e])) : v[e];
+  if constexpr (sizeof(Tout) == 2) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if constexpr (std::is_same<Tout, __nv_bfloat16>::value) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(w[2 * e], w[2 * e + 1]);
+        pk[e] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(w[2 * e], w[2 * e + 1]);
+        pk[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    if (ncols >= 32) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d4[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+    } else {
+      const Tout* src = reinterpret_cast<const Tout*>(pk);
+      for (int e = 0; e < ncols; ++e) dst[e] = src[e];
+    }
+  } else {
+    if (ncols >= 32) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d4[e] = make_float4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+    } else {
+      for (int e = 0; e < ncols; ++e) dst[e] = w[e];
+    }
+  }
+}
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(256, 1)
+    gemm_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
+                const __grid_constant__ CUtensorMap tm_b) {
+  using C = GemmCfg<sizeof(Tin)>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* bar_full = bars;
+  uint64_t* bar_empty = bars + C::kStages;
+  uint64_t* bar_acc_full = bar_empty + C::kStages;
+  uint64_t* bar_acc_empty = bar_acc_full + 2;
+  uint64_t* bar_teardown = bar_acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_teardown + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_pid_m = (p.M + C::kBM - 1) / C::kBM;
+  const int num_pid_n = (p.N + C::kBN - 1) / C::kBN;
+  const int num_tiles = num_pid_m * num_pid_n;
+  const int nkb = (p.K + C::kBK - 1) / C::kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_full + s, 1);
+      mbar_init(bar_empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_acc_full + b, 1);
+      mbar_init(bar_acc_empty + b, 128);
+    }
+    mbar_init(bar_teardown, 1);
+    *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const bool skip = *abort_flag != 0;
+
+  if (!skip && warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+      int pm, pn;
+      gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+      const int m0 = pm * C::kBM, n0 = pn * C::kBN;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!(ok = mbar_wait(bar_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty))) break;
+        uint8_t* st = smem + s * C::kStageBytes;
+        mbar_arrive_expect_tx(bar_full + s, C::kStageBytes);
+        tma_load_2d(st, &tm_a, bar_full + s, kb * C::kBK, m0);
+#pragma unroll
+        for (int a = 0; a < C::kBN / C::kBAtomN; ++a)
+          tma_load_2d(st + C::kABytes + a * C::kBAtomBytes, &tm_b, bar_full + s, n0 + a * C::kBAtomN, kb * C::kBK);
+      }
+    }
+    // Wait (bounded) for the last copy issued into every stage.
+    volatile int no_abort = 0;
+    for (int x = max(0, it - C::kStages); x < it; ++x)
+      mbar_wait(bar_full + (x % C::kStages), (x / C::kStages) & 1, &no_abort, kDevTimeoutTeardown);
+  } else if (!skip && warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc(GemmFmt<Tin>::kFmt, C::kBM, C::kBN, 0, 1);
+    const uint32_t base = smem_u32(smem);
+    int it = 0, tcount = 0;
+    bool ok = true, any = false;
+    for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++tcount) {
+      const int buf = tcount & 1;
+      const uint32_t use = tcount >> 1;
+      if (!(ok = mbar_wait(bar_acc_empty + buf, (use & 1) ^ 1, abort_flag, kDevTimeoutAcc))) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * C::kBN;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t ph = (it / C::kStages) & 1;
+        if (!(ok = mbar_wait(bar_full + s, ph, abort_flag, kDevTimeoutKV))) break;
+        tc_fence_after();
+        const uint32_t sa = base + s * C::kStageBytes;
+        const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < C::kBK / C::kKInstr; ++kk) {
+          const uint64_t ad = umma_desc_sw128(sa + kk * 32, 16, 1024);
+          const uint64_t bd = umma_desc_mn<sizeof(Tin)>(sb + kk * C::kKInstr * 128, C::kBAtomBytes);
+          const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (sizeof(Tin) == 4)
+            mma_ss_tf32(d, ad, bd, idesc, acc);
+          else
+            mma_ss_f16(d, ad, bd, idesc, acc);
+        }
+        mma_commit(bar_empty + s);
+        any = true;
+      }
+      if (!ok) break;
+      mma_commit(bar_acc_full + buf);
+    }
+    if (any) {
+      volatile int no_abort = 0;
+      mma_commit(bar_teardown);
+      mbar_wait(bar_teardown, 0, &no_abort, kDevTimeoutTeardown);
+    }
+  } else if (!skip && warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    int tcount = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+      const int buf = tcount & 1;
+      const uint32_t use = tcount >> 1;
+      if (!mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc)) break;
+      tc_fence_after();
+      int pm, pn;
+      gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+      const int row = pm * C::kBM + r;
+      const int n0 = pn * C::kBN;
+      Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
+#pragma unroll 1
+      for (int cc = 0; cc < C::kBN / 32; ++cc) {
+        uint32_t rr[32];
+        tmem_ld32(tmem + lane_base + buf * C::kBN + cc * 32, rr);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+        const int ncols = min(32, p.N - n0 - cc * 32);
+        if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
+      }
+      tc_fence_before();
+      mbar_arrive(bar_acc_empty + buf);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <typename Tin, typename Tout>
+static int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
+  using C = GemmCfg<sizeof(Tin)>;
+  auto kern = gemm_kernel<Tin, Tout>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (rc) return rc;
+  const int elt = sizeof(Tin);
+  const CUtensorMapDataType dt = elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : L.in_dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  rc = make_2d_map(&ta, L.a, dt, elt, L.K, L.M, L.lda, C::kBK, C::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // B is the MN-major operand: tf32 needs the 32-byte-chunk swizzle there.
+  rc = make_2d_map(&tb, L.b, dt, elt, L.N, L.K, L.ldb, C::kBAtomN, C::kBK,
+                   elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  GemmKernelParams kp;
+  kp.c = L.c;
+  kp.ldc = L.ldc;
+  kp.M = L.M;
+  kp.N = L.N;
+  kp.K = L.K;
+  kp.group_m = L.group_m > 0 ? L.group_m : 8;
+  kp.round_f16 = L.round_f16;
+  const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
+  if (tiles <= 0) return 0;
+  int sms = num_sms();
+  if (sms <= 0) return kErrLaunch;
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+}
+
+int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
+  if (L.M < 0 || L.N < 0 || L.K < 0) return kErrInvalidArg;
+  if (L.M == 0 || L.N == 0) return 0;
+  const int in = L.in_dtype, out = L.out_dtype;
+  if (in == kDtypeF16) {
+    if (out == kDtypeF16) return launch_gemm<__half, __half>(L, stream);
+    if (out == kDtypeBF16) return launch_gemm<__half, __nv_bfloat16>(L, stream);
+    if (out == kDtypeF32) return launch_gemm<__half, float>(L, stream);
+  } else if (in == kDtypeBF16) {
+    if (out == kDtypeF16) return launch_gemm<__nv_bfloat16, __half>(L, stream);
+    if (out == kDtypeBF16) return launch_gemm<__nv_bfloat16, __nv_bfloat16>(L, stream);
+    if (out == kDtypeF32) return launch_gemm<__nv_bfloat16, float>(L, stream);
+  } else if (in == kDtypeF32) {
+    if (out == kDtypeF16) return launch_gemm<float, __half>(L, stream);
+    if (out == kDtypeBF16) return launch_gemm<float, __nv_bfloat16>(L, stream);
+    if (out == kDtypeF32) return launch_gemm<float, float>(L, stream);
+  }
+  return kErrInvalidArg;
+}
+
+int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads) {
+  cudaFuncAttributes a{};
+  const void* k = in_dtype == kDtypeF32    ? reinterpret_cast<const void*>(gemm_kernel<float, __half>)
+                  : in_dtype == kDtypeBF16 ? reinterpret_cast<const void*>(gemm_kernel<__nv_bfloat16, __half>)
+                                           : reinterpret_cast<const void*>(gemm_kernel<__half, __half>);
+  if (cudaFuncGetAttributes(&a, k) != cudaSuccess) return kErrLaunch;
+  *regs = a.numRegs;
+  *smem = in_dtype == kDtypeF32 ? GemmCfg<4>::kSmemBytes : GemmCfg<2>::kSmemBytes;
+  *threads = 256;
+  return 0;
+}
+
+}  // namespace fab

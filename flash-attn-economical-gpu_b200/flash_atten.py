@@ -1,0 +1,347 @@
+"""FlashAttention forward on B200 (drop-in for the reference's flash_atten.py).
+
+`flash_attention(launch_spec)` and `flash_attention_kernel_mapping` keep the
+reference's contract (flash_atten.py:364-383): the spec's `function_name`
+selects a kernel, the kernel is launched as `kernel[grid](*kernel_args,
+**kernel_kwargs)`, and the call returns `kernel_args[3]` (o), or `(o, lse)`
+when `kernel_args[4]` is a tensor.  The three kernel names map to launcher
+objects that accept exactly the Triton kernels' argument lists
+(flash_atten.py:14-51, 136-173, 261-276) and call the sm_100a tcgen05 kernel
+through the C ABI (include/fa_b200.h).  There is no Triton and no CPU path:
+the native library must be loaded and the tensors must live on a CUDA device.
+
+`attention_forward` is the direct entry used by the SDPA drop-in and the
+benchmarks: same maths, plus grouped-query heads mapped inside the kernel.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+from dataclasses import dataclass
+
+import torch
+
+import _native
+from tuner import FlashAttentionLaunchSpec
+
+logger = logging.getLogger(__name__)
+
+
+def _require_cuda_tensor(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU implementation)")
+
+
+def _tma_ready(t: torch.Tensor, strides: tuple[int, ...]) -> bool:
+    """Unit stride on the last dim, 16-byte aligned base and outer strides."""
+    es = t.element_size()
+    if strides[-1] != 1:
+        return False
+    if t.data_ptr() % 16:
+        return False
+    return all((s * es) % 16 == 0 for s, n in zip(strides[:-1], t.shape[:-1]) if n > 1)
+
+
+def _padded_like(t: torch.Tensor) -> torch.Tensor:
+    """Uninitialised tensor shaped like `t` whose rows start on 16-byte boundaries."""
+    per16 = 16 // t.element_size()
+    d = t.shape[-1]
+    dp = -(-d // per16) * per16
+    return torch.empty((*t.shape[:-1], dp), device=t.device, dtype=t.dtype)[..., :d]
+
+
+def _as_view(t: torch.Tensor, shape: tuple[int, ...], strides: tuple[int, ...]) -> torch.Tensor:
+    """The tensor the reference kernel reads: `t`'s storage seen through explicit strides."""
+    if tuple(t.shape) == tuple(shape) and tuple(t.stride()) == tuple(strides):
+        return t
+    return torch.as_strided(t, shape, strides, t.storage_offset())
+
+
+def _conform(t: torch.Tensor) -> torch.Tensor:
+    """A TMA-readable version of `t` (a row-padded copy only when needed)."""
+    if _tma_ready(t, tuple(t.stride())):
+        return t
+    buf = _padded_like(t)
+    buf.copy_(t)
+    return buf
+
+
+@dataclass
+class _KernelMetadata:
+    shared: int
+    num_warps: int
+    tmem_columns: int
+
+
+class _CompiledKernelInfo:
+    """What `warmup` returns: the facts the reference's tuner reads (tuner.py:355-368)."""
+
+    def __init__(self, attrs: _native.FabKernelAttrs, tmem_columns: int = 0):
+        self.n_regs = int(attrs.registers_per_thread)
+        self.metadata = _KernelMetadata(int(attrs.shared_bytes), int(attrs.threads) // 32, tmem_columns)
+
+    def _init_handles(self) -> None:
+        return None
+
+
+def _launch_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    lse: torch.Tensor | None,
+    *,
+    causal: bool,
+    sm_scale: float,
+    what: str,
+    entry: str = "general",
+) -> None:
+    """Validate, conform and launch one attention forward through the C ABI.
+
+    `entry` picks the C entry point: "basic" / "optimize_shared_mem" /
+    "nomask" for the reference-named kernels, "general" (`fab_attention_fwd`,
+    grouped-query heads) otherwise.
+
+    q/o: [B, Hq, M, D]; k/v: [B, Hkv, N, D]; lse: [B, Hq, M] fp32 or None.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
+        _require_cuda_tensor(name, t)
+    if q.dtype != k.dtype or q.dtype != v.dtype or q.dtype != o.dtype:
+        raise ValueError(f"{what}: q, k, v and o must share one dtype, got {q.dtype}, {k.dtype}, {v.dtype}, {o.dtype}")
+    dt = _native.dtype_code(q.dtype)
+    B, Hq, M, D = q.shape
+    Bk, Hkv, N, Dk = k.shape
+    if tuple(v.shape) != tuple(k.shape) or Bk != B or Dk != D or tuple(o.shape) != tuple(q.shape):
+        raise ValueError(f"{what}: inconsistent shapes q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)} o={tuple(o.shape)}")
+    if Hkv == 0 or Hq % Hkv:
+        raise ValueError(f"{what}: query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
+    if lse is not None:
+        _require_cuda_tensor("lse", lse)
+        if lse.dtype != torch.float32 or tuple(lse.shape) != (B, Hq, M):
+            raise ValueError(f"{what}: lse must be float32 with shape {(B, Hq, M)}")
+    if B * Hq * M == 0:
+        return
+    sm_scale = float(sm_scale)
+    if sm_scale < 0:
+        # softmax(s * c) == softmax(|c| * (-q) k^T): fold the sign into Q.
+        q = -q
+        sm_scale = -sm_scale
+    elif sm_scale == 0:
+        # Uniform weights over the visible keys; a vanishing positive scale gives the same weights.
+        sm_scale = 1e-30
+    qc, kc, vc = _conform(q), _conform(k), _conform(v)
+    oc = o if _tma_ready(o, tuple(o.stride())) else _padded_like(o)
+    lc = lse
+    if lse is not None and lse.data_ptr() % 4:
+        lc = torch.empty_like(lse, memory_format=torch.contiguous_format)
+    with torch.cuda.device(q.device):
+        stream = ctypes.c_void_p(_native.current_stream_handle(q.device))
+        if entry == "nomask" and all(t.is_contiguous() for t in (qc, kc, vc, oc)):
+            rc = _native.lib.fab_flash_attn_fwd_block_d_nomask_contiguous(
+                qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr(), B, Hq, M, N, D, sm_scale, dt, stream
+            )
+        elif entry in ("basic", "optimize_shared_mem") and Hq == Hkv:
+            fn = (
+                _native.lib.fab_flash_attn_fwd_basic
+                if entry == "basic"
+                else _native.lib.fab_flash_attn_fwd_optimize_shared_mem
+            )
+            lse_ptr = ctypes.cast(ctypes.c_void_p(lc.data_ptr()), ctypes.POINTER(ctypes.c_float)) if lc is not None else None
+            rc = fn(
+                qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr(), lse_ptr,
+                *qc.stride(), *kc.stride(), *vc.stride(), *oc.stride(),
+                *(lc.stride() if lc is not None else (0, 0, 0)),
+                B, Hq, M, N, D, sm_scale, 1 if causal else 0, 1 if lc is not None else 0, dt, stream,
+            )
+        else:
+            p = _native.FabAttentionParams()
+            p.q, p.k, p.v, p.o = qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr()
+            p.lse = lc.data_ptr() if lc is not None else None
+            p.q_stride_b, p.q_stride_h, p.q_stride_s = qc.stride()[:3]
+            p.k_stride_b, p.k_stride_h, p.k_stride_s = kc.stride()[:3]
+            p.v_stride_b, p.v_stride_h, p.v_stride_s = vc.stride()[:3]
+            p.o_stride_b, p.o_stride_h, p.o_stride_s = oc.stride()[:3]
+            if lc is not None:
+                p.lse_stride_b, p.lse_stride_h, p.lse_stride_s = lc.stride()
+            p.batch, p.heads_q, p.heads_kv, p.seqlen_q, p.seqlen_k, p.head_dim = B, Hq, Hkv, M, N, D
+            p.dtype = dt
+            p.sm_scale = sm_scale
+            p.causal = 1 if causal else 0
+            rc = _native.lib.fab_attention_fwd(ctypes.byref(p), stream)
+    _native.check(rc, what)
+    if oc is not o:
+        o.copy_(oc)
+    if lc is not None and lc is not lse:
+        lse.copy_(lc)
+
+
+class _StridedAttentionKernel:
+    """Stands in for `_flash_attn_fwd_kernel_basic` / `_optimize_shared_mem` (Triton JITFunctions).
+
+    Positional arguments (flash_atten.py:15-44): q, k, v, o, lse (tensor or 0),
+    19 element strides, H, M, N, D, sm_scale.  Keyword arguments: causal,
+    HAS_LSE and the Triton tiling knobs (BLOCK_*, num_warps, num_stages,
+    debug), which the sm_100a kernel does not need and ignores.  The batch
+    size is grid[1] // H, as in the Triton launch.
+    """
+
+    def __init__(self, name: str):
+        self.__name__ = name
+        self.fn_name = name
+
+    def __repr__(self) -> str:
+        return f"<sm_100a attention kernel {self.__name__}>"
+
+    def __getitem__(self, grid):
+        grid = tuple(grid) if isinstance(grid, (tuple, list)) else (grid,)
+
+        def launch(*args, **kwargs):
+            return self._run(grid, args, kwargs)
+
+        return launch
+
+    def _parse(self, grid, args, kwargs):
+        if len(args) != 29:
+            raise TypeError(f"{self.__name__} expects 29 positional arguments, got {len(args)}")
+        q, k, v, o, lse = args[:5]
+        strides = [int(s) for s in args[5:24]]
+        H, M, N, D = (int(x) for x in args[24:28])
+        sm_scale = float(args[28])
+        causal = bool(kwargs.get("causal", False))
+        has_lse = bool(kwargs.get("HAS_LSE", False))
+        if H <= 0:
+            raise ValueError(f"{self.__name__}: H must be positive")
+        if len(grid) < 2 or int(grid[1]) % H:
+            raise ValueError(f"{self.__name__}: grid[1] must be batch*H, got grid={grid} with H={H}")
+        B = int(grid[1]) // H
+        return q, k, v, o, lse, strides, B, H, M, N, D, sm_scale, causal, has_lse
+
+    def _run(self, grid, args, kwargs):
+        q, k, v, o, lse, st, B, H, M, N, D, sm_scale, causal, has_lse = self._parse(grid, args, kwargs)
+        qv = _as_view(q, (B, H, M, D), tuple(st[0:4]))
+        kv = _as_view(k, (B, H, N, D), tuple(st[4:8]))
+        vv = _as_view(v, (B, H, N, D), tuple(st[8:12]))
+        ov = _as_view(o, (B, H, M, D), tuple(st[12:16]))
+        lv = None
+        if has_lse:
+            if not isinstance(lse, torch.Tensor):
+                raise ValueError(f"{self.__name__}: HAS_LSE=True needs an lse tensor")
+            lv = _as_view(lse, (B, H, M), tuple(st[16:19]))
+        entry = "basic" if self.__name__.endswith("_basic") else "optimize_shared_mem"
+        _launch_attention(qv, kv, vv, ov, lv, causal=causal, sm_scale=sm_scale, what=self.__name__, entry=entry)
+
+    def warmup(self, *args, grid, **kwargs):
+        q = args[0]
+        D = int(args[27])
+        return _CompiledKernelInfo(
+            _native.kernel_attrs(_native.FAB_KERNEL_ATTENTION, _native.dtype_code(q.dtype), D),
+            int(_native.fa_config(_native.dtype_code(q.dtype), D).tmem_columns),
+        )
+
+
+class _ContiguousAttentionKernel(_StridedAttentionKernel):
+    """Stands in for `_flash_attn_fwd_kernel_block_d_nomask_contiguous` (flash_atten.py:261-276).
+
+    Positional arguments: q, k, v, o, H, M, N, D, sm_scale over contiguous
+    [B, H, M|N, D] storage; non-causal, no LSE.  Unlike the Triton kernel,
+    M, N and D need not be multiples of any tile size.
+    """
+
+    def _run(self, grid, args, kwargs):
+        if len(args) != 9:
+            raise TypeError(f"{self.__name__} expects 9 positional arguments, got {len(args)}")
+        q, k, v, o = args[:4]
+        H, M, N, D = (int(x) for x in args[4:8])
+        sm_scale = float(args[8])
+        if H <= 0 or len(grid) < 2 or int(grid[1]) % H:
+            raise ValueError(f"{self.__name__}: grid[1] must be batch*H, got grid={grid} with H={H}")
+        B = int(grid[1]) // H
+
+        def contiguous_view(t, S):
+            return _as_view(t, (B, H, S, D), (H * S * D, S * D, D, 1))
+
+        _launch_attention(
+            contiguous_view(q, M),
+            contiguous_view(k, N),
+            contiguous_view(v, N),
+            contiguous_view(o, M),
+            None,
+            causal=False,
+            sm_scale=sm_scale,
+            what=self.__name__,
+            entry="nomask",
+        )
+
+    def warmup(self, *args, grid, **kwargs):
+        q = args[0]
+        D = int(args[7])
+        return _CompiledKernelInfo(
+            _native.kernel_attrs(_native.FAB_KERNEL_ATTENTION, _native.dtype_code(q.dtype), D),
+            int(_native.fa_config(_native.dtype_code(q.dtype), D).tmem_columns),
+        )
+
+
+_flash_attn_fwd_kernel_basic = _StridedAttentionKernel("_flash_attn_fwd_kernel_basic")
+_flash_attn_fwd_kernel_optimize_shared_mem = _StridedAttentionKernel("_flash_attn_fwd_kernel_optimize_shared_mem")
+_flash_attn_fwd_kernel_block_d_nomask_contiguous = _ContiguousAttentionKernel(
+    "_flash_attn_fwd_kernel_block_d_nomask_contiguous"
+)
+
+flash_attention_kernel_mapping = {
+    "_flash_attn_fwd_kernel_basic": _flash_attn_fwd_kernel_basic,
+    "_flash_attn_fwd_kernel_optimize_shared_mem": _flash_attn_fwd_kernel_optimize_shared_mem,
+    "_flash_attn_fwd_kernel_block_d_nomask_contiguous": _flash_attn_fwd_kernel_block_d_nomask_contiguous,
+}
+
+
+def flash_attention(
+    launch_spec: FlashAttentionLaunchSpec,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """Launch the kernel a launch spec names; return o, or (o, lse) when the spec carries an lse buffer."""
+    if launch_spec.function_name in flash_attention_kernel_mapping:
+        flash_attention_kernel_mapping[launch_spec.function_name][launch_spec.grid](
+            *launch_spec.kernel_args, **launch_spec.kernel_kwargs
+        )
+    else:
+        raise NameError(f"No such kernel named {launch_spec.function_name}.")
+    o = launch_spec.kernel_args[3]
+    lse = launch_spec.kernel_args[4] if isinstance(launch_spec.kernel_args[4], torch.Tensor) else None
+    return (o, lse) if lse is not None else o
+
+
+def attention_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = False,
+    sm_scale: float | None = None,
+    return_lse: bool = False,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """softmax(sm_scale * q k^T [causal]) v for q [B, Hq, M, D], k/v [B, Hkv, N, D].
+
+    Query head h attends to key/value head h // (Hq // Hkv) (grouped-query
+    attention without copying K/V).  Causal masking is top-left aligned, as in
+    the reference (key n visible to query m iff m >= n) and torch SDPA.
+    """
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("attention_forward expects q, k, v with shape [batch, heads, seq, head_dim]")
+    if sm_scale is None:
+        sm_scale = q.shape[-1] ** -0.5
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    lse = torch.empty(q.shape[:3], device=q.device, dtype=torch.float32) if return_lse else None
+    _launch_attention(q, k, v, o, lse, causal=causal, sm_scale=sm_scale, what="attention_forward")
+    return (o, lse) if return_lse else o
+
+
+__all__ = [
+    "flash_attention_kernel_mapping",
+    "flash_attention",
+    "attention_forward",
+    "_flash_attn_fwd_kernel_basic",
+    "_flash_attn_fwd_kernel_optimize_shared_mem",
+    "_flash_attn_fwd_kernel_block_d_nomask_contiguous",
+]

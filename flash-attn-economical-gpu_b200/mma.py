@@ -1,0 +1,181 @@
+"""Matmul on B200 (drop-in for the reference's mma.py).
+
+`_matmul_contiguous_kernel[grid](a, b, c, M, N, K, BLOCK_M=..., BLOCK_N=...,
+BLOCK_K=..., GROUP_M=..., USE_CACHE_EVICTION_HINTS=..., num_warps=...,
+num_stages=...)` keeps the Triton kernel's call form (mma.py:8-21) and
+result: C = A B over row-major contiguous storage with fp32 accumulation,
+rounded to fp16 and then stored in C's dtype (mma.py:51-52).  It runs the
+persistent sm_100a tcgen05 GEMM through the C ABI (`fab_matmul_contiguous`);
+the Triton tiling keywords (BLOCK_*, GROUP_M, cache hints, num_warps,
+num_stages) are accepted and not needed.  `_select_2d_contiguous_config` accepts and
+rejects exactly the shapes the reference accepts and rejects (mma.py:63-81)
+and reports the tile the sm_100a kernel uses.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+
+import torch
+
+import _native
+from tuner import get_architecture
+
+logger = logging.getLogger(__name__)
+
+# Tile of the sm_100a kernel: 128x256 outputs per CTA, one 128-byte swizzle
+# atom of K per stage, 4 stages, 8 warps (TMA, MMA, 4 epilogue + 2 spare).
+SM100_BLOCK_M = 128
+SM100_BLOCK_N = 256
+SM100_NUM_WARPS = 8
+SM100_NUM_STAGES = 4
+
+
+def _sm100_block_k(element_size: int = 2) -> int:
+    return 128 // element_size
+
+
+def _require_cuda_tensor(name: str, t) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU implementation)")
+
+
+def _gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    c: torch.Tensor,
+    M: int,
+    N: int,
+    K: int,
+    *,
+    lda: int,
+    ldb: int,
+    ldc: int,
+    round_f16: bool,
+    group_m: int = 8,
+    what: str = "gemm",
+) -> None:
+    """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements)."""
+    for name, t in (("a", a), ("b", b), ("c", c)):
+        _require_cuda_tensor(name, t)
+    if a.dtype != b.dtype:
+        raise ValueError(f"{what}: a and b must share one dtype, got {a.dtype} and {b.dtype}")
+    p = _native.FabGemmParams()
+    p.a, p.b, p.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    p.lda, p.ldb, p.ldc = int(lda), int(ldb), int(ldc)
+    p.M, p.N, p.K = int(M), int(N), int(K)
+    p.in_dtype = _native.dtype_code(a.dtype)
+    p.out_dtype = _native.dtype_code(c.dtype)
+    p.round_f16 = 1 if round_f16 else 0
+    p.group_m = int(group_m)
+    with torch.cuda.device(a.device):
+        rc = _native.lib.fab_gemm(ctypes.byref(p), ctypes.c_void_p(_native.current_stream_handle(a.device)))
+    _native.check(rc, what)
+
+
+class _MatmulKernel:
+    """Stands in for the Triton JITFunction `_matmul_contiguous_kernel`."""
+
+    __name__ = "_matmul_contiguous_kernel"
+
+    def __repr__(self) -> str:
+        return "<sm_100a matmul kernel _matmul_contiguous_kernel>"
+
+    def __getitem__(self, grid):
+        def launch(a, b, c, M, N, K, **kwargs):
+            return self._run(a, b, c, int(M), int(N), int(K), kwargs)
+
+        return launch
+
+    def _run(self, a, b, c, M, N, K, kwargs):
+        for name, t in (("a", a), ("b", b), ("c", c)):
+            _require_cuda_tensor(name, t)
+        if a.numel() < M * K or b.numel() < K * N or c.numel() < M * N:
+            raise ValueError("_matmul_contiguous_kernel: a, b, c are smaller than M*K, K*N, M*N")
+        ok = all(t.is_contiguous() and t.data_ptr() % 16 == 0 for t in (a, b, c))
+        es_in, es_out = a.element_size(), c.element_size()
+        ok = ok and (K * es_in) % 16 == 0 and (N * es_in) % 16 == 0 and (N * es_out) % 16 == 0
+        if not ok:
+            raise ValueError(
+                "_matmul_contiguous_kernel needs contiguous 16-byte aligned a, b, c and rows of K and N "
+                "elements that are multiples of 16 bytes"
+            )
+        with torch.cuda.device(a.device):
+            rc = _native.lib.fab_matmul_contiguous(
+                a.data_ptr(),
+                b.data_ptr(),
+                c.data_ptr(),
+                M,
+                N,
+                K,
+                _native.dtype_code(a.dtype),
+                _native.dtype_code(c.dtype),
+                1,
+                ctypes.c_void_p(_native.current_stream_handle(a.device)),
+            )
+        _native.check(rc, "_matmul_contiguous_kernel")
+
+    def warmup(self, *args, grid=None, **kwargs):
+        a = args[0]
+        attrs = _native.kernel_attrs(_native.FAB_KERNEL_MATMUL, _native.dtype_code(a.dtype))
+        return attrs
+
+
+_matmul_contiguous_kernel = _MatmulKernel()
+
+
+def _supports_contiguous_cache_eviction_hints(device=None) -> bool:
+    if not torch.cuda.is_available():
+        return False
+    major, _ = torch.cuda.get_device_capability(device)
+    return major >= 8
+
+
+def _select_2d_contiguous_config(m: int, n: int, k: int) -> tuple[int, int, int, int, int, int]:
+    """(BLOCK_M, BLOCK_N, BLOCK_K, GROUP_M, num_warps, num_stages) for an accepted shape.
+
+    Acceptance and error messages follow mma.py:63-81; the returned tile is
+    the sm_100a kernel's (it has no divisibility requirement of its own).
+    """
+    if k % 32 != 0:
+        raise ValueError("fast 2D contiguous matmul requires K % 32 == 0")
+    accepted = (
+        (m >= 2048 and n >= 2048 and m % 128 == 0 and n % 128 == 0)
+        or (m % 128 == 0 and n % 64 == 0)
+        or (m % 128 == 0 and n % 128 == 0)
+        or (m % 64 == 0 and n % 256 == 0)
+    )
+    if not accepted:
+        raise ValueError(
+            "fast 2D contiguous matmul requires a supported divisible tile: "
+            "(M % 128 == 0 and N % 64 == 0), "
+            "(M % 128 == 0 and N % 128 == 0), or "
+            "(M % 64 == 0 and N % 256 == 0), with K % 32 == 0"
+        )
+    return SM100_BLOCK_M, SM100_BLOCK_N, _sm100_block_k(2), 8, SM100_NUM_WARPS, SM100_NUM_STAGES
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, out_dtype: torch.dtype | None = None, round_f16: bool = False) -> torch.Tensor:
+    """C = A B for 2-D row-major a [M, K], b [K, N] (any leading dims with unit column stride)."""
+    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"matmul expects a [M, K] and b [K, N], got {tuple(a.shape)} and {tuple(b.shape)}")
+    M, K = a.shape
+    N = b.shape[1]
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if b.stride(1) != 1:
+        b = b.contiguous()
+    c = torch.empty((M, N), device=a.device, dtype=out_dtype or a.dtype)
+    _gemm(a, b, c, M, N, K, lda=a.stride(0), ldb=b.stride(0), ldc=c.stride(0), round_f16=round_f16, what="matmul")
+    return c
+
+
+__all__ = [
+    "_select_2d_contiguous_config",
+    "_supports_contiguous_cache_eviction_hints",
+    "_matmul_contiguous_kernel",
+    "matmul",
+    "get_architecture",
+]

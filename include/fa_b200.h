@@ -1,0 +1,203 @@
+/*
+ * fa_b200.h -- C ABI of the B200 (sm_100a) FlashAttention-forward and matmul
+ * kernels that stand in for the Triton kernels of flash-attn-economical-gpu.
+ *
+ * Every entry point takes plain device pointers, sizes and element strides,
+ * launches asynchronously on the given CUDA stream (a cudaStream_t passed as
+ * void*; NULL is the legacy default stream) and returns FAB_OK or a FAB_ERR_*
+ * code.  Nothing here allocates device memory, synchronises the stream or
+ * aborts the process.  All entry points are safe to call from several host
+ * threads.
+ *
+ * Layout rules shared by the attention entry points: tensors are indexed
+ * [batch, head, seq, head_dim] with arbitrary element strides for the first
+ * three dims, stride 1 along head_dim, 16-byte aligned base pointers and
+ * strides that are multiples of 16 bytes (the Tensor Memory Accelerator reads
+ * them directly).  Inputs outside these rules return FAB_ERR_INVALID_ARG; the
+ * Python layer copies such tensors into conforming ones first.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define FAB_OK 0
+#define FAB_ERR_INVALID_ARG 1     /* bad pointer, shape, stride or alignment */
+#define FAB_ERR_UNSUPPORTED 2     /* valid request outside the kernels' range (e.g. head_dim > 256) */
+#define FAB_ERR_LAUNCH 3          /* the CUDA launch itself failed */
+#define FAB_ERR_DEVICE_TIMEOUT 4  /* a kernel gave up on a bounded wait (see fab_get_device_error) */
+#define FAB_ERR_CUDA 5            /* another CUDA runtime error */
+
+/* Element types. */
+#define FAB_DTYPE_F16 0
+#define FAB_DTYPE_BF16 1
+#define FAB_DTYPE_F32 2 /* computed on the tensor cores as tf32, like Triton's default tl.dot */
+
+/*
+ * Replaces `_flash_attn_fwd_kernel_basic[grid](q, k, v, o, lse, strides..., H, M, N, D,
+ * sm_scale, causal=, HAS_LSE=, ...)` (flash_atten.py:14-51, launched from
+ * flash_atten.py:377 with grid (cdiv(M, BLOCK_M), B*H) built at tuner.py:264-295).
+ * o = softmax(sm_scale * q k^T [causal: key n visible to query m iff m >= n]) v,
+ * fp32 softmax, P rounded to the input dtype before P*V; lse[b,h,m] (fp32,
+ * natural log) is written when has_lse != 0.  sm_scale must be > 0.
+ */
+int fab_flash_attn_fwd_basic(const void* q, const void* k, const void* v, void* o, float* lse,
+                             int64_t stride_qb, int64_t stride_qh, int64_t stride_qm, int64_t stride_qd,
+                             int64_t stride_kb, int64_t stride_kh, int64_t stride_kn, int64_t stride_kd,
+                             int64_t stride_vb, int64_t stride_vh, int64_t stride_vn, int64_t stride_vd,
+                             int64_t stride_ob, int64_t stride_oh, int64_t stride_om, int64_t stride_od,
+                             int64_t stride_lb, int64_t stride_lh, int64_t stride_lm, int B, int H, int M, int N,
+                             int D, float sm_scale, int causal, int has_lse, int dtype, void* stream);
+
+/*
+ * Replaces `_flash_attn_fwd_kernel_optimize_shared_mem[grid](...)` (flash_atten.py:136-173).
+ * Same arguments and results as fab_flash_attn_fwd_basic; on sm_100a both
+ * variants run the same tcgen05 kernel.
+ */
+int fab_flash_attn_fwd_optimize_shared_mem(const void* q, const void* k, const void* v, void* o, float* lse,
+                                           int64_t stride_qb, int64_t stride_qh, int64_t stride_qm,
+                                           int64_t stride_qd, int64_t stride_kb, int64_t stride_kh,
+                                           int64_t stride_kn, int64_t stride_kd, int64_t stride_vb,
+                                           int64_t stride_vh, int64_t stride_vn, int64_t stride_vd,
+                                           int64_t stride_ob, int64_t stride_oh, int64_t stride_om,
+                                           int64_t stride_od, int64_t stride_lb, int64_t stride_lh,
+                                           int64_t stride_lm, int B, int H, int M, int N, int D, float sm_scale,
+                                           int causal, int has_lse, int dtype, void* stream);
+
+/*
+ * Replaces `_flash_attn_fwd_kernel_block_d_nomask_contiguous[grid](q, k, v, o, H, M, N, D,
+ * sm_scale, ...)` (flash_atten.py:261-276, launch args at tuner.py:639-650): contiguous
+ * [B, H, M|N, D] tensors, non-causal, no LSE.  B is grid[1] / H of the Triton
+ * launch.  Unlike the Triton kernel, M, N and D need not divide any tile size.
+ */
+int fab_flash_attn_fwd_block_d_nomask_contiguous(const void* q, const void* k, const void* v, void* o, int B,
+                                                 int H, int M, int N, int D, float sm_scale, int dtype,
+                                                 void* stream);
+
+/*
+ * General attention forward with grouped-query heads mapped in the kernel
+ * (query head h reads key/value head h / (Hq / Hkv)).  Replaces the
+ * `_repeat_kv_for_gqa` + `_run_block_d_nomask_vanilla` pair behind the SDPA
+ * patch (ttft.py:169-219, 299-327), without materialising repeated K/V.
+ * Strides are in elements, stride along head_dim must be 1.
+ */
+typedef struct fab_attention_params {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse; /* may be NULL */
+  int64_t q_stride_b, q_stride_h, q_stride_s;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  int64_t o_stride_b, o_stride_h, o_stride_s;
+  int64_t lse_stride_b, lse_stride_h, lse_stride_s;
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int seqlen_q;
+  int seqlen_k;
+  int head_dim;
+  int dtype;
+  float sm_scale;
+  int causal;
+} fab_attention_params;
+
+int fab_attention_fwd(const fab_attention_params* params, void* stream);
+
+/*
+ * Replaces `_matmul_contiguous_kernel[grid](a, b, c, M, N, K, BLOCK_M=..., ...)`
+ * (mma.py:8-21, launched as in test_mma.py:318-332): row-major contiguous
+ * A[M,K], B[K,N], C[M,N], fp32 accumulation.  round_f16 != 0 rounds the
+ * accumulator to fp16 before storing it in out_dtype, as the Triton kernel's
+ * `accumulator.to(tl.float16)` store does (mma.py:51-52).  Unlike the Triton
+ * kernel, M, N and K need not divide the tile sizes (K and N must be
+ * multiples of 16 bytes' worth of elements).
+ */
+int fab_matmul_contiguous(const void* a, const void* b, void* c, int M, int N, int K, int in_dtype,
+                          int out_dtype, int round_f16, void* stream);
+
+/* General row-major GEMM with leading dimensions (elements); used by the TTFT model. */
+typedef struct fab_gemm_params {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t lda, ldb, ldc;
+  int M, N, K;
+  int in_dtype;
+  int out_dtype;
+  int round_f16;
+  int group_m; /* tile-row group for L2 reuse, 0 = default (8) */
+} fab_gemm_params;
+
+int fab_gemm(const fab_gemm_params* params, void* stream);
+
+/*
+ * Static sm_100a tile table that replaces the reference tuner's compile-and-rank
+ * search (tuner.py:414-561): the configuration the attention kernel uses for a
+ * dtype and head_dim.
+ */
+typedef struct fab_fa_config {
+  int head_dim_padded; /* head_dim rounded up to whole 128-byte swizzle atoms */
+  int q_tiles_per_cta; /* 128-row query tiles per CTA (BLOCK_M = 128 * this) */
+  int block_n;         /* keys per KV tile */
+  int stages;          /* K and V ring depth */
+  int threads;
+  int smem_bytes;
+  int tmem_columns;
+} fab_fa_config;
+
+int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out);
+
+/*
+ * Compiled-kernel facts that replace Triton's `kernel.warmup(...)` metadata
+ * (tuner.py:355-368: metadata.shared, metadata.num_warps, n_regs).
+ * which: 0 = attention kernel for (dtype, head_dim), 1 = matmul kernel for dtype.
+ */
+#define FAB_KERNEL_ATTENTION 0
+#define FAB_KERNEL_MATMUL 1
+typedef struct fab_kernel_attrs {
+  int registers_per_thread;
+  int shared_bytes;
+  int threads;
+} fab_kernel_attrs;
+
+int fab_kernel_attrs_query(int which, int dtype, int head_dim, fab_kernel_attrs* out);
+
+/* Device limits that replace exceptions.get_sm_resource_limits() (exceptions.py:760-775). */
+typedef struct fab_device_limits {
+  int shared_bytes_per_sm;
+  int shared_bytes_per_block_optin;
+  int registers_per_sm;
+  int warp_size;
+  int max_threads_per_block;
+  int multiprocessor_count;
+  int cc_major;
+  int cc_minor;
+} fab_device_limits;
+
+int fab_device_limits_query(int device, fab_device_limits* out);
+
+/*
+ * Reads and clears the device error word of the current device.  *code is 0
+ * when no kernel has given up on a bounded wait, else a positive code naming
+ * the wait.  Synchronises with the device (call it between launches).
+ */
+int fab_get_device_error(int* code);
+
+/* Human-readable text for a FAB_* return code. */
+const char* fab_error_string(int rc);
+
+/* ABI version of this header (incremented on incompatible changes). */
+int fab_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */

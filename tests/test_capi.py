@@ -1,0 +1,141 @@
+"""The C-ABI library loads, exports every declared symbol, and validates arguments.
+
+Runs without a GPU: only entry points that return before touching the device
+are called.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+import _native
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fa_b200.h"
+
+
+def _declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(fab_[a-z0-9_]+)\s*\(", text))
+
+
+def test_header_declares_the_boundary():
+    names = _declared_functions()
+    for required in (
+        "fab_flash_attn_fwd_basic",
+        "fab_flash_attn_fwd_optimize_shared_mem",
+        "fab_flash_attn_fwd_block_d_nomask_contiguous",
+        "fab_attention_fwd",
+        "fab_matmul_contiguous",
+        "fab_gemm",
+    ):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r"\bT (fab_[a-z0-9_]+)$", out.stdout, flags=re.M))
+    declared = _declared_functions()
+    assert declared <= exported, f"declared but not exported: {sorted(declared - exported)}"
+    for name in declared:
+        assert hasattr(_native.lib, name)
+
+
+def test_python_binding_covers_every_declared_symbol():
+    assert _declared_functions() == set(_native.PROTOTYPES)
+
+
+def test_abi_version_and_error_strings():
+    assert _native.lib.fab_abi_version() == _native.ABI_VERSION
+    assert _native.error_string(_native.FAB_OK) == "ok"
+    for rc in range(1, 6):
+        assert _native.error_string(rc) != "unknown error"
+    assert _native.error_string(99) == "unknown error"
+
+
+def test_return_code_mapping():
+    _native.check(_native.FAB_OK, "x")
+    with pytest.raises(ValueError):
+        _native.check(_native.FAB_ERR_INVALID_ARG, "x")
+    with pytest.raises(ValueError):
+        _native.check(_native.FAB_ERR_UNSUPPORTED, "x")
+    with pytest.raises(_native.DeviceTimeoutError):
+        _native.check(_native.FAB_ERR_DEVICE_TIMEOUT, "x")
+    with pytest.raises(RuntimeError):
+        _native.check(_native.FAB_ERR_LAUNCH, "x")
+
+
+@pytest.mark.parametrize(
+    "dtype, D, expect",
+    [
+        # (head_dim_padded, q_tiles_per_cta, block_n, stages)
+        (_native.FAB_DTYPE_BF16, 64, (64, 2, 128, 3)),
+        (_native.FAB_DTYPE_BF16, 128, (128, 2, 128, 2)),
+        (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 2)),
+        (_native.FAB_DTYPE_F16, 256, (256, 1, 64, 2)),
+        (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 2)),
+        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 2)),
+    ],
+)
+def test_tile_table(dtype, D, expect):
+    cfg = _native.fa_config(dtype, D)
+    assert (cfg.head_dim_padded, cfg.q_tiles_per_cta, cfg.block_n, cfg.stages) == expect
+    assert cfg.threads == 128 * (1 + cfg.q_tiles_per_cta)
+    assert cfg.smem_bytes <= 232448
+    assert cfg.tmem_columns in (256, 512)
+    assert cfg.q_tiles_per_cta * (cfg.block_n + cfg.head_dim_padded) <= cfg.tmem_columns
+
+
+def test_tile_table_rejects_out_of_range_head_dims():
+    assert _native.fa_config(_native.FAB_DTYPE_BF16, 512) is None
+    assert _native.fa_config(_native.FAB_DTYPE_F32, 256) is None
+    with pytest.raises(ValueError):
+        _native.fa_config(7, 64)
+
+
+def test_null_and_bad_arguments_are_rejected_before_any_launch():
+    lib = _native.lib
+    assert lib.fab_attention_fwd(None, None) == _native.FAB_ERR_INVALID_ARG
+    assert lib.fab_gemm(None, None) == _native.FAB_ERR_INVALID_ARG
+    p = _native.FabGemmParams()
+    p.M, p.N, p.K = -1, 8, 8
+    assert lib.fab_gemm(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
+    p.M, p.N, p.K, p.in_dtype, p.out_dtype = 8, 8, 8, 9, 0
+    assert lib.fab_gemm(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
+    # Empty problems are a no-op.
+    p.M, p.N, p.in_dtype = 0, 8, 0
+    assert lib.fab_gemm(ctypes.byref(p), None) == _native.FAB_OK
+    a = _native.FabAttentionParams()
+    a.batch, a.heads_q, a.heads_kv, a.seqlen_q, a.seqlen_k, a.head_dim, a.dtype = 1, 4, 3, 16, 16, 64, 1
+    a.sm_scale = 0.125
+    a.q = a.k = a.v = a.o = 4096
+    assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_ERR_INVALID_ARG  # 4 % 3 != 0
+    a.heads_kv = 2
+    a.sm_scale = -1.0
+    assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_ERR_UNSUPPORTED
+    a.sm_scale = 0.125
+    a.head_dim = 512
+    assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_ERR_UNSUPPORTED
+    a.head_dim = 64
+    a.seqlen_q = 0
+    assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_OK
+    a.seqlen_q = 16
+    a.o = 4100  # not 16-byte aligned
+    assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_ERR_INVALID_ARG
+
+
+def test_strided_entry_requires_unit_head_dim_stride():
+    lib = _native.lib
+    args = [4096, 4096, 4096, 4096, None]
+    strides = [1024, 256, 64, 2] + [1024, 256, 64, 1] * 2 + [1024, 256, 64, 1] + [0, 0, 0]
+    rc = lib.fab_flash_attn_fwd_basic(*args, *strides, 1, 4, 4, 4, 64, 0.125, 0, 0, 1, None)
+    assert rc == _native.FAB_ERR_INVALID_ARG
+    # HAS_LSE without an lse pointer
+    strides[3] = 1
+    rc = lib.fab_flash_attn_fwd_basic(*args, *strides, 1, 4, 4, 4, 64, 0.125, 0, 1, 1, None)
+    assert rc == _native.FAB_ERR_INVALID_ARG

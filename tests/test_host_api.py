@@ -1,0 +1,211 @@
+"""Host-side behaviour of the drop-in modules (no GPU needed).
+
+Mirrors what the reference's Python layer guarantees: argument validation
+and error types of tuner.py, the dispatch contract of flash_atten.py and the
+shape acceptance of mma.py.
+"""
+from __future__ import annotations
+
+import pickle
+
+import pytest
+import torch
+
+import exceptions
+import flash_atten
+import mma
+import tuner
+from tuner import (
+    FlashAttenTuneArguments,
+    FlashAttentionBlockDNomaskTuner,
+    FlashAttentionLaunchSpec,
+    FlashAttentionOptimizeSharedMemTuner,
+    FlashAttentionTuner,
+)
+
+
+# ------------------------------------------------------------- tune arguments
+@pytest.mark.parametrize(
+    "kwargs, message",
+    [
+        (dict(BLOCK_N=0), "BLOCK_N must be positive when provided"),
+        (dict(BLOCK_M=0), "BLOCK_M must be positive when provided"),
+        (dict(BLOCK_M=48), "BLOCK_M must be a power of 2 when provided"),
+        (dict(BLOCK_N_PAD=24), "BLOCK_N_PAD must be a power of 2 when provided"),
+        (dict(BLOCK_DMODEL=-2), "BLOCK_DMODEL must be positive when provided"),
+        (dict(BLOCK_DMODEL=96), "BLOCK_DMODEL must be a power of 2 when provided"),
+        (dict(BLOCK_DMODEL_OUTER=12), "BLOCK_DMODEL_OUTER must be a power of 2 when provided"),
+        (dict(NUM_WARPS=0), "NUM_WARPS must be positive when provided"),
+        (dict(NUM_STAGES=-1), "NUM_STAGES must be positive when provided"),
+    ],
+)
+def test_tune_argument_validation(kwargs, message):
+    with pytest.raises(ValueError, match=message):
+        FlashAttenTuneArguments(**kwargs)
+
+
+def test_tune_arguments_accept_reference_presets():
+    # the presets the reference's tests and ttft.py use (test_flash_atten.py:641-724, ttft.py:145-166)
+    FlashAttenTuneArguments(BLOCK_N=64, BLOCK_M=128, BLOCK_N_PAD=64, BLOCK_DMODEL=128, BLOCK_DMODEL_OUTER=64,
+                            NUM_WARPS=8, NUM_STAGES=3)
+    FlashAttenTuneArguments(BLOCK_N=48, NUM_WARPS=3, NUM_STAGES=5)  # BLOCK_N / warps / stages need not be powers of 2
+
+
+# ------------------------------------------------------------------- tuners
+def test_tuner_shape_validation(fake_limits):
+    q, k = (1, 2, 128, 64), (1, 2, 128, 64)
+    with pytest.raises(ValueError, match="must all be 4D"):
+        FlashAttentionTuner((2, 128, 64), k, k, 2, causal=False, return_lse=False)
+    with pytest.raises(ValueError, match="Batch and head dimensions must match"):
+        FlashAttentionTuner(q, (1, 1, 128, 64), (1, 1, 128, 64), 2, causal=False, return_lse=False)
+    with pytest.raises(ValueError, match="Last dimension must match"):
+        FlashAttentionTuner(q, (1, 2, 128, 32), (1, 2, 128, 32), 2, causal=False, return_lse=False)
+    with pytest.raises(ValueError, match="sequence lengths must match"):
+        FlashAttentionTuner(q, k, (1, 2, 64, 64), 2, causal=False, return_lse=False)
+    with pytest.raises(ValueError, match="BLOCK_DMODEL must be >= D"):
+        FlashAttentionTuner(q, k, k, 2, causal=False, return_lse=False, tune_args=FlashAttenTuneArguments(BLOCK_DMODEL=32))
+    with pytest.raises(ValueError, match="BLOCK_N cannot exceed BLOCK_N_PAD"):
+        FlashAttentionTuner(q, k, k, 2, causal=False, return_lse=False,
+                            tune_args=FlashAttenTuneArguments(BLOCK_N=128, BLOCK_N_PAD=64))
+    with pytest.raises(ValueError, match="NUM_WARPS must be <= 32"):
+        FlashAttentionTuner(q, k, k, 2, causal=False, return_lse=False, tune_args=FlashAttenTuneArguments(NUM_WARPS=64))
+    # the sliced variant allows BLOCK_DMODEL < D (tuner.py:604-605)
+    FlashAttentionBlockDNomaskTuner(q, k, k, 2, causal=False, return_lse=False,
+                                    tune_args=FlashAttenTuneArguments(BLOCK_DMODEL=32))
+
+
+def test_tuner_candidates_come_from_the_sm100_table(fake_limits):
+    t = FlashAttentionTuner((4, 32, 8192, 128), (4, 32, 8192, 128), (4, 32, 8192, 128), 2, causal=True, return_lse=False)
+    (cfg,) = t._candidate_configs()
+    assert cfg["BLOCK_M"] == 256 and cfg["BLOCK_N"] == 128 and cfg["BLOCK_DMODEL"] == 128
+    assert cfg["num_warps"] == 12 and cfg["num_stages"] == 2
+    t256 = FlashAttentionOptimizeSharedMemTuner((2, 16, 64, 256), (2, 16, 64, 256), (2, 16, 64, 256), 2,
+                                                causal=True, return_lse=False)
+    (cfg,) = t256._candidate_configs()
+    assert cfg["BLOCK_M"] == 128 and cfg["BLOCK_N"] == 64 and cfg["BLOCK_DMODEL"] == 256
+    t512 = FlashAttentionTuner((1, 1, 64, 512), (1, 1, 64, 512), (1, 1, 64, 512), 2, causal=False, return_lse=False)
+    assert t512._candidate_configs() == []
+    # the reference's shared-memory estimate formula (tuner.py:237-245)
+    assert t.estimate_flash_fwd_shared_bytes(block_m=128, block_n_pad=64, block_dmodel=128, element_size=2) == 2 * 128 * 256
+
+
+def test_runtime_shape_mismatch(fake_limits):
+    t = FlashAttentionTuner((1, 1, 16, 64), (1, 1, 16, 64), (1, 1, 16, 64), 2, causal=False, return_lse=False)
+    x = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="do not match the tuner shapes"):
+        t.build_launch_spec(x, x, x, sm_scale=0.1, o=x, lse=None)
+    with pytest.raises(ValueError, match="expects \\(q, k, v\\)"):
+        t.build_launch_spec(x, x, sm_scale=0.1, o=x, lse=None)
+
+
+def test_update_data_swaps_inputs_only():
+    spec = FlashAttentionLaunchSpec(grid=(1, 1), kernel_args=("q", "k", "v", "o", "lse", 1, 2), kernel_kwargs={},
+                                    launch_context={}, function_name="x", tune_args=FlashAttenTuneArguments(),
+                                    input_shapes={})
+    spec.update_data(("q2", "k2", "v2"))
+    assert spec.kernel_args == ("q2", "k2", "v2", "o", "lse", 1, 2)
+
+
+def test_power_of_two_helpers():
+    assert [tuner._next_power_of_two(x) for x in (1, 2, 3, 5, 64, 65)] == [1, 2, 4, 8, 64, 128]
+    with pytest.raises(ValueError):
+        tuner._next_power_of_two(0)
+
+
+# -------------------------------------------------------------- dispatch
+def test_unknown_kernel_name_raises_name_error():
+    spec = FlashAttentionLaunchSpec(grid=(1, 1), kernel_args=(None,) * 5, kernel_kwargs={}, launch_context={},
+                                    function_name="_no_such_kernel", tune_args=FlashAttenTuneArguments(),
+                                    input_shapes={})
+    with pytest.raises(NameError, match="No such kernel named _no_such_kernel"):
+        flash_atten.flash_attention(spec)
+
+
+def test_kernel_mapping_names_match_reference():
+    assert set(flash_atten.flash_attention_kernel_mapping) == {
+        "_flash_attn_fwd_kernel_basic",
+        "_flash_attn_fwd_kernel_optimize_shared_mem",
+        "_flash_attn_fwd_kernel_block_d_nomask_contiguous",
+    }
+    assert flash_atten._flash_attn_fwd_kernel_basic is flash_atten.flash_attention_kernel_mapping["_flash_attn_fwd_kernel_basic"]
+
+
+def test_launchers_refuse_cpu_tensors():
+    x = torch.zeros(1, 1, 16, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        flash_atten.attention_forward(x, x, x)
+    args = (x, x, x, x, 0, *x.stride(), *x.stride(), *x.stride(), *x.stride(), 0, 0, 0, 1, 16, 16, 64, 0.125)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        flash_atten._flash_attn_fwd_kernel_basic[(1, 1)](*args, causal=False, HAS_LSE=False)
+    with pytest.raises(TypeError, match="29 positional arguments"):
+        flash_atten._flash_attn_fwd_kernel_basic[(1, 1)](*args[:-1])
+    with pytest.raises(TypeError, match="9 positional arguments"):
+        flash_atten._flash_attn_fwd_kernel_block_d_nomask_contiguous[(1, 1)](x, x, x, x, 1, 16, 16, 64)
+    a = torch.zeros(128, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        mma._matmul_contiguous_kernel[(1,)](a, a.T.contiguous(), a, 128, 128, 64)
+
+
+def test_launcher_grid_must_cover_batch_times_heads():
+    x = torch.zeros(1, 3, 16, 64, dtype=torch.float16)
+    args = (x, x, x, x, 0, *x.stride(), *x.stride(), *x.stride(), *x.stride(), 0, 0, 0, 2, 16, 16, 64, 0.125)
+    with pytest.raises(ValueError, match="grid\\[1\\] must be batch\\*H"):
+        flash_atten._flash_attn_fwd_kernel_basic[(1, 3)](*args)
+
+
+# ------------------------------------------------------------------ matmul
+def _reference_acceptance(m, n, k):
+    """mma.py:63-81 restated: which shapes the reference accepts."""
+    if k % 32:
+        return False
+    return (m >= 2048 and n >= 2048 and m % 128 == 0 and n % 128 == 0) or (m % 128 == 0 and n % 64 == 0) or (
+        m % 128 == 0 and n % 128 == 0) or (m % 64 == 0 and n % 256 == 0)
+
+
+@pytest.mark.parametrize("m", [64, 128, 192, 1000, 1024, 4096])
+@pytest.mark.parametrize("n", [64, 96, 256, 512, 1000, 16384])
+@pytest.mark.parametrize("k", [32, 48, 256])
+def test_select_config_accepts_what_the_reference_accepts(m, n, k):
+    if _reference_acceptance(m, n, k):
+        cfg = mma._select_2d_contiguous_config(m, n, k)
+        assert len(cfg) == 6 and cfg[:3] == (128, 256, 64)
+    else:
+        with pytest.raises(ValueError, match="fast 2D contiguous matmul requires"):
+            mma._select_2d_contiguous_config(m, n, k)
+
+
+def test_cache_hints_probe_without_cuda():
+    if not torch.cuda.is_available():
+        assert mma._supports_contiguous_cache_eviction_hints() is False
+
+
+# -------------------------------------------------------------- exceptions
+def test_out_of_resources_message_and_pickle():
+    exc = exceptions.OutOfResourcesWithDetail(
+        300000, 232448, "shared memory", kernel_name="k", launch_context={"a": 1}, extra_detail="nothing fit."
+    )
+    text = str(exc)
+    assert text.startswith("out of resource: shared memory, Required: 300000, Hardware limit: 232448.")
+    assert "more shared memory per SM" in text and "Kernel: k." in text and "Launch context: a=1." in text
+    assert text.endswith("nothing fit.")
+    assert isinstance(exc, exceptions.OutOfResources)
+    base = pickle.loads(pickle.dumps(exceptions.OutOfResources(1, 2, "registers")))
+    assert (base.required, base.limit, base.name) == (1, 2, "registers")
+    wrapped = exceptions.OutOfResourcesWithDetail.from_out_of_resources(base, kernel_name="x")
+    assert wrapped.original_exception is base and "register file" in str(wrapped)
+
+
+def test_resource_usage_summary_format():
+    ctx = {
+        "compiled_shared_memory_bytes_per_block": 197728,
+        "available_shared_memory_bytes_per_sm": 232448,
+        "attempted_register_file_size_bytes_per_block": 258048,
+        "available_register_file_size_bytes_per_sm": 262144,
+        "attempted_registers_per_block": 64512,
+        "available_registers_per_sm": 65536,
+    }
+    s = exceptions._resource_usage_summary("k", ctx, tune_args=FlashAttenTuneArguments(BLOCK_M=256),
+                                           input_shapes={"q": (1, 2, 3, 4), "lse": None})
+    assert s.startswith("k tuner resources: \nshared=197728/232448 bytes per block/SM, ")
+    assert "registers=64512/65536 per block/SM" in s
+    assert "tune_args=BLOCK_M=256" in s and "input_shapes=q=(1, 2, 3, 4)" in s
