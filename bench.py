@@ -1,0 +1,578 @@
+"""Benchmark of the hot path: attention forward (and matmul) on B200.
+
+Contract: `python bench.py --gpus N --steps K --warmup W [--impl ours|reference]`
+prints ONE JSON line on rank 0.  For N > 1 it runs under torchrun, one rank
+per GPU; each rank owns an independent shard of (batch, head) work units
+(weak scaling, no data-path collective), timing is the max over ranks.
+
+Default workload (the north-star case): attention forward,
+B=4 per GPU, H=32, S=8192, D=128, bf16, non-causal, seeded N(0,1) inputs.
+  value  : whole-job TFLOP/s with inputs resident in HBM (CUDA events around
+           K steps; the 805 MB of inputs per step exceed the 126 MB L2, so no
+           flush is needed between steps).
+  e2e    : the same metric through the public API (`flash_atten.attention_forward`)
+           with host buffers: every step copies q, k, v from pinned host memory
+           and reads o back, inside the timed region.
+  roofline: tensor-bound; achieved = algorithmic FLOPs per launch / mean launch
+           time (CUDA events on the launch stream), peak = measured dense bf16
+           from MEASURED_PEAKS.json.
+  cpu_baseline: the reference's CPU path (torch SDPA on fp32 CPU copies,
+           test_flash_atten.py:459-461, 498-499) on a bounded sample of the
+           same workload, timed on this host's cores.
+
+`--impl reference` times that same CPU path as the benchmark arm (the
+reference has no GPU path that runs without Triton; its published numbers
+are for its Triton kernels on T4/A10).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "flash-attn-economical-gpu_b200"
+for _p in (str(PKG), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "FA fwd TFLOPS (% of B200 bf16 peak) vs torch SDPA; Qwen2.5-7B-arch TTFT ms"
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    # name: (B, Hq, Hkv, S, D, causal)
+    "fa_s8192_noncausal": (4, 32, 32, 8192, 128, False),
+    "fa_s8192_causal": (4, 32, 32, 8192, 128, True),
+    "fa_s4096_noncausal": (4, 32, 32, 4096, 128, False),
+    "fa_s2048_noncausal": (4, 32, 32, 2048, 128, False),
+    "fa_s1024_noncausal": (4, 32, 32, 1024, 128, False),
+    "fa_d256_s8192_causal": (2, 16, 16, 8192, 256, True),
+    "fa_gqa_s8192_causal": (2, 16, 4, 8192, 128, True),
+}
+GEMM_WORKLOADS = {"gemm_8192": 8192, "gemm_16384": 16384, "gemm_4096": 4096}
+
+
+def attention_flops(B, H, S, D, causal):
+    score = S * (S + 1) / 2 if causal else S * S
+    return 4.0 * B * H * D * score
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+        except Exception:
+            pass
+    return FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def committed_traffic(workload: str):
+    """DRAM bytes per launch from the committed ncu summary for this workload, if one exists."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.is_file():
+        return None
+    try:
+        return json.loads(path.read_text()).get(workload)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle",
+        0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x10: "sync_boost",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[int] = []
+        self.masks: set[int] = set()
+        self.errors: set[str] = set()
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(visible.split(",")[device_index]) if visible else device_index
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._handle = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(int(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)))
+                mask = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle))
+                self.masks.add(mask)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception as exc:
+                self.errors.add(f"{type(exc).__name__}: {exc}"[:120])
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._handle is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        out = {
+            "sm_mhz": statistics.median(self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+            "reason_masks": sorted(hex(m) for m in self.masks),
+        }
+        if self.errors:
+            out["nvml_errors"] = sorted(self.errors)
+        return out
+
+
+# ---------------------------------------------------------------- helpers
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def shard_units(total_units: int, world: int, rank: int) -> range:
+    """Contiguous block of work units owned by `rank` (balanced to within one unit)."""
+    base, extra = divmod(total_units, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def cpu_attention_sample(S, D, causal, target_s=10.0, max_heads=64):
+    """The reference's CPU path (fp32 torch SDPA on CPU) on a bounded sample of the workload."""
+    import torch.nn.functional as F
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+
+    def run(h):
+        q, k, v = (torch.randn(1, h, S, D, generator=g) for _ in range(3))
+        t0 = time.perf_counter()
+        F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        return time.perf_counter() - t0
+
+    run(1)  # warm-up
+    t1 = run(1)
+    heads = max(1, min(max_heads, int(target_s / max(t1, 1e-6))))
+    t = run(heads) if heads > 1 else t1
+    flops = attention_flops(1, heads, S, D, causal)
+    return {
+        "value": flops / t / 1e12,
+        "unit": "TFLOP/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{heads} of the workload's (batch, head) units at S={S} D={D} causal={causal}, fp32 torch SDPA "
+                  f"on CPU copies (the reference's oracle path), one timed pass of {t:.2f} s",
+        "seconds": t,
+    }
+
+
+def peaks_entry(achieved_tflops, workload):
+    burst, sustained, source = measured_peaks()
+    traffic = committed_traffic(workload)
+    return {
+        "bound": "tensor",
+        "achieved": round(achieved_tflops, 1),
+        "peak": burst,
+        "unit": "TFLOP/s",
+        "frac": round(achieved_tflops / burst, 4),
+        "peak_source": f"{source} dense bf16 (burst; a kernel timed alone); sustained {sustained}",
+        "traffic": traffic,
+    }
+
+
+# ------------------------------------------------------------ attention arm
+def run_attention(args, world, rank, local):
+    import _native
+    from flash_atten import attention_forward
+
+    B, Hq, Hkv, S, D, causal = WORKLOADS[args.workload]
+    dev = torch.device("cuda", local)
+    dtype = torch.bfloat16
+    # Each rank owns batch rows [rank*B, (rank+1)*B) of a global batch of B*world sequences.
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    q = torch.randn(B, Hq, S, D, generator=g, device=dev, dtype=dtype)
+    k = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
+    v = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
+    o = torch.empty_like(q)
+    flops = attention_flops(B, Hq, S, D, causal)
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        attention_forward(q, k, v, causal=causal, out=o)
+    torch.cuda.synchronize(dev)
+    if _native.device_error():
+        raise RuntimeError("device error during warm-up")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            attention_forward(q, k, v, causal=causal, out=o)
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    elapsed_ms = max_over_ranks(t_begin.elapsed_time(t_end), world)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if _native.device_error():
+        raise RuntimeError("device error during the timed region")
+    total_flops = sum_over_ranks(flops * args.steps, world)
+    value = total_flops / (elapsed_ms / 1e3) / 1e12
+    achieved = flops / (launch_ms / 1e3) / 1e12
+
+    # ---- e2e through the public API with host buffers
+    qh = q.cpu().pin_memory()
+    kh = k.cpu().pin_memory()
+    vh = v.cpu().pin_memory()
+    oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        qd = qh.to(dev, non_blocking=True)
+        kd = kh.to(dev, non_blocking=True)
+        vd = vh.to(dev, non_blocking=True)
+        out = attention_forward(qd, kd, vd, causal=causal)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = sum_over_ranks(flops * e2e_steps, world) / (e2e_ms / 1e3) / 1e12
+    h2d = (q.numel() + k.numel() + v.numel()) * q.element_size()
+    d2h = o.numel() * o.element_size()
+
+    # ---- same-box comparators (rank 0 only, not part of the metric)
+    comparators = {}
+    if rank == 0 and not args.no_compare:
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        for name, be in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+            try:
+                rep = Hq // Hkv
+                kk = k if rep == 1 else k.repeat_interleave(rep, dim=1)
+                vv = v if rep == 1 else v.repeat_interleave(rep, dim=1)
+                with sdpa_kernel([be]):
+                    for _ in range(3):
+                        F.scaled_dot_product_attention(q, kk, vv, is_causal=causal)
+                    torch.cuda.synchronize(dev)
+                    c0 = torch.cuda.Event(enable_timing=True)
+                    c1 = torch.cuda.Event(enable_timing=True)
+                    c0.record(stream)
+                    for _ in range(10):
+                        F.scaled_dot_product_attention(q, kk, vv, is_causal=causal)
+                    c1.record(stream)
+                    torch.cuda.synchronize(dev)
+                comparators[name + "_tflops"] = round(flops * 10 / (c0.elapsed_time(c1) / 1e3) / 1e12, 1)
+            except Exception as exc:  # a backend may not support the shape
+                comparators[name + "_tflops"] = f"unavailable: {type(exc).__name__}"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_attention_sample(S, D, causal, target_s=args.cpu_seconds)
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/k/v per rank (no dataset in the reference for this path)",
+        "config": {
+            "workload": f"attention forward B{B} Hq{Hq} Hkv{Hkv} S{S} D{D} bf16 {'causal' if causal else 'non-causal'}"
+                        " per GPU (BASELINE config 2/3)",
+            "global_batch": B * world,
+            "seq_len": S,
+            "heads_q": Hq,
+            "heads_kv": Hkv,
+            "head_dim": D,
+            "causal": causal,
+            "parallelism": f"dp{world} (each rank owns {B} sequences x {Hq} heads; no collective)",
+            "l2_policy": f"inputs {3 * q.numel() * 2 / 1e6:.0f} MB per step > 126 MB L2; no flush",
+        },
+        "e2e": {
+            "value": round(e2e_value, 1),
+            "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "flash_atten.attention_forward on pinned host buffers (H2D q,k,v + D2H o inside the timed region)",
+        },
+        "roofline": peaks_entry(achieved, args.workload),
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "comparators": comparators,
+    }
+    if cpu is not None:
+        cpu = dict(cpu)
+        cpu.pop("seconds", None)
+        result["cpu_baseline"] = cpu
+    return result
+
+
+# ------------------------------------------------------------------ gemm arm
+def run_gemm(args, world, rank, local):
+    import _native
+    from mma import matmul
+
+    n = GEMM_WORKLOADS[args.workload]
+    dev = torch.device("cuda", local)
+    dtype = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    # Rank r owns output column block r of a (n) x (n * world) product; A is replicated.
+    a = (torch.randn(n, n, generator=g, device=dev) / n ** 0.5).to(dtype)
+    b = (torch.randn(n, n, generator=g, device=dev) / n ** 0.5).to(dtype)
+    flops = 2.0 * n ** 3
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if 3 * n * n * 2 < L2_BYTES * 2 else None
+    for _ in range(args.warmup):
+        matmul(a, b)
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    total_ms = 0.0
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            starts[i].record(stream)
+            matmul(a, b)
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    barrier(world)
+    total_ms = max_over_ranks(total_ms, world)
+    if _native.device_error():
+        raise RuntimeError("device error during the timed region")
+    value = sum_over_ranks(flops * args.steps, world) / (total_ms / 1e3) / 1e12
+    achieved = flops / (total_ms / args.steps / 1e3) / 1e12
+    comparators = {}
+    if rank == 0 and not args.no_compare:
+        for _ in range(3):
+            torch.matmul(a, b)
+        torch.cuda.synchronize(dev)
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(10):
+            torch.matmul(a, b)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        comparators["torch_matmul_cublas_tflops"] = round(flops * 10 / (c0.elapsed_time(c1) / 1e3) / 1e12, 1)
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1)/sqrt(K)",
+        "config": {"workload": f"matmul {n}x{n}x{n} bf16 per GPU (BASELINE config 4)",
+                   "parallelism": f"dp{world} (output-column shards, A replicated; no collective)",
+                   "l2_policy": "L2 flushed between steps" if flush is not None else "operands > L2"},
+        "roofline": peaks_entry(achieved, args.workload),
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "comparators": comparators,
+    }
+
+
+# ------------------------------------------------------------- reference arm
+def run_reference(args, world, rank):
+    """The reference's CPU path (fp32 torch SDPA on CPU copies) as the benchmark arm; rank 0 only."""
+    if rank != 0:
+        return None
+    B, Hq, Hkv, S, D, causal = WORKLOADS.get(args.workload, WORKLOADS["fa_s8192_noncausal"])
+    import torch.nn.functional as F
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    probe = cpu_attention_sample(S, D, causal, target_s=1.0, max_heads=1)
+    per_head_s = probe["seconds"]
+    # Each step: a bounded sample of the workload sized so the whole run stays within a few minutes.
+    budget_s = 150.0 / max(1, args.steps + args.warmup)
+    heads = max(1, min(Hq, int(budget_s / max(per_head_s, 1e-6))))
+    q, k, v = (torch.randn(1, heads, S, D, generator=g) for _ in range(3))
+    for _ in range(args.warmup):
+        F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        times.append(time.perf_counter() - t0)
+    flops = attention_flops(1, heads, S, D, causal)
+    value = flops * len(times) / sum(times) / 1e12
+    sample = (f"{heads} (batch, head) unit(s) of the workload per step at S={S} D={D} causal={causal}, fp32 torch "
+              "SDPA on CPU (the reference's oracle path, test_flash_atten.py:459-461, 498-499)")
+    return {
+        "metric": METRIC,
+        "impl": "reference",
+        "value": round(value, 4),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * sum(times) / len(times), 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded N(0,1)",
+        "config": {"workload": f"attention forward B{B} Hq{Hq} S{S} D{D} {'causal' if causal else 'non-causal'}"
+                               " (bounded CPU sample per step)",
+                   "parallelism": "rank 0 host cores"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="fa_s8192_noncausal", choices=sorted(WORKLOADS) + sorted(GEMM_WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-compare", action="store_true", help="skip the torch comparators")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        # CPU-only arm: no process group; ranks other than 0 exit without work.
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        result = run_reference(args, world, int(os.environ.get("RANK", "0")))
+        if result is not None:
+            print(json.dumps(result), flush=True)
+        return
+    world, rank, local = setup_dist(args)
+    try:
+        if args.workload in GEMM_WORKLOADS:
+            result = run_gemm(args, world, rank, local)
+        else:
+            result = run_attention(args, world, rank, local)
+        if rank == 0 and result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -63,7 +63,7 @@ class FabGemmParams(ctypes.Structure):
 class FabFaConfig(ctypes.Structure):
     _fields_ = [
         ("head_dim_padded", _i32), ("q_tiles_per_cta", _i32), ("block_n", _i32), ("stages", _i32),
-        ("threads", _i32), ("smem_bytes", _i32), ("tmem_columns", _i32),
+        ("threads", _i32), ("smem_bytes", _i32), ("tmem_columns", _i32), ("s_buffers", _i32),
     ]
 
 
@@ -96,7 +96,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 def _load() -> ctypes.CDLL:

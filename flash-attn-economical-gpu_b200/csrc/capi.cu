@@ -162,7 +162,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 1; }
+int fab_abi_version(void) { return 2; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -360,6 +360,7 @@ int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out) {
   out->threads = c.threads;
   out->smem_bytes = c.smem_bytes;
   out->tmem_columns = c.tmem_cols;
+  out->s_buffers = c.s_bufs;
   return kOk;
 }
 

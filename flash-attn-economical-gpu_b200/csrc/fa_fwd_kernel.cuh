@@ -14,11 +14,18 @@
 // Per KV tile j and Q tile i:
 //   S_i   = Q_i K_j^T            tcgen05.mma SS, fp32 in TMEM
 //   P_i   = exp2(S_i*c - m_i)    softmax group: tcgen05.ld S, tcgen05.st P
-//                                (P overwrites the first columns of S_i)
+//                                (P overwrites the first columns of its S buffer)
 //   O_i  += P_i V_j              tcgen05.mma TS (A = P from TMEM)
-// With two Q tiles per CTA the tensor core computes one tile's MMAs while the
-// other tile's softmax runs.  The running max is only moved when it grows by
-// more than 2^8, so O is rescaled rarely; the final O / l is unaffected.
+// Two ways to keep the tensor core busy while a softmax runs:
+//   * two Q tiles per CTA (head dims up to 128): the tensor core computes one
+//     tile's products while the other tile's softmax runs;
+//   * two S buffers for one Q tile (head dim 256, fp32 128): S(j+1) is
+//     computed while softmax(j) runs.
+// The S product that reuses an S buffer is issued right after the P*V product
+// that reads the P held there; tcgen05.mma instructions from one thread
+// execute in issue order, so the write cannot overtake the read.  The running
+// max is only moved when it grows by more than 2^8, so O is rescaled rarely;
+// the final O / l is unaffected.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -27,9 +34,15 @@
 #include "fa_internal.h"
 #include "ptx.cuh"
 
+// Of every 16 pairs of scores, this many are exponentiated by exp2_poly2 on
+// the FMA pipe and the rest by ex2.approx on the MUFU unit.
+#ifndef FAB_FA_POLY_PAIRS_PER_16
+#define FAB_FA_POLY_PAIRS_PER_16 0
+#endif
+
 namespace fab {
 
-template <int kElt, int kDP, int kNQ, int kBN, int kStages>
+template <int kElt, int kDP, int kNQ, int kBN, int kStages, int kSB>
 struct FaCfg {
   static constexpr int kBM = 128;                    // rows per Q tile (TMEM lanes)
   static constexpr int kAtom = 128 / kElt;           // elements per 128-byte swizzle atom
@@ -40,18 +53,19 @@ struct FaCfg {
   static constexpr int kKVTileBytes = kKVAtomBytes * kNumAtoms;
   static constexpr int kKInstr = 32 / kElt;          // K extent of one MMA instruction
   static constexpr int kThreads = 128 + kNQ * 128;
-  static constexpr int kPCols = kBN * kElt / 4;      // 32-bit TMEM columns of one P tile
-  static constexpr int kTmemUsed = kNQ * (kBN + kDP);
+  static constexpr int kSlots = kNQ * kSB;           // S/P buffers in TMEM
+  static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                     : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kNumBars = 1 + 4 * kStages + 3 * kNQ + 1;
+  static constexpr int kNumBars = 1 + 4 * kStages + 2 * kSlots + kNQ + 1;
   static constexpr int kDataBytes = kNQ * kQTileBytes + 2 * kStages * kKVTileBytes;
   static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
+  static_assert(kSB == 1 || kNQ == 1, "two S buffers only with one Q tile");
   static_assert(kTmemUsed <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  __host__ __device__ static constexpr int tmem_s(int i) { return i * kBN; }
-  __host__ __device__ static constexpr int tmem_o(int i) { return kNQ * kBN + i * kDP; }
+  __host__ __device__ static constexpr int tmem_s(int slot) { return slot * kBN; }
+  __host__ __device__ static constexpr int tmem_o(int i) { return kSlots * kBN + i * kDP; }
 };
 
 template <typename T>
@@ -82,6 +96,7 @@ struct ElemOps<float> {
 };
 
 // Store 32 fp32 values (already normalised) as one 32-column chunk of an O row.
+// Every array index is static so the values stay in registers.
 template <typename T>
 __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int ncols) {
   if constexpr (sizeof(T) == 2) {
@@ -93,8 +108,14 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 #pragma unroll
       for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
     } else {
-      const T* src = reinterpret_cast<const T*>(w);
-      for (int e = 0; e < ncols; ++e) dst[e] = src[e];
+      uint32_t* d2 = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        if (2 * e + 1 < ncols)
+          d2[e] = w[e];
+        else if (2 * e < ncols)
+          reinterpret_cast<uint16_t*>(dst)[2 * e] = static_cast<uint16_t>(w[e] & 0xFFFFu);
+      }
     }
   } else {
     if (ncols >= 32) {
@@ -102,16 +123,18 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 #pragma unroll
       for (int e = 0; e < 8; ++e) d4[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
     } else {
-      for (int e = 0; e < ncols; ++e) dst[e] = v[e];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (e < ncols) dst[e] = v[e];
     }
   }
 }
 
-template <typename T, int kDP, int kNQ, int kBN, int kStages>
+template <typename T, int kDP, int kNQ, int kBN, int kStages, int kSB>
 __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     fa_fwd_kernel(const __grid_constant__ FaKernelParams p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
-  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages>;
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages, kSB>;
   constexpr float kNegInf = -INFINITY;
 
   extern __shared__ uint8_t smem_raw[];
@@ -126,9 +149,9 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
   uint64_t* bar_v_full = bar_k_full + kStages;
   uint64_t* bar_k_empty = bar_v_full + kStages;
   uint64_t* bar_v_empty = bar_k_empty + kStages;
-  uint64_t* bar_s_full = bar_v_empty + kStages;
-  uint64_t* bar_p_full = bar_s_full + kNQ;
-  uint64_t* bar_o_done = bar_p_full + kNQ;
+  uint64_t* bar_s_full = bar_v_empty + kStages;  // [kSlots]
+  uint64_t* bar_p_full = bar_s_full + C::kSlots; // [kSlots]
+  uint64_t* bar_o_done = bar_p_full + C::kSlots; // [kNQ]
   uint64_t* bar_teardown = bar_o_done + kNQ;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_teardown + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -156,11 +179,11 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       mbar_init(bar_k_empty + s, 1);
       mbar_init(bar_v_empty + s, 1);
     }
-    for (int i = 0; i < kNQ; ++i) {
-      mbar_init(bar_s_full + i, 1);
-      mbar_init(bar_p_full + i, C::kBM);
-      mbar_init(bar_o_done + i, 1);
+    for (int x = 0; x < C::kSlots; ++x) {
+      mbar_init(bar_s_full + x, 1);
+      mbar_init(bar_p_full + x, 4);  // one arrival per softmax warp
     }
+    for (int i = 0; i < kNQ; ++i) mbar_init(bar_o_done + i, 1);
     mbar_init(bar_teardown, 1);
     *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
     mbar_fence_init();
@@ -221,8 +244,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     const uint32_t sq_addr = smem_u32(sQ);
     const uint32_t sk_addr = smem_u32(sK);
     const uint32_t sv_addr = smem_u32(sV);
-    auto issue_qk = [&](int i, int s) {
-      const uint32_t d = tmem + C::tmem_s(i);
+    auto issue_qk = [&](int i, int slot, int s) {
+      const uint32_t d = tmem + C::tmem_s(slot);
 #pragma unroll
       for (int kk = 0; kk < kDP / C::kKInstr; ++kk) {
         const int a = kk >> 2;
@@ -235,9 +258,9 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
           mma_ss_f16(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
       }
     };
-    auto issue_pv = [&](int i, int s, bool acc) {
+    auto issue_pv = [&](int i, int slot, int s, bool acc) {
       const uint32_t d = tmem + C::tmem_o(i);
-      const uint32_t pa = tmem + C::tmem_s(i);
+      const uint32_t pa = tmem + C::tmem_s(slot);
 #pragma unroll
       for (int kk = 0; kk < kBN / C::kKInstr; ++kk) {
         const uint64_t bd = umma_desc_mn<sizeof(T)>(sv_addr + s * C::kKVTileBytes + kk * C::kKInstr * 128,
@@ -253,39 +276,37 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
     bool ok = mbar_wait(bar_q_full, 0, abort_flag, kDevTimeoutQ);
     bool any_issued = false;
-    if (ok && nt > 0) {
-      ok = mbar_wait(bar_k_full, 0, abort_flag, kDevTimeoutKV);
-      if (ok) {
-        tc_fence_after();
-        for (int i = 0; i < kNQ; ++i) {
-          issue_qk(i, 0);
-          mma_commit(bar_s_full + i);
-        }
-        mma_commit(bar_k_empty);
-        any_issued = true;
+    // Prologue: S for the first kSB KV tiles of every Q tile.
+    for (int j = 0; ok && j < min(kSB, nt); ++j) {
+      if (!(ok = mbar_wait(bar_k_full + (j % kStages), (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+      tc_fence_after();
+      for (int i = 0; i < kNQ; ++i) {
+        issue_qk(i, i * kSB + j, j % kStages);
+        mma_commit(bar_s_full + i * kSB + j);
       }
-      for (int j = 0; ok && j < nt; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int s1 = (j + 1) % kStages;
-        const uint32_t ph1 = ((j + 1) / kStages) & 1;
-        if (!(ok = mbar_wait(bar_v_full + s, ph, abort_flag, kDevTimeoutKV))) break;
-        for (int i = 0; i < kNQ; ++i) {
-          if (!(ok = mbar_wait(bar_p_full + i, j & 1, abort_flag, kDevTimeoutP))) break;
+      mma_commit(bar_k_empty + (j % kStages));
+      any_issued = true;
+    }
+    for (int j = 0; ok && j < nt; ++j) {
+      const int s = j % kStages;
+      if (!(ok = mbar_wait(bar_v_full + s, (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+      const int jn = j + kSB;  // the KV tile whose S product reuses this S buffer
+      const int sn = jn % kStages;
+      for (int i = 0; i < kNQ; ++i) {
+        const int slot = i * kSB + (j % kSB);
+        if (!(ok = mbar_wait(bar_p_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutP))) break;
+        tc_fence_after();
+        issue_pv(i, slot, s, j > 0);
+        // With one S buffer nobody needs O before the end; with two, the
+        // softmax may rescale O while this product is still in flight.
+        if (kSB == 2 || j == nt - 1) mma_commit(bar_o_done + i);
+        if (i == kNQ - 1) mma_commit(bar_v_empty + s);
+        if (jn < nt) {
+          if (i == 0 && !(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
           tc_fence_after();
-          issue_pv(i, s, j > 0);
-          mma_commit(bar_o_done + i);
-          if (i == kNQ - 1) mma_commit(bar_v_empty + s);
-          if (j + 1 < nt) {
-            if (i == 0 && !(ok = mbar_wait(bar_k_full + s1, ph1, abort_flag, kDevTimeoutKV))) break;
-            // S_i(j+1) reuses the TMEM columns that P_i(j) occupies: start it
-            // only after the P*V product that reads them has completed.
-            if (!(ok = mbar_wait(bar_o_done + i, j & 1, abort_flag, kDevTimeoutO))) break;
-            tc_fence_after();
-            issue_qk(i, s1);
-            mma_commit(bar_s_full + i);
-            if (i == kNQ - 1) mma_commit(bar_k_empty + s1);
-          }
+          issue_qk(i, slot, sn);
+          mma_commit(bar_s_full + slot);
+          if (i == kNQ - 1) mma_commit(bar_k_empty + sn);
         }
       }
     }
@@ -302,14 +323,15 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     const int r = wq * 32 + lane;
     const int row = m0 + i * C::kBM + r;
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t t_s = tmem + lane_base + C::tmem_s(i);
     const uint32_t t_o = tmem + lane_base + C::tmem_o(i);
     const float c = p.scale_log2;
     float m_run = kNegInf;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      if (!(ok = mbar_wait_warp(bar_s_full + i, j & 1, abort_flag, kDevTimeoutS))) break;
+      const int slot = i * kSB + (j % kSB);
+      const uint32_t t_s = tmem + lane_base + C::tmem_s(slot);
+      if (!(ok = mbar_wait_warp(bar_s_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutS))) break;
       tc_fence_after();
       float s[kBN];
 #pragma unroll
@@ -328,44 +350,66 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         for (int e = 0; e < kBN; ++e)
           if (col0 + e >= lim) s[e] = kNegInf;
       }
-      float mx = s[0];
+      // Row max: eight independent three-input max chains.
+      float mxv[8];
 #pragma unroll
-      for (int e = 1; e < kBN; ++e) mx = fmaxf(mx, s[e]);
+      for (int a = 0; a < 8; ++a) mxv[a] = s[a];
+#pragma unroll
+      for (int e = 8; e + 16 <= kBN; e += 16)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mxv[a] = fmax3(mxv[a], s[e + a], s[e + 8 + a]);
+      if constexpr (kBN % 16 == 8)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mxv[a] = fmaxf(mxv[a], s[kBN - 8 + a]);
+      const float mx = fmax3(fmax3(mxv[0], mxv[1], mxv[2]), fmax3(mxv[3], mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]));
       const float m_cand = fmaxf(m_run, mx * c);
       const bool rescale = m_cand > m_run + 8.0f;
       const float m_new = rescale ? m_cand : m_run;
       const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.0f;
       const float m_base = (m_new == kNegInf) ? 0.f : m_new;
-      float lsum = 0.f;
+      // p = 2^(s*c - m_base), two scores at a time.
+      const float2 c2 = make_float2(c, c);
+      const float2 nmb2 = make_float2(-m_base, -m_base);
+      float2 lsum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int cc = 0; cc < kBN / 32; ++cc) {
-        if constexpr (sizeof(T) == 2) {
-          uint32_t pk[16];
+        constexpr int kPk = sizeof(T) == 2 ? 16 : 32;
+        uint32_t pk[kPk];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(fmaf(s[cc * 32 + 2 * e], c, -m_base));
-            const float p1 = ex2_approx(fmaf(s[cc * 32 + 2 * e + 1], c, -m_base));
-            lsum += p0 + p1;
-            pk[e] = ElemOps<T>::pack2(p0, p1);
+        for (int e = 0; e < 16; ++e) {
+          const float2 x = __ffma2_rn(make_float2(s[cc * 32 + 2 * e], s[cc * 32 + 2 * e + 1]), c2, nmb2);
+          float2 pp;
+          // Spread FAB_FA_POLY_PAIRS_PER_16 polynomial pairs evenly among the 16.
+          if ((e * FAB_FA_POLY_PAIRS_PER_16) % 16 < FAB_FA_POLY_PAIRS_PER_16) {
+            pp = exp2_poly2(x);
+          } else {
+            pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
           }
+          lsum2[e & 1] = __fadd2_rn(lsum2[e & 1], pp);
+          if constexpr (sizeof(T) == 2) {
+            pk[e] = ElemOps<T>::pack2(pp.x, pp.y);
+          } else {
+            pk[2 * e] = __float_as_uint(pp.x);
+            pk[2 * e + 1] = __float_as_uint(pp.y);
+          }
+        }
+        if constexpr (sizeof(T) == 2) {
           tmem_st16(t_s + cc * 16, pk);
         } else {
-          uint32_t pk[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float p0 = ex2_approx(fmaf(s[cc * 32 + e], c, -m_base));
-            lsum += p0;
-            pk[e] = __float_as_uint(p0);
-          }
           tmem_st32(t_s + cc * 32, pk);
         }
       }
+      const float2 lsum_pair = __fadd2_rn(lsum2[0], lsum2[1]);
+      const float lsum = lsum_pair.x + lsum_pair.y;
       tmem_wait_st();
       if (j > 0) {
-        // O_i must hold the finished product of KV tile j-1 before it is
-        // rescaled and before P_i(j) is released to the MMA issuer.
-        if (!(ok = mbar_wait_warp(bar_o_done + i, (j - 1) & 1, abort_flag, kDevTimeoutO))) break;
-        tc_fence_after();
+        // With one S buffer, S_i(j) was issued after P*V of tile j-1 and its
+        // commit covers that product, so O_i is already final here.  With two
+        // S buffers that product may still be running: wait for it.
+        if constexpr (kSB == 2) {
+          if (!(ok = mbar_wait_warp(bar_o_done + i, (j - 1) & 1, abort_flag, kDevTimeoutO))) break;
+          tc_fence_after();
+        }
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int cc = 0; cc < kDP / 32; ++cc) {
@@ -382,13 +426,17 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       l_run = l_run * alpha + lsum;
       m_run = m_new;
       tc_fence_before();
-      mbar_arrive(bar_p_full + i);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p_full + slot);
     }
 
     // ------------------------------------------------------------ epilogue
     T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sm;
     if (ok && nt > 0) {
-      ok = mbar_wait_warp(bar_o_done + i, (nt - 1) & 1, abort_flag, kDevTimeoutO);
+      // One S buffer: O's only commit comes after the last product (phase 0);
+      // two: one commit per KV tile.
+      const uint32_t last_phase = kSB == 2 ? ((nt - 1) & 1) : 0u;
+      ok = mbar_wait_warp(bar_o_done + i, last_phase, abort_flag, kDevTimeoutO);
       if (ok) {
         tc_fence_after();
         const float inv_l = 1.0f / l_run;
@@ -427,10 +475,10 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
 // ---------------------------------------------------------------- host side
 
-template <typename T, int kDP, int kNQ, int kBN, int kStages>
+template <typename T, int kDP, int kNQ, int kBN, int kStages, int kSB>
 static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
-  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages>;
-  auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kStages>;
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages, kSB>;
+  auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kStages, kSB>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
   CUtensorMap tq, tk, tv;
@@ -443,10 +491,12 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, L.M, L.Hq, L.B, L.q_ss, L.q_sh, L.q_sb, C::kAtom, C::kBM,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_bhsd_map(&tk, L.k, dt, elt, L.D, L.N, L.Hkv, L.B, L.k_ss, L.k_sh, L.k_sb, C::kAtom, kBN,
+  // With no keys the kernel never reads K/V, but a tensor map needs extents >= 1.
+  const int n_map = L.N > 0 ? L.N : 1;
+  rc = make_bhsd_map(&tk, L.k, dt, elt, L.D, n_map, L.Hkv, L.B, L.k_ss, L.k_sh, L.k_sb, C::kAtom, kBN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_bhsd_map(&tv, L.v, dt, elt, L.D, L.N, L.Hkv, L.B, L.v_ss, L.v_sh, L.v_sb, C::kAtom, kBN, v_swz);
+  rc = make_bhsd_map(&tv, L.v, dt, elt, L.D, n_map, L.Hkv, L.B, L.v_ss, L.v_sh, L.v_sb, C::kAtom, kBN, v_swz);
   if (rc) return rc;
   FaKernelParams kp;
   kp.o = L.o;
@@ -473,80 +523,88 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 
-// Per-(dtype, padded head dim) tile table for sm_100a.  Returns the chosen
-// configuration's static facts for the tuner and the launch.
+// The sm_100a tile table: one instantiation per (element size, padded head dim).
+#define FAB_FA_TABLE(X)                                  \
+  X(2, 64, 2, 128, 3, 1)    /* 16-bit, head dim <= 64 */  \
+  X(2, 128, 2, 128, 2, 1)   /* 16-bit, head dim <= 128 */ \
+  X(2, 256, 1, 64, 2, 2)    /* 16-bit, head dim <= 256 */ \
+  X(4, 64, 2, 128, 2, 1)    /* fp32/tf32, head dim <= 64 */ \
+  X(4, 128, 1, 64, 2, 2)    /* fp32/tf32, head dim <= 128 */
+
+static bool fa_table_lookup(int elt, int D, int* d_pad) {
+  int best = 0;
+#define FAB_FA_PICK(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && D <= DP && (best == 0 || DP < best)) best = DP;
+  FAB_FA_TABLE(FAB_FA_PICK)
+#undef FAB_FA_PICK
+  *d_pad = best;
+  return best != 0;
+}
+
 int fa_select_config(int dtype, int D, FaConfigInfo* out) {
   if (D <= 0) return kErrInvalidArg;
-  FaConfigInfo c{};
-  if (dtype == kDtypeF32) {
-    if (D <= 64) {
-      c = {64, 2, 128, 2, FaCfg<4, 64, 2, 128, 2>::kThreads, FaCfg<4, 64, 2, 128, 2>::kSmemBytes,
-           FaCfg<4, 64, 2, 128, 2>::kTmemAlloc};
-    } else if (D <= 128) {
-      c = {128, 1, 64, 2, FaCfg<4, 128, 1, 64, 2>::kThreads, FaCfg<4, 128, 1, 64, 2>::kSmemBytes,
-           FaCfg<4, 128, 1, 64, 2>::kTmemAlloc};
-    } else {
-      return kErrUnsupported;
-    }
-  } else if (dtype == kDtypeF16 || dtype == kDtypeBF16) {
-    if (D <= 64) {
-      c = {64, 2, 128, 3, FaCfg<2, 64, 2, 128, 3>::kThreads, FaCfg<2, 64, 2, 128, 3>::kSmemBytes,
-           FaCfg<2, 64, 2, 128, 3>::kTmemAlloc};
-    } else if (D <= 128) {
-      c = {128, 2, 128, 2, FaCfg<2, 128, 2, 128, 2>::kThreads, FaCfg<2, 128, 2, 128, 2>::kSmemBytes,
-           FaCfg<2, 128, 2, 128, 2>::kTmemAlloc};
-    } else if (D <= 256) {
-      c = {256, 1, 64, 2, FaCfg<2, 256, 1, 64, 2>::kThreads, FaCfg<2, 256, 1, 64, 2>::kSmemBytes,
-           FaCfg<2, 256, 1, 64, 2>::kTmemAlloc};
-    } else {
-      return kErrUnsupported;
-    }
-  } else {
-    return kErrInvalidArg;
+  if (dtype != kDtypeF16 && dtype != kDtypeBF16 && dtype != kDtypeF32) return kErrInvalidArg;
+  const int elt = dtype == kDtypeF32 ? 4 : 2;
+  int dp = 0;
+  if (!fa_table_lookup(elt, D, &dp)) return kErrUnsupported;
+#define FAB_FA_FILL(E, DP, NQ, BN, ST, SB)                                                         \
+  if (elt == E && dp == DP) {                                                                     \
+    using Cf = FaCfg<E, DP, NQ, BN, ST, SB>;                                                      \
+    *out = FaConfigInfo{DP, NQ, BN, ST, Cf::kThreads, Cf::kSmemBytes, Cf::kTmemAlloc, SB};        \
+    return 0;                                                                                     \
   }
-  *out = c;
-  return 0;
+  FAB_FA_TABLE(FAB_FA_FILL)
+#undef FAB_FA_FILL
+  return kErrUnsupported;
+}
+
+// Dispatch helpers: templates, so the branch for the other element size is
+// discarded instead of instantiated.
+template <int E, int DP, int NQ, int BN, int ST, int SB>
+static int launch_entry(const FaLaunch& L, cudaStream_t stream) {
+  if constexpr (E == 4) {
+    return launch_fa<float, DP, NQ, BN, ST, SB>(L, stream);
+  } else {
+    if (L.dtype == kDtypeBF16) return launch_fa<__nv_bfloat16, DP, NQ, BN, ST, SB>(L, stream);
+    return launch_fa<__half, DP, NQ, BN, ST, SB>(L, stream);
+  }
+}
+
+template <int E, int DP, int NQ, int BN, int ST, int SB>
+static const void* kernel_entry(int dtype) {
+  if constexpr (E == 4) {
+    return reinterpret_cast<const void*>(fa_fwd_kernel<float, DP, NQ, BN, ST, SB>);
+  } else {
+    if (dtype == kDtypeBF16) return reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, DP, NQ, BN, ST, SB>);
+    return reinterpret_cast<const void*>(fa_fwd_kernel<__half, DP, NQ, BN, ST, SB>);
+  }
 }
 
 int fa_forward(const FaLaunch& L, cudaStream_t stream) {
   FaConfigInfo c;
   int rc = fa_select_config(L.dtype, L.D, &c);
   if (rc) return rc;
-  if (L.dtype == kDtypeF32) {
-    if (c.d_pad == 64) return launch_fa<float, 64, 2, 128, 2>(L, stream);
-    return launch_fa<float, 128, 1, 64, 2>(L, stream);
-  }
-  if (L.dtype == kDtypeBF16) {
-    if (c.d_pad == 64) return launch_fa<__nv_bfloat16, 64, 2, 128, 3>(L, stream);
-    if (c.d_pad == 128) return launch_fa<__nv_bfloat16, 128, 2, 128, 2>(L, stream);
-    return launch_fa<__nv_bfloat16, 256, 1, 64, 2>(L, stream);
-  }
-  if (c.d_pad == 64) return launch_fa<__half, 64, 2, 128, 3>(L, stream);
-  if (c.d_pad == 128) return launch_fa<__half, 128, 2, 128, 2>(L, stream);
-  return launch_fa<__half, 256, 1, 64, 2>(L, stream);
+  const int elt = L.dtype == kDtypeF32 ? 4 : 2;
+#define FAB_FA_LAUNCH(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && c.d_pad == DP) return launch_entry<E, DP, NQ, BN, ST, SB>(L, stream);
+  FAB_FA_TABLE(FAB_FA_LAUNCH)
+#undef FAB_FA_LAUNCH
+  return kErrUnsupported;
 }
 
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads) {
   FaConfigInfo c;
   int rc = fa_select_config(dtype, D, &c);
   if (rc) return rc;
-  cudaFuncAttributes a{};
-  cudaError_t e = cudaSuccess;
+  const int elt = dtype == kDtypeF32 ? 4 : 2;
   const void* k = nullptr;
-  if (dtype == kDtypeF32) {
-    k = c.d_pad == 64 ? reinterpret_cast<const void*>(fa_fwd_kernel<float, 64, 2, 128, 2>)
-                      : reinterpret_cast<const void*>(fa_fwd_kernel<float, 128, 1, 64, 2>);
-  } else if (dtype == kDtypeBF16) {
-    k = c.d_pad == 64    ? reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 64, 2, 128, 3>)
-        : c.d_pad == 128 ? reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 128, 2, 128, 2>)
-                         : reinterpret_cast<const void*>(fa_fwd_kernel<__nv_bfloat16, 256, 1, 64, 2>);
-  } else {
-    k = c.d_pad == 64    ? reinterpret_cast<const void*>(fa_fwd_kernel<__half, 64, 2, 128, 3>)
-        : c.d_pad == 128 ? reinterpret_cast<const void*>(fa_fwd_kernel<__half, 128, 2, 128, 2>)
-                         : reinterpret_cast<const void*>(fa_fwd_kernel<__half, 256, 1, 64, 2>);
-  }
-  e = cudaFuncGetAttributes(&a, k);
-  if (e != cudaSuccess) return kErrLaunch;
+#define FAB_FA_ATTR(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && c.d_pad == DP) k = kernel_entry<E, DP, NQ, BN, ST, SB>(dtype);
+  FAB_FA_TABLE(FAB_FA_ATTR)
+#undef FAB_FA_ATTR
+  if (k == nullptr) return kErrUnsupported;
+  cudaFuncAttributes a{};
+  if (cudaFuncGetAttributes(&a, k) != cudaSuccess) return kErrLaunch;
   *regs = a.numRegs;
   *smem = c.smem_bytes;
   *threads = c.threads;

@@ -59,6 +59,7 @@ struct FaConfigInfo {
   int threads;
   int smem_bytes;
   int tmem_cols;
+  int s_bufs;
 };
 
 struct GemmKernelParams {

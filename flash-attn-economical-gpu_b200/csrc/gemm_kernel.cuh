@@ -85,8 +85,15 @@ __device__ __forceinline__ void gemm_store_chunk(Tout* dst, const float (&v)[32]
 #pragma unroll
       for (int e = 0; e < 4; ++e) d4[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
     } else {
-      const Tout* src = reinterpret_cast<const Tout*>(pk);
-      for (int e = 0; e < ncols; ++e) dst[e] = src[e];
+      // Ragged edge: static indices only, so pk stays in registers.
+      uint32_t* d2 = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        if (2 * e + 1 < ncols)
+          d2[e] = pk[e];
+        else if (2 * e < ncols)
+          reinterpret_cast<uint16_t*>(dst)[2 * e] = static_cast<uint16_t>(pk[e] & 0xFFFFu);
+      }
     }
   } else {
     if (ncols >= 32) {
@@ -94,7 +101,9 @@ __device__ __forceinline__ void gemm_store_chunk(Tout* dst, const float (&v)[32]
 #pragma unroll
       for (int e = 0; e < 8; ++e) d4[e] = make_float4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
     } else {
-      for (int e = 0; e < ncols; ++e) dst[e] = w[e];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (e < ncols) dst[e] = w[e];
     }
   }
 }

@@ -302,4 +302,38 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe, leaving the MUFU unit to other work.
+// Method: Cody & Waite range reduction, x = n + f with n = round(x) taken from
+// the low mantissa bits of x + 1.5*2^23 and f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial whose coefficients are a relative-error minimax (Remez)
+// fit made for this library (max relative error 7.5e-5, below the rounding of
+// P to bf16/fp16/tf32); 2^n applied by adding n to the exponent field.
+// Inputs below -126 are clamped there (the result is then < 1e-37).
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 j = __fadd2_rn(x, make_float2(kRoundMagic, kRoundMagic));
+  const float2 n = __fadd2_rn(j, make_float2(-kRoundMagic, -kRoundMagic));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(f, make_float2(kExp2C3, kExp2C3), make_float2(kExp2C2, kExp2C2));
+  p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+  p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+  const uint32_t rx = __float_as_uint(p.x) + (__float_as_uint(j.x) << 23);
+  const uint32_t ry = __float_as_uint(p.y) + (__float_as_uint(j.y) << 23);
+  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
+}
+
 }  // namespace fab

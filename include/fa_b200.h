@@ -150,6 +150,7 @@ typedef struct fab_fa_config {
   int threads;
   int smem_bytes;
   int tmem_columns;
+  int s_buffers;       /* S/P buffers per query tile in TMEM (2 lets S(j+1) overlap softmax(j)) */
 } fab_fa_config;
 
 int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out);

@@ -37,8 +37,14 @@ def tiled_attention_forward(
     p_dtype: str = "fp32",
     block_m: int = 64,
     block_n: int = 64,
+    q_row_offset: int = 0,
 ) -> tuple[np.ndarray, np.ndarray]:
-    """Returns (o [B,Hq,M,D] fp32, lse [B,Hq,M] fp32) for q [B,Hq,M,D], k/v [B,Hkv,N,D]."""
+    """Returns (o [B,Hq,M,D] fp32, lse [B,Hq,M] fp32) for q [B,Hq,M,D], k/v [B,Hkv,N,D].
+
+    `q_row_offset` treats q as rows [offset, offset + M) of a longer query
+    sequence (the causal mask then compares offset + m with n), so a slice of
+    a large problem can be checked on its own.
+    """
     q = np.asarray(q, dtype=np.float32)
     k = np.asarray(k, dtype=np.float32)
     v = np.asarray(v, dtype=np.float32)
@@ -65,7 +71,8 @@ def tiled_attention_forward(
                         cols = np.arange(n0, min(n0 + block_n, N))
                         qk = (qt @ k[b, hk, cols].T).astype(np.float32) * np.float32(sm_scale)
                         if causal:
-                            qk = np.where(rows[:, None] >= cols[None, :], qk, -np.inf).astype(np.float32)
+                            visible = (rows[:, None] + q_row_offset) >= cols[None, :]
+                            qk = np.where(visible, qk, -np.inf).astype(np.float32)
                         m_ij = np.maximum(m_i, qk.max(axis=1))
                         p = np.exp(qk - m_ij[:, None]).astype(np.float32)
                         l_ij = p.sum(axis=1, dtype=np.float32)

@@ -73,22 +73,23 @@ def test_return_code_mapping():
 @pytest.mark.parametrize(
     "dtype, D, expect",
     [
-        # (head_dim_padded, q_tiles_per_cta, block_n, stages)
-        (_native.FAB_DTYPE_BF16, 64, (64, 2, 128, 3)),
-        (_native.FAB_DTYPE_BF16, 128, (128, 2, 128, 2)),
-        (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 2)),
-        (_native.FAB_DTYPE_F16, 256, (256, 1, 64, 2)),
-        (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 2)),
-        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 2)),
+        # (head_dim_padded, q_tiles_per_cta, block_n, stages, s_buffers)
+        (_native.FAB_DTYPE_BF16, 64, (64, 2, 128, 3, 1)),
+        (_native.FAB_DTYPE_BF16, 128, (128, 2, 128, 2, 1)),
+        (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 2, 1)),
+        (_native.FAB_DTYPE_F16, 256, (256, 1, 64, 2, 2)),
+        (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 2, 1)),
+        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 2, 2)),
     ],
 )
 def test_tile_table(dtype, D, expect):
     cfg = _native.fa_config(dtype, D)
-    assert (cfg.head_dim_padded, cfg.q_tiles_per_cta, cfg.block_n, cfg.stages) == expect
+    assert (cfg.head_dim_padded, cfg.q_tiles_per_cta, cfg.block_n, cfg.stages, cfg.s_buffers) == expect
     assert cfg.threads == 128 * (1 + cfg.q_tiles_per_cta)
     assert cfg.smem_bytes <= 232448
     assert cfg.tmem_columns in (256, 512)
-    assert cfg.q_tiles_per_cta * (cfg.block_n + cfg.head_dim_padded) <= cfg.tmem_columns
+    used = cfg.q_tiles_per_cta * (cfg.s_buffers * cfg.block_n + cfg.head_dim_padded)
+    assert used <= cfg.tmem_columns
 
 
 def test_tile_table_rejects_out_of_range_head_dims():

@@ -1,0 +1,278 @@
+"""Attention forward on the GPU, through the C ABI, against the reference and the oracle.
+
+Tolerance: fp16/bf16 outputs within max-abs 2e-2 and
+rtol 1e-2 of an fp32 reference on the same inputs; the LSE is compared in
+fp32 (atol 2e-3).  fp32 inputs run on the tensor cores as tf32, like the
+reference's Triton `tl.dot` default, under the same tolerance.
+"""
+from __future__ import annotations
+
+import json
+import zlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import _native
+import flash_atten
+from flash_atten import attention_forward, flash_attention
+from oracle.fa_oracle import tiled_attention_forward
+from tuner import (
+    FlashAttenTuneArguments,
+    FlashAttentionBlockDNomaskTuner,
+    FlashAttentionOptimizeSharedMemTuner,
+    FlashAttentionTuner,
+)
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 2e-2
+LSE_ATOL = 2e-3
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = json.loads((GOLDEN / "golden.json").read_text())["cases"]
+ARRAYS = np.load(GOLDEN / "golden.npz")
+P_DTYPE = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(cuda_device):
+    yield
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0, "a kernel gave up on a bounded wait"
+
+
+def _close(actual: torch.Tensor, expected, rtol=RTOL, atol=ATOL):
+    expected = torch.as_tensor(np.asarray(expected, dtype=np.float32))
+    torch.testing.assert_close(actual.detach().float().cpu(), expected, rtol=rtol, atol=atol)
+
+
+def _inputs(shape, dtype, seed, dev):
+    B, Hq, Hkv, M, N, D = shape
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, M, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    v = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    return q, k, v, q.to(dev), k.to(dev), v.to(dev)
+
+
+def _oracle(q, k, v, causal, dtype, sm_scale=None):
+    return tiled_attention_forward(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal,
+                                   p_dtype=P_DTYPE[dtype], sm_scale=sm_scale)
+
+
+# ------------------------------------------------------------ golden vectors
+ATT = [c for c in CASES if c["kind"] == "attention"]
+
+
+@pytest.mark.parametrize("case", ATT, ids=lambda c: c["name"])
+def test_reference_golden_through_dropin(case, cuda_device):
+    """The reference's own outputs, reproduced through the same entry point the reference case used."""
+    g = lambda key: torch.from_numpy(ARRAYS[f"{case['name']}.{key}"])  # noqa: E731
+    q, k, v = (g(x).to(cuda_device) for x in ("q", "k", "v"))
+    ref_o = ARRAYS[f"{case['name']}.o"]
+    if case["Hkv"] != case["Hq"]:
+        o = attention_forward(q, k, v, causal=case["causal"], sm_scale=case["sm_scale"])
+        _close(o, ref_o)
+        return
+    tuner_cls = {
+        "_flash_attn_fwd_kernel_basic": FlashAttentionTuner,
+        "_flash_attn_fwd_kernel_optimize_shared_mem": FlashAttentionOptimizeSharedMemTuner,
+        "_flash_attn_fwd_kernel_block_d_nomask_contiguous": FlashAttentionBlockDNomaskTuner,
+    }[case["kernel"]]
+    spec = tuner_cls(tuple(q.shape), tuple(k.shape), tuple(v.shape), q.element_size(), causal=case["causal"],
+                     return_lse=case["has_lse"]).build_flash_attention_launch_spec(q, k, v, sm_scale=case["sm_scale"])
+    out = flash_attention(spec)
+    if case["has_lse"]:
+        o, lse = out
+        _close(lse, ARRAYS[f"{case['name']}.lse"], rtol=1e-4, atol=LSE_ATOL)
+    else:
+        o = out
+    assert o.dtype == q.dtype and tuple(o.shape) == tuple(q.shape)
+    _close(o, ref_o)
+
+
+def test_config1_exact_baseline_case(cuda_device):
+    """B1 H4 S256 D64 fp32 N(0,1) from seed 0, scale 1/8, vs torch SDPA math on CPU."""
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, 4, 256, 64, generator=g) for _ in range(3))
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=0.125)
+    spec = FlashAttentionTuner(tuple(q.shape), tuple(k.shape), tuple(v.shape), 4, causal=False,
+                               return_lse=False).build_flash_attention_launch_spec(
+        q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), sm_scale=0.125)
+    _close(flash_attention(spec), ref.numpy())
+
+
+# --------------------------------------------------------- oracle parity sweep
+SHAPES = [
+    (1, 2, 2, 128, 128, 64),
+    (1, 2, 2, 257, 300, 64),
+    (2, 2, 2, 384, 200, 128),
+    (1, 3, 3, 1, 77, 128),
+    (1, 2, 2, 129, 513, 128),
+    (1, 2, 2, 200, 190, 256),
+    (1, 2, 2, 65, 257, 256),
+    (1, 2, 2, 100, 33, 80),
+    (1, 1, 1, 33, 45, 16),
+]
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "B{}H{}/{}M{}N{}D{}".format(*s))
+def test_oracle_parity_16bit(shape, dtype, causal, cuda_device):
+    q, k, v, qd, kd, vd = _inputs(shape, dtype, seed=zlib.crc32(repr((shape, str(dtype), causal)).encode()),
+                                  dev=cuda_device)
+    o, lse = attention_forward(qd, kd, vd, causal=causal, return_lse=True)
+    ro, rl = _oracle(q, k, v, causal, dtype)
+    _close(o, ro)
+    _close(lse, rl, rtol=1e-4, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+@pytest.mark.parametrize("shape", [(1, 4, 4, 256, 256, 64), (1, 2, 2, 150, 130, 128), (1, 2, 2, 70, 99, 32),
+                                   (2, 2, 1, 129, 200, 100)], ids=lambda s: "B{}H{}/{}M{}N{}D{}".format(*s))
+def test_oracle_parity_fp32_tf32(shape, causal, cuda_device):
+    q, k, v, qd, kd, vd = _inputs(shape, torch.float32, seed=11, dev=cuda_device)
+    o, lse = attention_forward(qd, kd, vd, causal=causal, return_lse=True)
+    ro, rl = _oracle(q, k, v, causal, torch.float32)
+    _close(o, ro)
+    _close(lse, rl, rtol=1e-3, atol=1e-2)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+def test_grouped_query_heads(causal, cuda_device):
+    """BASELINE config 3 GQA shape (16 query heads over 4 KV heads, D=128), shortened sequence."""
+    shape = (2, 16, 4, 640, 640, 128)
+    q, k, v, qd, kd, vd = _inputs(shape, torch.bfloat16, seed=5, dev=cuda_device)
+    o = attention_forward(qd, kd, vd, causal=causal)
+    ro, _ = _oracle(q, k, v, causal, torch.bfloat16)
+    _close(o, ro)
+
+
+def test_strided_inputs_through_basic_launcher(cuda_device):
+    """Non-contiguous q/k/v/o ([B,S,H,D] storage viewed as [B,H,S,D]) with explicit strides, as the
+    reference's basic kernel accepts (flash_atten.py:21-39)."""
+    B, H, S, D = 2, 3, 200, 64
+    g = torch.Generator().manual_seed(3)
+    qs, ks, vs = (torch.randn(B, S, H, D, generator=g).half().to(cuda_device) for _ in range(3))
+    q, k, v = (t.transpose(1, 2) for t in (qs, ks, vs))
+    o = torch.empty(B, S, H, D, dtype=torch.float16, device=cuda_device).transpose(1, 2)
+    lse = torch.empty(B, H, S, dtype=torch.float32, device=cuda_device)
+    args = (q, k, v, o, lse, *q.stride(), *k.stride(), *v.stride(), *o.stride(), *lse.stride(), H, S, S, D, D ** -0.5)
+    flash_atten._flash_attn_fwd_kernel_basic[(2, B * H)](*args, causal=True, HAS_LSE=True, BLOCK_M=128, BLOCK_N=64,
+                                                         BLOCK_N_PAD=64, BLOCK_DMODEL=64, num_warps=8, num_stages=1)
+    ro, rl = _oracle(q.cpu(), k.cpu(), v.cpu(), True, torch.float16)
+    _close(o, ro)
+    _close(lse, rl, rtol=1e-4, atol=LSE_ATOL)
+
+
+def test_unaligned_rows_and_offsets(cuda_device):
+    """Head dim whose rows are not 16-byte multiples, and a storage offset that breaks 16-byte alignment."""
+    q, k, v, qd, kd, vd = _inputs((1, 2, 2, 50, 70, 20), torch.float16, seed=8, dev=cuda_device)
+    o = attention_forward(qd, kd, vd, causal=True)
+    ro, _ = _oracle(q, k, v, True, torch.float16)
+    _close(o, ro)
+    base = torch.randn(1 + 2 * 64 * 64, dtype=torch.bfloat16, device=cuda_device)
+    qo = base[1:].view(1, 2, 64, 64)  # data_ptr is 2 bytes past an aligned boundary
+    o2 = attention_forward(qo, qo, qo)
+    ro2, _ = _oracle(qo.cpu(), qo.cpu(), qo.cpu(), False, torch.bfloat16)
+    _close(o2, ro2)
+
+
+def test_contiguous_launcher_with_reference_tune_args(cuda_device):
+    """The TTFT preset of the sliced kernel (ttft.py:145-166) on a non-tile-multiple sequence."""
+    q, k, v, qd, kd, vd = _inputs((1, 4, 4, 300, 300, 128), torch.float16, seed=9, dev=cuda_device)
+    tune = FlashAttenTuneArguments(BLOCK_N=64, BLOCK_M=128, BLOCK_N_PAD=64, BLOCK_DMODEL=128, BLOCK_DMODEL_OUTER=64,
+                                   NUM_WARPS=8, NUM_STAGES=3)
+    spec = FlashAttentionBlockDNomaskTuner(tuple(qd.shape), tuple(kd.shape), tuple(vd.shape), 2, causal=False,
+                                           return_lse=False, tune_args=tune).build_flash_attention_launch_spec(qd, kd, vd)
+    o = flash_attention(spec)
+    ro, _ = _oracle(q, k, v, False, torch.float16)
+    _close(o, ro)
+    # update_data: same spec, new inputs, same output buffer
+    q2, k2, v2, q2d, k2d, v2d = _inputs((1, 4, 4, 300, 300, 128), torch.float16, seed=10, dev=cuda_device)
+    spec.update_data((q2d, k2d, v2d))
+    o2 = flash_attention(spec)
+    assert o2.data_ptr() == o.data_ptr()
+    _close(o2, _oracle(q2, k2, v2, False, torch.float16)[0])
+
+
+@pytest.mark.parametrize("scale", [-0.2, 0.0, 1.5])
+def test_scale_variants(scale, cuda_device):
+    q, k, v, qd, kd, vd = _inputs((1, 2, 2, 130, 140, 64), torch.bfloat16, seed=12, dev=cuda_device)
+    o = attention_forward(qd, kd, vd, causal=True, sm_scale=scale)
+    ro, _ = _oracle(q, k, v, True, torch.bfloat16, sm_scale=scale)
+    _close(o, ro)
+
+
+def test_empty_inputs(cuda_device):
+    q = torch.randn(1, 2, 5, 64, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(1, 2, 0, 64, device=cuda_device, dtype=torch.bfloat16)
+    o, lse = attention_forward(q, k, k, return_lse=True)
+    assert torch.isnan(o.float()).all()  # 0/0, as the reference's acc / l_i with no keys
+    assert torch.isneginf(lse).all()
+    q0 = torch.randn(1, 2, 0, 64, device=cuda_device, dtype=torch.bfloat16)
+    kk = torch.randn(1, 2, 7, 64, device=cuda_device, dtype=torch.bfloat16)
+    assert attention_forward(q0, kk, kk).shape == (1, 2, 0, 64)
+
+
+def test_deterministic(cuda_device):
+    _, _, _, qd, kd, vd = _inputs((2, 4, 4, 700, 700, 128), torch.bfloat16, seed=13, dev=cuda_device)
+    a = attention_forward(qd, kd, vd, causal=True)
+    b = attention_forward(qd, kd, vd, causal=True)
+    assert torch.equal(a, b)
+
+
+def test_unsupported_head_dim_raises(cuda_device):
+    x = torch.randn(1, 1, 8, 512, device=cuda_device, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        attention_forward(x, x, x)
+
+
+# ------------------------------------------------------- full BASELINE sizes
+def _sampled_rows_check(q, k, v, o, causal, dtype, picks):
+    """Oracle on selected (b, h, row-block) slices of a full-size problem."""
+    for b, h, m0, m1 in picks:
+        hk = h // (q.shape[1] // k.shape[1])
+        n_end = min(k.shape[2], m1) if causal else k.shape[2]
+        qs = q[b:b + 1, h:h + 1, m0:m1].float().cpu()
+        ks = k[b:b + 1, hk:hk + 1, :n_end].float().cpu()
+        vs = v[b:b + 1, hk:hk + 1, :n_end].float().cpu()
+        ro, _ = tiled_attention_forward(qs.numpy(), ks.numpy(), vs.numpy(), causal=causal, p_dtype=P_DTYPE[dtype],
+                                        block_m=128, block_n=512, q_row_offset=m0)
+        _close(o[b, h, m0:m1], ro[0, 0])
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+def test_config2_full_size_sampled(causal, cuda_device):
+    """BASELINE config 2 at S=8192: B4 H32 D128 bf16; rows sampled across heads and positions."""
+    B, H, S, D = 4, 32, 8192, 128
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
+    o = attention_forward(q, k, v, causal=causal)
+    assert not torch.isnan(o).any()
+    picks = [(0, 0, 0, 128), (1, 17, 4096, 4224), (3, 31, 8064, 8192), (2, 5, 1000, 1100)]
+    _sampled_rows_check(q, k, v, o, causal, torch.bfloat16, picks)
+
+
+def test_config3_d256_full_size_sampled(cuda_device):
+    """D=256, B2 H16 S8192 bf16, causal, scale 1/16."""
+    B, H, S, D = 2, 16, 8192, 256
+    g = torch.Generator(device=cuda_device).manual_seed(22)
+    q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
+    o = attention_forward(q, k, v, causal=True, sm_scale=1 / 16)
+    assert not torch.isnan(o).any()
+    _sampled_rows_check(q, k, v, o, True, torch.bfloat16, [(0, 0, 0, 128), (1, 15, 8000, 8192), (0, 7, 3000, 3128)])
+
+
+def test_config3_gqa_full_size_sampled(cuda_device):
+    """BASELINE config 3 GQA: 16 query heads over 4 KV heads, D=128, S=8192, causal."""
+    B, Hq, Hkv, S, D = 2, 16, 4, 8192, 128
+    g = torch.Generator(device=cuda_device).manual_seed(23)
+    q = torch.randn(B, Hq, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16)
+    o = attention_forward(q, k, v, causal=True)
+    _sampled_rows_check(q, k, v, o, True, torch.bfloat16, [(0, 3, 0, 128), (1, 12, 6000, 6128), (1, 15, 8064, 8192)])
