@@ -53,6 +53,15 @@ struct FaCfg {
   static constexpr int kKVTileBytes = kKVAtomBytes * kNumAtoms;
   static constexpr int kKInstr = 32 / kElt;          // K extent of one MMA instruction
   static constexpr int kThreads = 128 + kNQ * 128;
+  // Register split for the 384-thread shape: the launch gives every thread
+  // kLaunchRegs; the TMA/MMA warpgroup gives registers back so the two
+  // softmax warpgroups can hold a whole 128-column S row without spilling.
+  static constexpr bool kSplitRegs = kNQ == 2;
+  static constexpr int kLaunchRegs = 168;            // 65536 / 384, rounded down to 8
+  static constexpr int kProducerRegs = 72;
+  static constexpr int kSoftmaxRegs = 216;
+  static_assert(!kSplitRegs || 128 * kProducerRegs + kNQ * 128 * kSoftmaxRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the block's launch allocation");
   static constexpr int kSlots = kNQ * kSB;           // S/P buffers in TMEM
   static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
@@ -197,7 +206,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const bool skip = *abort_flag != 0;
-
+  // Role dispatch.  Warpgroup 0 (TMA producer, MMA issuer, two spare warps)
+  // and the softmax warpgroups each re-split registers first, unconditionally
+  // and warpgroup-uniformly, so the release always happens and the softmax
+  // increase can always be satisfied; each role's code stays inside its
+  // warpgroup's branch.
+  if (warp < 4) {
+    if constexpr (C::kSplitRegs) setmaxnreg_dec<C::kProducerRegs>();
   if (!skip && warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     tma_prefetch_desc(&tm_q);
@@ -316,7 +331,10 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       mma_commit(bar_teardown);
       mbar_wait(bar_teardown, 0, &no_abort, kDevTimeoutTeardown);
     }
-  } else if (!skip && warp >= 4) {
+  }
+  } else {
+    if constexpr (C::kSplitRegs) setmaxnreg_inc<C::kSoftmaxRegs>();
+  if (!skip) {
     // ------------------------------------------------------------ softmax
     const int i = (warp - 4) >> 2;
     const int wq = warp & 3;
@@ -463,6 +481,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       if (p.lse != nullptr) p.lse[b * p.l_sb + h * p.l_sh + static_cast<int64_t>(row) * p.l_sm] = kNegInf;
     }
   }
+  }
 
   // ------------------------------------------------------------ teardown
   tc_fence_before();
@@ -481,6 +500,13 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kStages, kSB>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
+  if constexpr (C::kSplitRegs) {
+    // The register split assumes the launch allocation it was sized for;
+    // refuse to launch a build that was compiled to anything else.
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, reinterpret_cast<const void*>(kern)) != cudaSuccess) return kErrLaunch;
+    if (a.numRegs != C::kLaunchRegs) return kErrUnsupported;
+  }
   CUtensorMap tq, tk, tv;
   const int elt = sizeof(T);
   const CUtensorMapDataType dt = elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
