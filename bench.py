@@ -412,6 +412,41 @@ def run_attention(args, world, rank, local):
     return result
 
 
+# ------------------------------------------------------------------- ttft
+def run_ttft(args, world, rank, local):
+    """Qwen2.5-7B-architecture prefill TTFT, tensor-parallel over the job's GPUs.
+
+    Same seeded random weights for every tensor-parallel degree; NCCL all-reduce after o_proj and
+    down_proj.  Three builds of the same decoder are timed: this repository's attention + GEMM, this
+    repository's attention + cuBLAS, and torch SDPA (cuDNN) + cuBLAS (the same-box comparator)."""
+    import ttft
+
+    dev = torch.device("cuda", local)
+    arch = ttft.KNOWN_ARCHS["Qwen/Qwen2.5-7B"]
+    shard = ttft.build_model_shard(arch, world, rank, seed=0, device=dev)
+    group = None
+    out = {"model": "Qwen2.5-7B architecture, random N(0,0.02) bf16 weights", "tp": world, "batch": 1,
+           "causal": True, "unit": "ms", "timing": "wall clock per prefill, synchronised, max over ranks"}
+    builds = {
+        "ours": ttft.Backends(attention="native", gemm="native"),
+        "ours_attention_cublas_gemm": ttft.Backends(attention="native", gemm="cublas"),
+        "torch_cudnn_sdpa_cublas": ttft.Backends(attention="cudnn", gemm="cublas"),
+    }
+    for S in args.ttft_lengths:
+        ids = ttft._make_random_input_ids(S, arch.vocab_size, dev, seed=S)
+        row = {}
+        for name, be in builds.items():
+            try:
+                samples = ttft.time_decoder_ttft_ms(shard, ids, be, repeats=args.ttft_repeats, warmups=1, group=group)
+                row[name] = round(statistics.median(samples), 2)
+            except Exception as exc:
+                row[name] = f"unavailable: {type(exc).__name__}: {str(exc)[:80]}"
+        out[f"prompt_{S}"] = row
+    del shard
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ gemm arm
 def run_gemm(args, world, rank, local):
     import _native
@@ -548,6 +583,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch comparators")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
+    ap.add_argument("--no-ttft", action="store_true", help="skip the Qwen2.5-7B-architecture TTFT measurement")
+    ap.add_argument("--ttft-lengths", type=int, nargs="+", default=[2048, 8192])
+    ap.add_argument("--ttft-repeats", type=int, default=3)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -564,6 +602,11 @@ def main():
             result = run_gemm(args, world, rank, local)
         else:
             result = run_attention(args, world, rank, local)
+            torch.cuda.empty_cache()
+            if not args.no_ttft:
+                ttft_result = run_ttft(args, world, rank, local)
+                if result is not None:
+                    result["ttft"] = ttft_result
         if rank == 0 and result is not None:
             print(json.dumps(result), flush=True)
     finally:

@@ -1,0 +1,760 @@
+"""Prefill time-to-first-token with the B200 attention kernel (drop-in for the reference's ttft.py).
+
+Two parts.
+
+1. The SDPA backend swap, with the reference's names and behaviour
+   (ttft.py:169-398): `backend_context(name, allow_causal_custom=, stats=)`
+   patches `torch.nn.functional.scaled_dot_product_attention` inside a `with`
+   block.  The backends "triton_block_d_nomask" / "triton_gqa" (names kept for
+   callers) route every SDPA call to the sm_100a kernel; grouped-query heads
+   are mapped in the kernel instead of `repeat_interleave` (ttft.py:203-209),
+   and `is_causal` is honoured when allowed (the reference computes
+   non-causal attention there, ttft.py:317-321).  "math", "efficient",
+   "flash" select torch's own backends as in the reference.
+
+2. A Qwen2.5-7B-architecture decoder (28 layers, hidden 3584, 28/4 heads,
+   head dim 128, SwiGLU 18944, vocab 152064, RMSNorm 1e-6, RoPE theta 1e6),
+   random N(0, 0.02) bf16 weights from a seed (no checkpoint download here),
+   tensor-parallel across ranks by attention heads and MLP columns with an
+   all-reduce after o_proj and after down_proj.  Uneven head counts (28 query
+   heads over 8 ranks) get a 4/4/4/4/3/3/3/3 split; a rank whose query heads
+   span two key/value heads issues one attention call per key/value head, so
+   the grouped-query mapping stays in the kernel.  Attention and the matmuls
+   are pluggable: "native" uses this repository's kernels, "torch" uses torch
+   SDPA (a chosen backend) and cuBLAS, the same-box comparator.
+
+TTFT is measured as in ttft.py:449-480: one forward over the prompt producing
+the last position's logits and its argmax, synchronised, repeated.
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import gc
+import math
+import os
+import statistics
+import time
+import warnings
+from dataclasses import dataclass, field
+from typing import Callable, Iterator
+
+import torch
+import torch.nn.functional as F
+
+from flash_atten import attention_forward, flash_attention
+from tuner import FlashAttentionBlockDNomaskTuner, FlashAttenTuneArguments
+
+try:
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+except ImportError:  # pragma: no cover - depends on the local torch build.
+    SDPBackend = None
+    sdpa_kernel = None
+
+
+DEFAULT_MODELS = ("Qwen/Qwen2.5-7B",)
+DEFAULT_PROMPT_LENGTHS = (2048, 8192)
+DTYPE = torch.bfloat16
+DEVICE = "cuda"
+
+
+# ------------------------------------------------------------------ shapes
+@dataclass(frozen=True)
+class ModelShape:
+    model_id: str
+    hidden_size: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    num_hidden_layers: int
+    head_dim: int
+    full_attention_layers: int
+    vocab_size: int
+
+
+@dataclass(frozen=True)
+class ArchConfig:
+    """Everything needed to build a Qwen2-family decoder from random weights."""
+
+    hidden_size: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    num_hidden_layers: int
+    head_dim: int
+    intermediate_size: int
+    vocab_size: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    qkv_bias: bool = True
+
+    def shape(self, model_id: str) -> ModelShape:
+        return ModelShape(model_id, self.hidden_size, self.num_attention_heads, self.num_key_value_heads,
+                          self.num_hidden_layers, self.head_dim, self.num_hidden_layers, self.vocab_size)
+
+
+# Architectures known without a download (published model configs).
+KNOWN_ARCHS = {
+    "Qwen/Qwen2.5-7B": ArchConfig(3584, 28, 4, 28, 128, 18944, 152064),
+    "Qwen/Qwen2.5-1.5B": ArchConfig(1536, 12, 2, 28, 128, 8960, 151936),
+    "Qwen/Qwen2.5-0.5B": ArchConfig(896, 14, 2, 24, 64, 4864, 151936),
+}
+
+
+def inspect_model_shape(model_id: str) -> ModelShape:
+    if model_id not in KNOWN_ARCHS:
+        raise ValueError(f"unknown model {model_id!r}; known: {sorted(KNOWN_ARCHS)} (no network for configs)")
+    return KNOWN_ARCHS[model_id].shape(model_id)
+
+
+def estimate_fp16_vram_gib(shape: ModelShape, prompt_len: int, parameter_count: int | None) -> float:
+    weight_bytes = 0 if parameter_count is None else parameter_count * 2
+    kv_bytes = 2 * shape.full_attention_layers * shape.num_key_value_heads * prompt_len * shape.head_dim * 2
+    return (weight_bytes + kv_bytes) / (1024 ** 3) * 1.35
+
+
+def _make_random_input_ids(prompt_len: int, vocab_size: int, device, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ids = torch.randint(0, max(1024, vocab_size), (1, prompt_len), generator=g, dtype=torch.long)
+    return ids.to(device)
+
+
+# ------------------------------------------------------- SDPA backend swap
+@dataclass(frozen=True)
+class BenchResult:
+    model_id: str
+    prompt_len: int
+    backend: str
+    mean_ms: float | None
+    p50_ms: float | None
+    samples_ms: tuple[float, ...]
+    status: str
+
+
+@dataclass
+class BackendUseStats:
+    backend: str
+    calls: int = 0
+
+
+def _block_d_tune_args(head_dim: int) -> FlashAttenTuneArguments:
+    """The reference's launch presets (ttft.py:145-166); validated, the sm_100a table picks the tile."""
+    if head_dim == 256:
+        return FlashAttenTuneArguments(BLOCK_N=64, BLOCK_M=128, BLOCK_N_PAD=64, BLOCK_DMODEL=32,
+                                       BLOCK_DMODEL_OUTER=256, NUM_WARPS=8, NUM_STAGES=4)
+    if head_dim == 128:
+        return FlashAttenTuneArguments(BLOCK_N=64, BLOCK_M=128, BLOCK_N_PAD=64, BLOCK_DMODEL=128,
+                                       BLOCK_DMODEL_OUTER=64, NUM_WARPS=8, NUM_STAGES=3)
+    raise ValueError(f"block-D nomask benchmark only has known launch settings for head_dim 128 or 256, got {head_dim}")
+
+
+def _run_block_d_nomask_vanilla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None) -> torch.Tensor:
+    """The reference's sliced-kernel SDPA path with its argument checks (ttft.py:169-196)."""
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("custom SDPA expects q, k, v with shape [batch, heads, seq, head_dim]")
+    if q.dtype != torch.float16 or k.dtype != torch.float16 or v.dtype != torch.float16:
+        raise ValueError("custom SDPA only supports float16 tensors")
+    if q.device.type != "cuda" or k.device.type != "cuda" or v.device.type != "cuda":
+        raise ValueError("custom SDPA only supports CUDA tensors")
+    if q.shape[0] != 1:
+        raise ValueError("custom SDPA benchmark expects batch size 1")
+    if q.shape[1] != k.shape[1] or q.shape[1] != v.shape[1]:
+        raise ValueError("vanilla block-D attention expects q, k, and v to have the same number of heads")
+    if q.shape[-1] != k.shape[-1] or q.shape[-1] != v.shape[-1]:
+        raise ValueError("q, k, and v must have the same head_dim")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    spec = FlashAttentionBlockDNomaskTuner(
+        tuple(q.shape), tuple(k.shape), tuple(v.shape), q.element_size(), causal=False, return_lse=False,
+        tune_args=_block_d_tune_args(q.shape[-1]),
+    ).build_flash_attention_launch_spec(q, k, v, sm_scale=scale)
+    return flash_attention(spec)
+
+
+def _raise_unsupported_triton(reason: str):
+    raise RuntimeError(f"triton_block_d_nomask unsupported SDPA call: {reason}")
+
+
+def _repeat_kv_for_gqa(k_or_v: torch.Tensor, query_heads: int) -> torch.Tensor:
+    kv_heads = k_or_v.shape[1]
+    if kv_heads == query_heads:
+        return k_or_v
+    if query_heads % kv_heads != 0:
+        raise ValueError(f"query_heads={query_heads} is not divisible by kv_heads={kv_heads}")
+    return k_or_v.repeat_interleave(query_heads // kv_heads, dim=1)
+
+
+def _run_block_d_nomask_sdpa(q, k, v, scale):
+    k = _repeat_kv_for_gqa(k, q.shape[1])
+    v = _repeat_kv_for_gqa(v, q.shape[1])
+    return _run_block_d_nomask_vanilla(q, k, v, scale)
+
+
+def _run_triton_gqa_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None,
+                         causal: bool = False) -> torch.Tensor:
+    """SDPA on the sm_100a kernel: any batch, grouped-query heads in-kernel, strided views read in place."""
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("custom SDPA expects q, k, v with shape [batch, heads, seq, head_dim]")
+    if k.shape[1] != v.shape[1] or q.shape[1] % k.shape[1]:
+        raise ValueError(f"query_heads={q.shape[1]} is not divisible by kv_heads={k.shape[1]}")
+    return attention_forward(q, k, v, causal=causal, sm_scale=scale)
+
+
+def _run_efficient_gqa_expanded_sdpa(q, k, v, sdpa_fn, *, attn_mask, dropout_p, is_causal, scale):
+    if attn_mask is not None:
+        raise RuntimeError("efficient_gqa_expanded unsupported SDPA call: attn_mask is not None")
+    if dropout_p != 0.0:
+        raise RuntimeError(f"efficient_gqa_expanded unsupported SDPA call: dropout_p={dropout_p}")
+    q = q.contiguous()
+    k = _repeat_kv_for_gqa(k, q.shape[1]).contiguous()
+    v = _repeat_kv_for_gqa(v, q.shape[1]).contiguous()
+    with torch_sdpa_backend("efficient"):
+        return sdpa_fn(q, k, v, is_causal=is_causal, dropout_p=0.0, scale=scale)
+
+
+@contextlib.contextmanager
+def force_noncausal_attention(model) -> Iterator[None]:
+    patched = []
+    for module in model.modules():
+        if hasattr(module, "is_causal"):
+            patched.append((module, module.is_causal))
+            module.is_causal = False
+    try:
+        yield
+    finally:
+        for module, old in patched:
+            module.is_causal = old
+
+
+@contextlib.contextmanager
+def patched_sdpa_with_efficient_gqa_expanded(*, stats: BackendUseStats | None = None) -> Iterator[None]:
+    original = F.scaled_dot_product_attention
+
+    def replacement(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
+        if stats is not None:
+            stats.calls += 1
+        return _run_efficient_gqa_expanded_sdpa(query, key, value, original, attn_mask=attn_mask, dropout_p=dropout_p,
+                                                is_causal=is_causal, scale=scale)
+
+    F.scaled_dot_product_attention = replacement
+    try:
+        yield
+    finally:
+        F.scaled_dot_product_attention = original
+
+
+@contextlib.contextmanager
+def patched_sdpa_with_triton_gqa(*, allow_causal: bool, stats: BackendUseStats | None = None) -> Iterator[None]:
+    """Route F.scaled_dot_product_attention to the sm_100a kernel (same checks as ttft.py:299-327)."""
+    original = F.scaled_dot_product_attention
+
+    def replacement(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
+        if dropout_p != 0.0:
+            _raise_unsupported_triton(f"dropout_p={dropout_p}")
+        if attn_mask is not None:
+            _raise_unsupported_triton("attn_mask is not None")
+        if is_causal and not allow_causal:
+            _raise_unsupported_triton("is_causal=True")
+        if stats is not None:
+            stats.calls += 1
+        return _run_triton_gqa_sdpa(query, key, value, scale, causal=bool(is_causal))
+
+    F.scaled_dot_product_attention = replacement
+    try:
+        yield
+    finally:
+        F.scaled_dot_product_attention = original
+
+
+@contextlib.contextmanager
+def torch_sdpa_backend(name: str) -> Iterator[None]:
+    if sdpa_kernel is None or SDPBackend is None:
+        raise RuntimeError("This PyTorch build does not expose torch.nn.attention.sdpa_kernel.")
+    backend = {
+        "math": SDPBackend.MATH,
+        "efficient": SDPBackend.EFFICIENT_ATTENTION,
+        "flash": SDPBackend.FLASH_ATTENTION,
+        "cudnn": SDPBackend.CUDNN_ATTENTION,
+    }[name]
+    with warnings.catch_warnings():
+        warnings.filterwarnings("error", message=".*kernel not used because.*")
+        warnings.filterwarnings("error", message=".*No available kernel.*")
+        warnings.filterwarnings("error", message=".*both fused kernels require query, key and value to have the same num_heads.*")
+        warnings.filterwarnings("error", message=".*has been runtime disabled.*")
+        with sdpa_kernel(backends=[backend]):
+            yield
+
+
+@contextlib.contextmanager
+def patched_sdpa_enable_gqa(*, stats: BackendUseStats | None = None) -> Iterator[None]:
+    original = F.scaled_dot_product_attention
+
+    def replacement(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None, enable_gqa=False):
+        if (not enable_gqa and query.ndim >= 3 and key.ndim >= 3 and value.ndim >= 3
+                and query.shape[-3] != key.shape[-3] and key.shape[-3] == value.shape[-3]
+                and query.shape[-3] % key.shape[-3] == 0):
+            enable_gqa = True
+        if stats is not None:
+            stats.calls += 1
+        return original(query, key, value, attn_mask, dropout_p, is_causal, scale=scale, enable_gqa=enable_gqa)
+
+    F.scaled_dot_product_attention = replacement
+    try:
+        yield
+    finally:
+        F.scaled_dot_product_attention = original
+
+
+@contextlib.contextmanager
+def backend_context(name: str, *, allow_causal_custom: bool, stats: BackendUseStats | None = None) -> Iterator[None]:
+    if name in {"math", "efficient", "flash", "cudnn"}:
+        with torch_sdpa_backend(name):
+            with patched_sdpa_enable_gqa(stats=stats):
+                yield
+        return
+    if name in {"triton_block_d_nomask", "triton_gqa", "native"}:
+        with patched_sdpa_with_triton_gqa(allow_causal=allow_causal_custom, stats=stats):
+            yield
+        return
+    if name == "efficient_gqa_expanded":
+        with patched_sdpa_with_efficient_gqa_expanded(stats=stats):
+            yield
+        return
+    raise ValueError(f"unknown backend {name}")
+
+
+# ------------------------------------------------------- tensor parallelism
+def head_partition(num_heads: int, world: int, rank: int) -> range:
+    """Contiguous query heads of `rank`: sizes differ by at most one (28 over 8 -> 4,4,4,4,3,3,3,3)."""
+    base, extra = divmod(num_heads, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def column_partition(size: int, world: int, rank: int) -> range:
+    return head_partition(size, world, rank)
+
+
+@dataclass(frozen=True)
+class RankPlan:
+    """What one tensor-parallel rank owns in every layer."""
+
+    q_heads: range
+    kv_heads: tuple[int, ...]            # key/value heads this rank computes
+    segments: tuple[tuple[int, int, int], ...]  # (first local q head, count, local kv index)
+    mlp_cols: range
+
+
+def rank_plan(arch: ArchConfig, world: int, rank: int) -> RankPlan:
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    if world > arch.num_attention_heads:
+        raise ValueError("more ranks than query heads")
+    group = arch.num_attention_heads // arch.num_key_value_heads
+    q_heads = head_partition(arch.num_attention_heads, world, rank)
+    kv_needed: list[int] = []
+    segments: list[tuple[int, int, int]] = []
+    for local, h in enumerate(q_heads):
+        kv = h // group
+        if not kv_needed or kv_needed[-1] != kv:
+            kv_needed.append(kv)
+            segments.append((local, 1, len(kv_needed) - 1))
+        else:
+            first, count, idx = segments[-1]
+            segments[-1] = (first, count + 1, idx)
+    return RankPlan(q_heads, tuple(kv_needed), tuple(segments),
+                    column_partition(arch.intermediate_size, world, rank))
+
+
+def _seeded_normal(shape, seed: int, device, std: float = 0.02, dtype=DTYPE) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(dtype)
+
+
+@dataclass
+class LayerShard:
+    ln_in: torch.Tensor
+    w_qkv: torch.Tensor          # [hidden, (nq + 2*nkv) * head_dim]
+    b_qkv: torch.Tensor | None   # [(nq + 2*nkv) * head_dim]
+    w_o: torch.Tensor            # [nq * head_dim, hidden]
+    ln_post: torch.Tensor
+    w_gate_up: torch.Tensor      # [hidden, 2 * mlp_local]
+    w_down: torch.Tensor         # [mlp_local, hidden]
+
+
+@dataclass
+class ModelShard:
+    arch: ArchConfig
+    plan: RankPlan
+    embed: torch.Tensor          # [vocab, hidden] (replicated)
+    layers: list[LayerShard]
+    ln_final: torch.Tensor
+    lm_head: torch.Tensor        # [hidden, vocab] (replicated)
+    num_layers: int = field(default=0)
+
+
+def full_weights_layer(arch: ArchConfig, layer: int, seed: int, device) -> dict[str, torch.Tensor]:
+    """The full (unsharded) weights of one layer, identical for every tensor-parallel degree.
+
+    Linear weights are stored [in, out] (row-major B operand of x @ W)."""
+    H, D = arch.hidden_size, arch.head_dim
+    nq, nkv, inter = arch.num_attention_heads, arch.num_key_value_heads, arch.intermediate_size
+    base = seed * 1_000_003 + layer * 101
+    w = {
+        "q": _seeded_normal((H, nq * D), base + 1, device),
+        "k": _seeded_normal((H, nkv * D), base + 2, device),
+        "v": _seeded_normal((H, nkv * D), base + 3, device),
+        "o": _seeded_normal((nq * D, H), base + 4, device),
+        "gate": _seeded_normal((H, inter), base + 5, device),
+        "up": _seeded_normal((H, inter), base + 6, device),
+        "down": _seeded_normal((inter, H), base + 7, device),
+        "ln_in": torch.ones(H, device=device, dtype=DTYPE),
+        "ln_post": torch.ones(H, device=device, dtype=DTYPE),
+    }
+    if arch.qkv_bias:
+        w["bq"] = _seeded_normal((nq * D,), base + 8, device)
+        w["bk"] = _seeded_normal((nkv * D,), base + 9, device)
+        w["bv"] = _seeded_normal((nkv * D,), base + 10, device)
+    return w
+
+
+def shard_layer(arch: ArchConfig, plan: RankPlan, w: dict[str, torch.Tensor]) -> LayerShard:
+    D = arch.head_dim
+    qcols = slice(plan.q_heads.start * D, plan.q_heads.stop * D)
+    kv_cols = [slice(h * D, (h + 1) * D) for h in plan.kv_heads]
+    w_qkv = torch.cat([w["q"][:, qcols]] + [w["k"][:, c] for c in kv_cols] + [w["v"][:, c] for c in kv_cols], dim=1)
+    b_qkv = None
+    if "bq" in w:
+        b_qkv = torch.cat([w["bq"][qcols]] + [w["bk"][c] for c in kv_cols] + [w["bv"][c] for c in kv_cols])
+    m = slice(plan.mlp_cols.start, plan.mlp_cols.stop)
+    return LayerShard(
+        ln_in=w["ln_in"],
+        w_qkv=w_qkv.contiguous(),
+        b_qkv=b_qkv,
+        w_o=w["o"][qcols].contiguous(),
+        ln_post=w["ln_post"],
+        w_gate_up=torch.cat([w["gate"][:, m], w["up"][:, m]], dim=1).contiguous(),
+        w_down=w["down"][m].contiguous(),
+    )
+
+
+def build_model_shard(arch: ArchConfig, world: int, rank: int, *, seed: int = 0, device=DEVICE,
+                      num_layers: int | None = None) -> ModelShard:
+    plan = rank_plan(arch, world, rank)
+    L = arch.num_hidden_layers if num_layers is None else num_layers
+    layers = []
+    for layer in range(L):
+        full = full_weights_layer(arch, layer, seed, device)
+        layers.append(shard_layer(arch, plan, full))
+        del full
+    embed = _seeded_normal((arch.vocab_size, arch.hidden_size), seed * 1_000_003 + 7_777_777, device)
+    lm_head = _seeded_normal((arch.hidden_size, arch.vocab_size), seed * 1_000_003 + 8_888_888, device)
+    return ModelShard(arch, plan, embed, layers, torch.ones(arch.hidden_size, device=device, dtype=DTYPE), lm_head, L)
+
+
+def rope_tables(arch: ArchConfig, seq_len: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [S, head_dim] of the rotate-half rotary embedding (Qwen2 / Llama form)."""
+    D = arch.head_dim
+    inv = 1.0 / (arch.rope_theta ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+    t = torch.arange(seq_len, device=device, dtype=torch.float32)
+    freqs = torch.outer(t, inv)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(DTYPE), emb.sin().to(DTYPE)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat([-x[..., h:], x[..., :h]], dim=-1)
+
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * xf.to(x.dtype)
+
+
+@dataclass
+class Backends:
+    """How the decoder runs its attention and its matmuls."""
+
+    attention: str = "native"       # "native" (this repository's kernel) or a torch SDPA backend name
+    gemm: str = "native"            # "native" (this repository's GEMM) or "cublas"
+
+
+def _matmul(a: torch.Tensor, b: torch.Tensor, how: str) -> torch.Tensor:
+    if how == "native":
+        from mma import matmul
+
+        return matmul(a, b)
+    if how == "cublas":
+        return a @ b
+    raise ValueError(f"unknown gemm backend {how!r}")
+
+
+def _attention_segments(q, k, v, out, plan: RankPlan, how: str) -> None:
+    """q/out [1, nq, S, D], k/v [1, nkv_local, S, D] (strided views); causal; one call per key/value head.
+
+    For torch backends the caller holds the `torch_sdpa_backend` context."""
+    for first, count, kv in plan.segments:
+        qs = q[:, first:first + count]
+        ks = k[:, kv:kv + 1]
+        vs = v[:, kv:kv + 1]
+        os_ = out[:, first:first + count]
+        if how == "native":
+            attention_forward(qs, ks, vs, causal=True, out=os_)
+        else:
+            os_.copy_(F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, enable_gqa=count > 1))
+
+
+def _all_reduce(x: torch.Tensor, group=None) -> None:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(x, group=group)
+
+
+def decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backends, *, group=None) -> torch.Tensor:
+    """Last-position logits [1, vocab] (fp32) of a prefill over input_ids [1, S]."""
+    ctx = contextlib.nullcontext() if backends.attention == "native" else torch_sdpa_backend(backends.attention)
+    with ctx:
+        return _decoder_forward(model, input_ids, backends, group)
+
+
+def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backends, group) -> torch.Tensor:
+    arch, plan = model.arch, model.plan
+    S = input_ids.shape[1]
+    D = arch.head_dim
+    nq = len(plan.q_heads)
+    nkv = len(plan.kv_heads)
+    cos, sin = rope_tables(arch, S, input_ids.device)
+    cos, sin = cos[:, None, :], sin[:, None, :]
+    x = model.embed[input_ids[0]]                                  # [S, hidden]
+    attn_out = torch.empty(S, nq, D, device=x.device, dtype=x.dtype)
+    for layer in model.layers:
+        h = _rms_norm(x, layer.ln_in, arch.rms_norm_eps)
+        qkv = _matmul(h, layer.w_qkv, backends.gemm)
+        if layer.b_qkv is not None:
+            qkv += layer.b_qkv
+        q = qkv[:, : nq * D].view(S, nq, D)
+        k = qkv[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
+        v = qkv[:, (nq + nkv) * D:].view(S, nkv, D)
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        # [S, H, D] storage seen as [1, H, S, D]: the kernel reads and writes these strided views in place.
+        _attention_segments(q.unsqueeze(0).transpose(1, 2), k.unsqueeze(0).transpose(1, 2),
+                            v.unsqueeze(0).transpose(1, 2), attn_out.unsqueeze(0).transpose(1, 2), plan,
+                            backends.attention)
+        o = _matmul(attn_out.view(S, nq * D), layer.w_o, backends.gemm)
+        _all_reduce(o, group)
+        x = x + o
+        h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
+        gu = _matmul(h, layer.w_gate_up, backends.gemm)
+        m = gu.shape[1] // 2
+        a = F.silu(gu[:, :m]) * gu[:, m:]
+        d = _matmul(a, layer.w_down, backends.gemm)
+        _all_reduce(d, group)
+        x = x + d
+    last = _rms_norm(x[-1:], model.ln_final, arch.rms_norm_eps)
+    return (last @ model.lm_head).float()
+
+
+def first_token(model: ModelShard, input_ids: torch.Tensor, backends: Backends, *, group=None) -> torch.Tensor:
+    return decoder_forward(model, input_ids, backends, group=group).argmax(dim=-1)
+
+
+def time_decoder_ttft_ms(model: ModelShard, input_ids: torch.Tensor, backends: Backends, *, repeats: int,
+                         warmups: int, group=None) -> tuple[float, ...]:
+    """Wall-clock TTFT per prefill, synchronised on both sides (as ttft.py:461-478); max over ranks."""
+    import torch.distributed as dist
+
+    samples = []
+    with torch.inference_mode():
+        for i in range(warmups + repeats):
+            if dist.is_available() and dist.is_initialized():
+                dist.barrier(group=group)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            tok = first_token(model, input_ids, backends, group=group)
+            torch.cuda.synchronize()
+            ms = (time.perf_counter() - t0) * 1e3
+            if dist.is_available() and dist.is_initialized():
+                t = torch.tensor([ms], device=input_ids.device, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+                ms = float(t.item())
+            del tok
+            if i >= warmups:
+                samples.append(ms)
+    return tuple(samples)
+
+
+# ----------------------------------------------- HF model path (reference form)
+def load_model(model_id: str | ArchConfig, *, num_layers: int | None = None, seed: int = 0, device=DEVICE):
+    """An HF Qwen2ForCausalLM with the architecture of `model_id`, random N(0, 0.02) bf16 weights.
+
+    Replaces `from_pretrained` (ttft.py:483-491): no checkpoint can be downloaded here."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    arch = model_id if isinstance(model_id, ArchConfig) else KNOWN_ARCHS[model_id]
+    cfg = Qwen2Config(
+        vocab_size=arch.vocab_size, hidden_size=arch.hidden_size, intermediate_size=arch.intermediate_size,
+        num_hidden_layers=num_layers or arch.num_hidden_layers, num_attention_heads=arch.num_attention_heads,
+        num_key_value_heads=arch.num_key_value_heads, head_dim=arch.head_dim, rms_norm_eps=arch.rms_norm_eps,
+        rope_theta=arch.rope_theta, max_position_embeddings=131072, tie_word_embeddings=False,
+        attn_implementation="sdpa", initializer_range=0.02,
+    )
+    torch.manual_seed(seed)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(DTYPE)
+    try:
+        with torch.device(device):
+            model = Qwen2ForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    return model.to(device=device, dtype=DTYPE).eval()
+
+
+def load_hf_weights_into_shard(hf_model, arch: ArchConfig, world: int = 1, rank: int = 0) -> ModelShard:
+    """Our decoder with exactly an HF model's weights (to check the decoder against HF)."""
+    plan = rank_plan(arch, world, rank)
+    layers = []
+    for layer in hf_model.model.layers:
+        at, mlp = layer.self_attn, layer.mlp
+        w = {
+            "q": at.q_proj.weight.T, "k": at.k_proj.weight.T, "v": at.v_proj.weight.T, "o": at.o_proj.weight.T,
+            "gate": mlp.gate_proj.weight.T, "up": mlp.up_proj.weight.T, "down": mlp.down_proj.weight.T,
+            "ln_in": layer.input_layernorm.weight, "ln_post": layer.post_attention_layernorm.weight,
+        }
+        if at.q_proj.bias is not None:
+            w.update(bq=at.q_proj.bias, bk=at.k_proj.bias, bv=at.v_proj.bias)
+        layers.append(shard_layer(arch, plan, w))
+    return ModelShard(arch, plan, hf_model.model.embed_tokens.weight, layers, hf_model.model.norm.weight,
+                      hf_model.lm_head.weight.T.contiguous(), len(layers))
+
+
+def _forward_final_logits(model, input_ids: torch.Tensor) -> torch.Tensor:
+    outputs = model(input_ids=input_ids, attention_mask=None, use_cache=True, logits_to_keep=1)
+    return outputs.logits[:, -1, :]
+
+
+def _forward_first_token(model, input_ids: torch.Tensor):
+    return _forward_final_logits(model, input_ids).argmax(dim=-1)
+
+
+def verify_against_flash(model, input_ids, *, backend: str, allow_causal_custom: bool, force_noncausal: bool,
+                         reference_backend: str = "flash") -> str:
+    """Final-token logits of `backend` against torch's flash SDPA on the same HF model (ttft.py:415-446)."""
+    if backend == reference_backend:
+        return "skipped"
+    causal_ctx = force_noncausal_attention(model) if force_noncausal else contextlib.nullcontext()
+    with torch.inference_mode():
+        with causal_ctx:
+            custom_stats = BackendUseStats(backend)
+            ref_stats = BackendUseStats(reference_backend)
+            with backend_context(backend, allow_causal_custom=allow_causal_custom, stats=custom_stats):
+                custom = _forward_final_logits(model, input_ids).detach().float()
+            with backend_context(reference_backend, allow_causal_custom=allow_causal_custom, stats=ref_stats):
+                ref = _forward_final_logits(model, input_ids).detach().float()
+    if custom_stats.calls <= 0:
+        raise RuntimeError(f"{backend} verification did not intercept any SDPA calls")
+    if ref_stats.calls <= 0:
+        raise RuntimeError(f"{reference_backend} verification did not intercept any SDPA calls")
+    max_abs = (custom - ref).abs().max().item()
+    max_rel = ((custom - ref).abs() / ref.abs().clamp_min(1.0e-6)).max().item()
+    token_match = bool(custom.argmax(dim=-1).eq(ref.argmax(dim=-1)).all().item())
+    close = torch.allclose(custom, ref, rtol=1.0e-1, atol=1.0e-1)
+    summary = f"close={close} next_token_match={token_match} max_abs={max_abs:.6f} max_rel={max_rel:.6f}"
+    if not close:
+        raise AssertionError(f"{backend} output differs from torch {reference_backend} reference: {summary}")
+    return f"{summary} backend_sdpa_calls={custom_stats.calls} {reference_backend}_sdpa_calls={ref_stats.calls}"
+
+
+def time_ttft_ms(model, input_ids, *, backend: str, repeats: int, warmups: int, allow_causal_custom: bool,
+                 force_noncausal: bool) -> tuple[float, ...]:
+    """TTFT of an HF model under an SDPA backend (ttft.py:449-480)."""
+    samples = []
+    total_calls = 0
+    with torch.inference_mode():
+        for idx in range(warmups + repeats):
+            torch.cuda.empty_cache()
+            torch.cuda.synchronize()
+            start = time.perf_counter()
+            causal_ctx = force_noncausal_attention(model) if force_noncausal else contextlib.nullcontext()
+            stats = BackendUseStats(backend)
+            with causal_ctx:
+                with backend_context(backend, allow_causal_custom=allow_causal_custom, stats=stats):
+                    out = _forward_first_token(model, input_ids)
+            torch.cuda.synchronize()
+            if stats.calls <= 0:
+                raise RuntimeError(f"{backend} did not intercept any SDPA calls")
+            total_calls += stats.calls
+            elapsed = (time.perf_counter() - start) * 1000.0
+            del out
+            if idx >= warmups:
+                samples.append(elapsed)
+    time_ttft_ms.last_sdpa_calls = total_calls
+    return tuple(samples)
+
+
+def plot_ttft_results(results: list[BenchResult]):
+    """Chart output is out of scope here (no matplotlib in this image); results are printed instead."""
+    print("[plot] skipped: charts are not produced by this build")
+    return []
+
+
+def run(args: argparse.Namespace) -> list[BenchResult]:
+    """The reference's HF TTFT sweep (ttft.py:552-636) on random-init models of the named architectures."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is required for TTFT benchmarking.")
+    torch.backends.cuda.matmul.allow_tf32 = True
+    print(f"[device] {torch.cuda.get_device_name()} dtype={DTYPE}")
+    results: list[BenchResult] = []
+    for model_id in args.models:
+        shape = inspect_model_shape(model_id)
+        model = load_model(model_id)
+        for prompt_len in args.lengths:
+            input_ids = _make_random_input_ids(prompt_len, shape.vocab_size, torch.device(DEVICE))
+            for backend in args.backends:
+                try:
+                    if args.verify_flash and backend not in ("flash", "cudnn"):
+                        v = verify_against_flash(model, input_ids, backend=backend,
+                                                 allow_causal_custom=args.allow_causal_custom,
+                                                 force_noncausal=args.force_noncausal)
+                        print(f"[verify] model={model_id} prompt_len={prompt_len} backend={backend} reference=flash {v}")
+                    samples = time_ttft_ms(model, input_ids, backend=backend, repeats=args.repeats,
+                                           warmups=args.warmups, allow_causal_custom=args.allow_causal_custom,
+                                           force_noncausal=args.force_noncausal)
+                    mean, p50 = statistics.mean(samples), statistics.median(samples)
+                    print(f"[result] model={model_id} prompt_len={prompt_len} backend={backend} mean={mean:.3f}ms "
+                          f"p50={p50:.3f}ms sdpa_calls={getattr(time_ttft_ms, 'last_sdpa_calls', 'n/a')} "
+                          f"samples={','.join(f'{x:.3f}' for x in samples)}")
+                    results.append(BenchResult(model_id, prompt_len, backend, mean, p50, samples, "ok"))
+                except Exception as exc:
+                    print(f"[result] model={model_id} prompt_len={prompt_len} backend={backend} status=failed error={exc}")
+                    results.append(BenchResult(model_id, prompt_len, backend, None, None, (), f"failed: {exc}"))
+                finally:
+                    gc.collect()
+                    torch.cuda.empty_cache()
+        del model
+        gc.collect()
+        torch.cuda.empty_cache()
+    if args.plot:
+        plot_ttft_results(results)
+    return results
+
+
+def parse_args(argv=None) -> argparse.Namespace:
+    parser = argparse.ArgumentParser(description="Benchmark HF-architecture TTFT across SDPA backends.")
+    parser.add_argument("--models", nargs="+", default=list(DEFAULT_MODELS))
+    parser.add_argument("--lengths", nargs="+", type=int, default=list(DEFAULT_PROMPT_LENGTHS))
+    parser.add_argument("--backends", nargs="+", default=["triton_gqa", "cudnn", "flash"])
+    parser.add_argument("--repeats", type=int, default=3)
+    parser.add_argument("--warmups", type=int, default=1)
+    parser.add_argument("--memory-fraction", type=float, default=0.88)
+    parser.add_argument("--force-noncausal", action=argparse.BooleanOptionalAction, default=False,
+                        help="Set HF attention modules to non-causal during the runs (the reference's default).")
+    parser.add_argument("--allow-causal-custom", action=argparse.BooleanOptionalAction, default=True,
+                        help="Let causal SDPA calls through to the custom kernel (which computes causal attention).")
+    parser.add_argument("--verify-flash", action=argparse.BooleanOptionalAction, default=True)
+    parser.add_argument("--plot", action=argparse.BooleanOptionalAction, default=False)
+    return parser.parse_args(argv)
+
+
+if __name__ == "__main__":
+    run(parse_args())
