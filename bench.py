@@ -83,7 +83,8 @@ def committed_traffic(workload: str):
     if not path.is_file():
         return None
     try:
-        return json.loads(path.read_text()).get(workload)
+        value = json.loads(path.read_text()).get(workload)
+        return int(value) if isinstance(value, (int, float)) else None
     except Exception:
         return None
 
