@@ -304,24 +304,44 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     }
     for (int j = 0; ok && j < nt; ++j) {
       const int s = j % kStages;
-      if (!(ok = mbar_wait(bar_v_full + s, (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
       const int jn = j + kSB;  // the KV tile whose S product reuses this S buffer
       const int sn = jn % kStages;
-      for (int i = 0; i < kNQ; ++i) {
-        const int slot = i * kSB + (j % kSB);
+      if (!(ok = mbar_wait(bar_v_full + s, (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+      if constexpr (kSB == 1) {
+        // Two Q tiles.  Each MMA burst is followed by a stall of a few hundred
+        // cycles before the issuing thread's next instruction, so P_i*V(j)
+        // and S_i(j+1) go out back to back: K(j+1) (loaded an iteration ago)
+        // is waited for up front and the K/V release commits come last.
+        if (jn < nt && !(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+        for (int i = 0; i < kNQ; ++i) {
+          const int slot = i;
+          if (!(ok = mbar_wait(bar_p_full + slot, j & 1, abort_flag, kDevTimeoutP))) break;
+          tc_fence_after();
+          issue_pv(i, slot, s, j > 0);
+          if (jn < nt) issue_qk(i, slot, sn);
+          if (j == nt - 1) mma_commit(bar_o_done + i);  // nobody reads O before the end
+          if (jn < nt) mma_commit(bar_s_full + slot);
+        }
+        if (!ok) break;
+        mma_commit(bar_v_empty + s);
+        if (jn < nt) mma_commit(bar_k_empty + sn);
+      } else {
+        // One Q tile, two S buffers.  The softmax of tile j+1 waits for
+        // P*V(j) before it may rescale O, and the producer's next V and K
+        // loads wait for V(j)'s stage: release both right after P*V(j);
+        // K(j+2) is issued only after V(j+1), so wait for it afterwards.
+        const int slot = j % kSB;
         if (!(ok = mbar_wait(bar_p_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutP))) break;
         tc_fence_after();
-        issue_pv(i, slot, s, j > 0);
-        // With one S buffer nobody needs O before the end; with two, the
-        // softmax may rescale O while this product is still in flight.
-        if (kSB == 2 || j == nt - 1) mma_commit(bar_o_done + i);
-        if (i == kNQ - 1) mma_commit(bar_v_empty + s);
+        issue_pv(0, slot, s, j > 0);
+        mma_commit(bar_o_done);
+        mma_commit(bar_v_empty + s);
         if (jn < nt) {
-          if (i == 0 && !(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+          if (!(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
           tc_fence_after();
-          issue_qk(i, slot, sn);
+          issue_qk(0, slot, sn);
           mma_commit(bar_s_full + slot);
-          if (i == kNQ - 1) mma_commit(bar_k_empty + sn);
+          mma_commit(bar_k_empty + sn);
         }
       }
     }
