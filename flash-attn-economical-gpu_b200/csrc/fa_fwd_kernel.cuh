@@ -70,7 +70,6 @@ struct FaCfg {
   static constexpr int kDataBytes = kNQ * kQTileBytes + 2 * kStages * kKVTileBytes;
   static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
-  static_assert(kSB == 1 || kNQ == 1, "two S buffers only with one Q tile");
   static_assert(kTmemUsed <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   __host__ __device__ static constexpr int tmem_s(int slot) { return slot * kBN; }
@@ -326,21 +325,29 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         mma_commit(bar_v_empty + s);
         if (jn < nt) mma_commit(bar_k_empty + sn);
       } else {
-        // One Q tile, two S buffers.  The softmax of tile j+1 waits for
-        // P*V(j) before it may rescale O, and the producer's next V and K
-        // loads wait for V(j)'s stage: release both right after P*V(j);
-        // K(j+2) is issued only after V(j+1), so wait for it afterwards.
-        const int slot = j % kSB;
-        if (!(ok = mbar_wait(bar_p_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutP))) break;
-        tc_fence_after();
-        issue_pv(0, slot, s, j > 0);
-        mma_commit(bar_o_done);
+        // Two S buffers per Q tile: S_i(j+1) is already in TMEM while the
+        // softmax works on tile j.  The softmax of tile j+1 waits for
+        // P_i*V(j) before it may rescale O, and the producer's next V and K
+        // loads wait for V(j)'s stage: release both right after the P*V
+        // products; K(j+2) is issued only after V(j+1), so wait for it
+        // afterwards.
+        for (int i = 0; i < kNQ; ++i) {
+          const int slot = i * kSB + j % kSB;
+          if (!(ok = mbar_wait(bar_p_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutP))) break;
+          tc_fence_after();
+          issue_pv(i, slot, s, j > 0);
+          mma_commit(bar_o_done + i);
+        }
+        if (!ok) break;
         mma_commit(bar_v_empty + s);
         if (jn < nt) {
           if (!(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
           tc_fence_after();
-          issue_qk(0, slot, sn);
-          mma_commit(bar_s_full + slot);
+          for (int i = 0; i < kNQ; ++i) {
+            const int slot = i * kSB + j % kSB;
+            issue_qk(i, slot, sn);
+            mma_commit(bar_s_full + slot);
+          }
           mma_commit(bar_k_empty + sn);
         }
       }
@@ -388,17 +395,20 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         for (int e = 0; e < kBN; ++e)
           if (col0 + e >= lim) s[e] = kNegInf;
       }
-      // Row max: eight independent three-input max chains.
+      // Row max: eight independent chains seeded with columns 0-7, then
+      // three-input max over 16 columns per step, then a last 8 if left.
       float mxv[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) mxv[a] = s[a];
+      constexpr int kSteps16 = (kBN - 8) / 16;
 #pragma unroll
-      for (int e = 8; e + 16 <= kBN; e += 16)
+      for (int t = 0; t < kSteps16; ++t)
 #pragma unroll
-        for (int a = 0; a < 8; ++a) mxv[a] = fmax3(mxv[a], s[e + a], s[e + 8 + a]);
-      if constexpr (kBN % 16 == 8)
+        for (int a = 0; a < 8; ++a) mxv[a] = fmax3(mxv[a], s[8 + 16 * t + a], s[16 + 16 * t + a]);
+      static_assert(kBN % 8 == 0, "BLOCK_N is a multiple of 8");
+      if constexpr (8 + 16 * kSteps16 < kBN)
 #pragma unroll
-        for (int a = 0; a < 8; ++a) mxv[a] = fmaxf(mxv[a], s[kBN - 8 + a]);
+        for (int a = 0; a < 8; ++a) mxv[a] = fmaxf(mxv[a], s[8 + 16 * kSteps16 + a]);
       const float mx = fmax3(fmax3(mxv[0], mxv[1], mxv[2]), fmax3(mxv[3], mxv[4], mxv[5]), fmaxf(mxv[6], mxv[7]));
       const float m_cand = fmaxf(m_run, mx * c);
       const bool rescale = m_cand > m_run + 8.0f;

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import json
 import zlib
+from math import log as math_log
 from pathlib import Path
 
 import numpy as np
@@ -205,6 +206,44 @@ def test_scale_variants(scale, cuda_device):
     o = attention_forward(qd, kd, vd, causal=True, sm_scale=scale)
     ro, _ = _oracle(q, k, v, True, torch.bfloat16, sm_scale=scale)
     _close(o, ro)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_dominant_key_at_every_tile_column(D, cuda_device):
+    """One key per head scores so far above the rest that exp of it overflows fp32 unless the row maximum
+    saw it; the heads place it at the first, middle and last columns of the first and second key tiles."""
+    positions = [0, 7, 63, 64, 119, 120, 127, 128, 191, 248, 255]
+    H, M, N = len(positions), 128, 256
+    g = torch.Generator().manual_seed(21)
+    q = torch.full((1, H, M, D), 4.0).to(torch.bfloat16)
+    k = (0.1 * torch.randn(1, H, N, D, generator=g)).to(torch.bfloat16)
+    v = torch.randn(1, H, N, D, generator=g).to(torch.bfloat16)
+    for h, pos in enumerate(positions):
+        k[0, h, pos] = 8.0
+    o = attention_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    ro, _ = _oracle(q, k, v, False, torch.bfloat16)
+    assert torch.isfinite(o.float()).all()
+    _close(o, ro)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_row_max_rising_every_key_tile(D, causal, cuda_device):
+    """Scores grow by about 2^9 from one 64-key block to the next, so the running max moves on every KV
+    tile and the kernel takes its rescale path each time."""
+    M, N = 256, 1024
+    g = torch.Generator().manual_seed(22)
+    q = (1.0 + 0.05 * torch.randn(1, 2, M, D, generator=g)).to(torch.bfloat16)
+    step = 9.0 * math_log(2.0) / (D ** 0.5)  # log2 gain of 9 per block at scale D^-0.5
+    ramp = (torch.arange(N) // 64).float() * step
+    k = (ramp[None, None, :, None] + 0.05 * torch.randn(1, 2, N, D, generator=g)).to(torch.bfloat16)
+    v = torch.randn(1, 2, N, D, generator=g).to(torch.bfloat16)
+    o, lse = attention_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), causal=causal,
+                               return_lse=True)
+    ro, rl = _oracle(q, k, v, causal, torch.bfloat16)
+    assert torch.isfinite(o.float()).all()
+    _close(o, ro)
+    _close(lse, rl, rtol=1e-3, atol=2e-3 * max(1.0, float(np.abs(rl).max()) / 100))
 
 
 def test_empty_inputs(cuda_device):
