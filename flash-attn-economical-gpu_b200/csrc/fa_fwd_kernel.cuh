@@ -255,17 +255,28 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     constexpr uint32_t kFmt = ElemOps<T>::kFmt;
     constexpr uint32_t idesc_qk = umma_idesc(kFmt, C::kBM, kBN, 0, 0);
     constexpr uint32_t idesc_pv = umma_idesc(kFmt, C::kBM, kDP, 0, 1);
-    const uint32_t sq_addr = smem_u32(sQ);
-    const uint32_t sk_addr = smem_u32(sK);
-    const uint32_t sv_addr = smem_u32(sV);
+    // Descriptors are built from precomputed words: per MMA only the low
+    // word's address field moves (see umma_desc_lo), which keeps this
+    // thread's instruction stream short -- it shares its SM sub-partition
+    // with two softmax warps.
+    constexpr uint32_t kHiK = umma_desc_hi(1024, kLayoutSw128);
+    constexpr uint32_t kHiV = sizeof(T) == 4 ? umma_desc_hi(512, kLayoutSw128Base32B) : umma_desc_hi(1024, kLayoutSw128);
+    const uint32_t q_lo = umma_desc_lo(smem_u32(sQ), 16);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(sK), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(sV), C::kKVAtomBytes);
     auto issue_qk = [&](int i, int slot, int s) {
       const uint32_t d = tmem + C::tmem_s(slot);
+      uint32_t qa = q_lo + i * (C::kQTileBytes >> 4);
+      uint32_t kb = k_lo + s * (C::kKVTileBytes >> 4);
+      // Opaque to the optimiser, so the per-step words are formed here rather
+      // than hoisted out of the tile loop into registers this warp lacks.
+      asm volatile("" : "+r"(qa), "+r"(kb));
 #pragma unroll
       for (int kk = 0; kk < kDP / C::kKInstr; ++kk) {
         const int a = kk >> 2;
         const uint32_t off = (kk & 3) * 32;
-        const uint64_t ad = umma_desc_sw128(sq_addr + i * C::kQTileBytes + a * C::kQAtomBytes + off, 16, 1024);
-        const uint64_t bd = umma_desc_sw128(sk_addr + s * C::kKVTileBytes + a * C::kKVAtomBytes + off, 16, 1024);
+        const uint64_t ad = umma_desc_join(qa + ((a * C::kQAtomBytes + off) >> 4), kHiK);
+        const uint64_t bd = umma_desc_join(kb + ((a * C::kKVAtomBytes + off) >> 4), kHiK);
         if constexpr (sizeof(T) == 4)
           mma_ss_tf32(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         else
@@ -275,10 +286,11 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     auto issue_pv = [&](int i, int slot, int s, bool acc) {
       const uint32_t d = tmem + C::tmem_o(i);
       const uint32_t pa = tmem + C::tmem_s(slot);
+      uint32_t vb = v_lo + s * (C::kKVTileBytes >> 4);
+      asm volatile("" : "+r"(vb));
 #pragma unroll
       for (int kk = 0; kk < kBN / C::kKInstr; ++kk) {
-        const uint64_t bd = umma_desc_mn<sizeof(T)>(sv_addr + s * C::kKVTileBytes + kk * C::kKInstr * 128,
-                                                    C::kKVAtomBytes);
+        const uint64_t bd = umma_desc_join(vb + ((kk * C::kKInstr * 128) >> 4), kHiV);
         const uint32_t a_t = pa + kk * (C::kKInstr * static_cast<int>(sizeof(T)) / 4);
         const uint32_t accum = (acc || kk > 0) ? 1u : 0u;
         if constexpr (sizeof(T) == 4)

@@ -269,7 +269,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 // MN-major tf32 operand may use, with 4-row K groups).
 enum UmmaLayout : uint32_t { kLayoutSw128Base32B = 1, kLayoutSw128 = 2 };
 
-__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+__host__ __device__ constexpr uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
@@ -282,6 +282,27 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
   return umma_desc(smem_addr, lbo, sbo, kLayoutSw128);
 }
+
+// The same descriptor as two 32-bit words, for issue loops that step through
+// a buffer: the low word holds (address >> 4) and LBO, the high word SBO,
+// version and layout.  Shared-memory addresses stay below 2^18, so a byte
+// offset added to the low word as (offset >> 4) never carries out of the
+// 14-bit address field.
+__host__ __device__ constexpr uint32_t umma_desc_lo(uint32_t smem_addr, uint32_t lbo) {
+  return ((smem_addr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t umma_desc_hi(uint32_t sbo, uint32_t layout) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (layout << 29);
+}
+__host__ __device__ constexpr uint64_t umma_desc_join(uint32_t lo, uint32_t hi) {
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+static_assert(umma_desc_join(umma_desc_lo(0x2F3A0u, 16384), umma_desc_hi(512, kLayoutSw128Base32B)) ==
+                  umma_desc(0x2F3A0u, 16384, 512, kLayoutSw128Base32B),
+              "split descriptor words");
+static_assert(umma_desc_join(umma_desc_lo(0x1230u, 16) + (0x400u >> 4), umma_desc_hi(1024, kLayoutSw128)) ==
+                  umma_desc(0x1630u, 16, 1024, kLayoutSw128),
+              "offset added to the low word");
 
 // MN-major operand descriptor: 128-byte column atoms `lbo` bytes apart.  For
 // 16-bit types 8-row K groups (1024 B) with the 16-byte-chunk swizzle; for
