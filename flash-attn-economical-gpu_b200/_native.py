@@ -22,6 +22,7 @@ FAB_ERR_UNSUPPORTED = 2
 FAB_ERR_LAUNCH = 3
 FAB_ERR_DEVICE_TIMEOUT = 4
 FAB_ERR_CUDA = 5
+FAB_ERR_WORKSPACE = 6
 
 FAB_DTYPE_F16 = 0
 FAB_DTYPE_BF16 = 1
@@ -86,6 +87,9 @@ PROTOTYPES = {
     "fab_flash_attn_fwd_optimize_shared_mem": (_i32, _STRIDED_FA_ARGS),
     "fab_flash_attn_fwd_block_d_nomask_contiguous": (_i32, [_vp] * 4 + [_i32] * 5 + [_f32, _i32, _vp]),
     "fab_attention_fwd": (_i32, [ctypes.POINTER(FabAttentionParams), _vp]),
+    "fab_attention_fwd_splitkv_workspace": (
+        _i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32)]),
+    "fab_attention_fwd_splitkv": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp, ctypes.c_size_t, _vp]),
     "fab_matmul_contiguous": (_i32, [_vp] * 3 + [_i32] * 6 + [_vp]),
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),
@@ -96,7 +100,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 def _load() -> ctypes.CDLL:
@@ -132,7 +136,7 @@ def check(rc: int, what: str) -> None:
     if rc == FAB_OK:
         return
     msg = f"{what}: {error_string(rc)} (code {rc})"
-    if rc in (FAB_ERR_INVALID_ARG, FAB_ERR_UNSUPPORTED):
+    if rc in (FAB_ERR_INVALID_ARG, FAB_ERR_UNSUPPORTED, FAB_ERR_WORKSPACE):
         raise ValueError(msg)
     if rc == FAB_ERR_DEVICE_TIMEOUT:
         raise DeviceTimeoutError(msg)

@@ -121,11 +121,16 @@ static int elt_size(int dtype) { return dtype == kDtypeF32 ? 4 : 2; }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Shared validation + launch for every attention entry point.
-static int attention_launch(FaLaunch L, cudaStream_t stream) {
+// Shared validation for every attention entry point.  Returns kOk with
+// *empty set when there is nothing to compute (no query rows).
+static int attention_validate(FaLaunch& L, bool* empty) {
+  *empty = false;
   if (L.dtype != kDtypeF16 && L.dtype != kDtypeBF16 && L.dtype != kDtypeF32) return kErrInvalidArg;
   if (L.B < 0 || L.Hq < 0 || L.Hkv < 0 || L.M < 0 || L.N < 0 || L.D <= 0) return kErrInvalidArg;
-  if (L.M == 0 || L.B == 0 || L.Hq == 0) return kOk;
+  if (L.M == 0 || L.B == 0 || L.Hq == 0) {
+    *empty = true;
+    return kOk;
+  }
   if (L.Hkv <= 0 || L.Hq % L.Hkv != 0) return kErrInvalidArg;
   if (!(L.sm_scale > 0.f) || !std::isfinite(L.sm_scale)) return kErrUnsupported;
   FaConfigInfo cfg;
@@ -153,7 +158,63 @@ static int attention_launch(FaLaunch L, cudaStream_t stream) {
   } else if (L.k == nullptr || L.v == nullptr) {
     return kErrInvalidArg;
   }
+  return kOk;
+}
+
+static int attention_launch(FaLaunch L, cudaStream_t stream) {
+  bool empty = false;
+  const int rc = attention_validate(L, &empty);
+  if (rc || empty) return rc;
   return fa_forward(L, stream);
+}
+
+static FaLaunch launch_from_params(const fab_attention_params* p) {
+  FaLaunch L{};
+  L.q = p->q;
+  L.k = p->k;
+  L.v = p->v;
+  L.o = p->o;
+  L.lse = p->lse;
+  L.q_sb = p->q_stride_b;
+  L.q_sh = p->q_stride_h;
+  L.q_ss = p->q_stride_s;
+  L.k_sb = p->k_stride_b;
+  L.k_sh = p->k_stride_h;
+  L.k_ss = p->k_stride_s;
+  L.v_sb = p->v_stride_b;
+  L.v_sh = p->v_stride_h;
+  L.v_ss = p->v_stride_s;
+  L.o_sb = p->o_stride_b;
+  L.o_sh = p->o_stride_h;
+  L.o_ss = p->o_stride_s;
+  L.l_sb = p->lse_stride_b;
+  L.l_sh = p->lse_stride_h;
+  L.l_ss = p->lse_stride_s;
+  L.B = p->batch;
+  L.Hq = p->heads_q;
+  L.Hkv = p->heads_kv;
+  L.M = p->seqlen_q;
+  L.N = p->seqlen_k;
+  L.D = p->head_dim;
+  L.dtype = p->dtype;
+  L.sm_scale = p->sm_scale;
+  L.causal = p->causal ? 1 : 0;
+  return L;
+}
+
+// Validated split-KV plan for the given request; *empty as above.
+static int splitkv_prepare(const fab_attention_params* p, int num_splits, FaLaunch* L, FaSplitPlan* plan,
+                           bool* empty) {
+  if (p == nullptr || plan == nullptr) return kErrInvalidArg;
+  *L = launch_from_params(p);
+  int rc = attention_validate(*L, empty);
+  if (rc || *empty) return rc;
+  rc = fa_split_plan(*L, num_splits, plan);
+  if (rc) return rc;
+  L->num_splits = plan->num_splits;
+  L->split_len = plan->split_len;
+  L->pack_gqa = plan->pack_gqa;
+  return kOk;
 }
 
 }  // namespace fab
@@ -162,7 +223,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 2; }
+int fab_abi_version(void) { return 3; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -178,6 +239,8 @@ const char* fab_error_string(int rc) {
       return "a kernel gave up on a bounded wait";
     case FAB_ERR_CUDA:
       return "CUDA runtime error";
+    case FAB_ERR_WORKSPACE:
+      return "workspace missing, misaligned or smaller than the split-KV plan needs";
     default:
       return "unknown error";
   }
@@ -263,37 +326,38 @@ int fab_flash_attn_fwd_block_d_nomask_contiguous(const void* q, const void* k, c
 
 int fab_attention_fwd(const fab_attention_params* p, void* stream) {
   if (p == nullptr) return kErrInvalidArg;
-  FaLaunch L{};
-  L.q = p->q;
-  L.k = p->k;
-  L.v = p->v;
-  L.o = p->o;
-  L.lse = p->lse;
-  L.q_sb = p->q_stride_b;
-  L.q_sh = p->q_stride_h;
-  L.q_ss = p->q_stride_s;
-  L.k_sb = p->k_stride_b;
-  L.k_sh = p->k_stride_h;
-  L.k_ss = p->k_stride_s;
-  L.v_sb = p->v_stride_b;
-  L.v_sh = p->v_stride_h;
-  L.v_ss = p->v_stride_s;
-  L.o_sb = p->o_stride_b;
-  L.o_sh = p->o_stride_h;
-  L.o_ss = p->o_stride_s;
-  L.l_sb = p->lse_stride_b;
-  L.l_sh = p->lse_stride_h;
-  L.l_ss = p->lse_stride_s;
-  L.B = p->batch;
-  L.Hq = p->heads_q;
-  L.Hkv = p->heads_kv;
-  L.M = p->seqlen_q;
-  L.N = p->seqlen_k;
-  L.D = p->head_dim;
-  L.dtype = p->dtype;
-  L.sm_scale = p->sm_scale;
-  L.causal = p->causal ? 1 : 0;
-  return attention_launch(L, static_cast<cudaStream_t>(stream));
+  return attention_launch(launch_from_params(p), static_cast<cudaStream_t>(stream));
+}
+
+int fab_attention_fwd_splitkv_workspace(const fab_attention_params* p, int num_splits, size_t* bytes,
+                                        int* splits_used) {
+  if (bytes == nullptr) return kErrInvalidArg;
+  FaLaunch L;
+  FaSplitPlan plan{};
+  bool empty = false;
+  const int rc = splitkv_prepare(p, num_splits, &L, &plan, &empty);
+  if (rc) return rc;
+  *bytes = empty ? 0 : plan.workspace_bytes;
+  if (splits_used != nullptr) *splits_used = empty ? 0 : plan.num_splits;
+  return kOk;
+}
+
+int fab_attention_fwd_splitkv(const fab_attention_params* p, int num_splits, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  FaLaunch L;
+  FaSplitPlan plan{};
+  bool empty = false;
+  int rc = splitkv_prepare(p, num_splits, &L, &plan, &empty);
+  if (rc || empty) return rc;
+  if (plan.num_splits > 1) {
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
+        workspace_bytes < plan.workspace_bytes)
+      return kErrWorkspace;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    L.o_part = reinterpret_cast<float*>(ws);
+    L.lse_part = reinterpret_cast<float*>(ws + plan.lse_offset);
+  }
+  return fa_forward_split(L, static_cast<cudaStream_t>(stream));
 }
 
 int fab_gemm(const fab_gemm_params* p, void* stream) {

@@ -29,6 +29,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "fa_internal.h"
@@ -169,15 +170,21 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
   // Work item: heads are the slow index so CTAs resident together share K/V
   // in L2; within a head the longest (causal) row blocks start first.
+  // Rows are the query positions of one (batch, query head), or with
+  // pack_gqa the (query head, position) pairs of the query heads sharing one
+  // key/value head.  blockIdx.y selects a split of split_len keys.
+  const int heads = p.pack_gqa ? p.Hq / p.group : p.Hq;
   const int bh = blockIdx.x / p.num_m_blocks;
   const int mblk = p.num_m_blocks - 1 - (blockIdx.x % p.num_m_blocks);
-  const int b = bh / p.Hq;
-  const int h = bh % p.Hq;
-  const int hk = h / p.group;
+  const int b = bh / heads;
+  const int h = bh % heads;  // query head; key/value head when packed
+  const int hk = p.pack_gqa ? h : h / p.group;
   const int m0 = mblk * kNQ * C::kBM;
-  int n_end = p.N;
-  if (p.causal) n_end = min(p.N, min(p.M, m0 + kNQ * C::kBM));
-  const int nt = (n_end + kBN - 1) / kBN;
+  const int n_begin = static_cast<int>(blockIdx.y) * p.split_len;
+  const int n_key_end = min(p.N, n_begin + p.split_len);  // keys of this split
+  int n_end = n_key_end;                                    // keys any row of this CTA may see
+  if (p.causal) n_end = min(n_end, p.pack_gqa ? p.Mq : min(p.M, m0 + kNQ * C::kBM));
+  const int nt = n_end > n_begin ? (n_end - n_begin + kBN - 1) / kBN : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       if (!mbar_wait(bar_k_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
       mbar_arrive_expect_tx(bar_k_full + s, C::kKVTileBytes);
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, j * kBN,
+        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, n_begin + j * kBN,
                     hk, b);
       if (!mbar_wait(bar_v_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) {
         issued = 2 * j + 1;
@@ -237,7 +244,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       }
       mbar_arrive_expect_tx(bar_v_full + s, C::kKVTileBytes);
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, j * kBN,
+        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, n_begin + j * kBN,
                     hk, b);
       issued = 2 * j + 2;
     }
@@ -379,6 +386,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const int row = m0 + i * C::kBM + r;
+    const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;  // query head of this row
+    const int qpos = p.pack_gqa ? row % p.Mq : row;            // its query position
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t t_o = tmem + lane_base + C::tmem_o(i);
     const float c = p.scale_log2;
@@ -399,10 +408,10 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         for (int e = 0; e < 32; ++e) s[cc * 32 + e] = __uint_as_float(rr[e]);
       }
       tmem_wait_ld();
-      const int col0 = j * kBN;
-      const bool need_mask = (col0 + kBN > p.N) || (p.causal && col0 + kBN - 1 > row);
+      const int col0 = n_begin + j * kBN;
+      const bool need_mask = (col0 + kBN > n_key_end) || (p.causal && col0 + kBN - 1 > qpos);
       if (need_mask) {
-        const int lim = p.causal ? min(p.N, row + 1) : p.N;
+        const int lim = p.causal ? min(n_key_end, qpos + 1) : n_key_end;
 #pragma unroll
         for (int e = 0; e < kBN; ++e)
           if (col0 + e >= lim) s[e] = kNegInf;
@@ -491,7 +500,17 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     }
 
     // ------------------------------------------------------------ epilogue
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sm;
+    // Single pass: O in the input dtype and LSE at the caller's strides.  Key
+    // splits: this split's normalised O in fp32 and its LSE, in the partial
+    // buffers the combine kernel reads.
+    const bool row_ok = row < p.M;
+    const int64_t part_row = (static_cast<int64_t>(blockIdx.y) * p.B + b) * p.Hq * static_cast<int64_t>(p.Mq) +
+                             static_cast<int64_t>(oh) * p.Mq + qpos;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm;
+    float* prow = p.o_part != nullptr ? p.o_part + part_row * p.D : nullptr;
+    float* lse_out = p.o_part != nullptr ? p.lse_part + part_row
+                     : p.lse != nullptr  ? p.lse + b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm
+                                         : nullptr;
     if (ok && nt > 0) {
       // One S buffer: O's only commit comes after the last product (phase 0);
       // two: one commit per KV tile.
@@ -509,18 +528,27 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]) * inv_l;
           const int ncols = min(32, p.D - cc * 32);
-          if (row < p.M && ncols > 0) store_o_chunk<T>(orow + cc * 32, v, ncols);
+          if (row_ok && ncols > 0) {
+            if (p.o_part != nullptr)
+              store_o_chunk<float>(prow + cc * 32, v, ncols);
+            else
+              store_o_chunk<T>(orow + cc * 32, v, ncols);
+          }
         }
-        if (p.lse != nullptr && row < p.M) {
+        if (lse_out != nullptr && row_ok) {
           const float m_base = (m_run == kNegInf) ? 0.f : m_run;
-          p.lse[b * p.l_sb + h * p.l_sh + static_cast<int64_t>(row) * p.l_sm] =
-              (m_base + log2f(l_run)) * 0.6931471805599453f;
+          *lse_out = (m_base + log2f(l_run)) * 0.6931471805599453f;
         }
       }
-    } else if (ok && nt == 0 && row < p.M) {
-      // No keys at all: 0/0 like the reference's acc / l_i.
-      for (int d = 0; d < p.D; ++d) orow[d] = static_cast<T>(NAN);
-      if (p.lse != nullptr) p.lse[b * p.l_sb + h * p.l_sh + static_cast<int64_t>(row) * p.l_sm] = kNegInf;
+    } else if (ok && nt == 0 && row_ok) {
+      if (p.o_part != nullptr) {
+        // An empty split: weight zero in the combine.
+        for (int d = 0; d < p.D; ++d) prow[d] = 0.f;
+      } else {
+        // No keys at all: 0/0 like the reference's acc / l_i.
+        for (int d = 0; d < p.D; ++d) orow[d] = static_cast<T>(NAN);
+      }
+      if (lse_out != nullptr) *lse_out = kNegInf;
     }
   }
   }
@@ -556,8 +584,19 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   // V is the MN-major operand of P*V: tf32 needs the 32-byte-chunk swizzle there.
   const CUtensorMapSwizzle v_swz = elt == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-  rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, L.M, L.Hq, L.B, L.q_ss, L.q_sh, L.q_sb, C::kAtom, C::kBM,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+  const int group = L.Hq / L.Hkv;
+  // Rows of the kernel's query tiles: positions of one head, or with pack_gqa
+  // the (head, position) pairs of one key/value head's query heads, which the
+  // caller has checked are evenly spaced in memory.
+  const int rows = L.pack_gqa ? group * L.M : L.M;
+  if (L.pack_gqa) {
+    const int64_t row_stride = L.M == 1 ? L.q_sh : L.q_ss;
+    rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, rows, L.Hkv, L.B, row_stride, group * L.q_sh, L.q_sb, C::kAtom,
+                       C::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, L.M, L.Hq, L.B, L.q_ss, L.q_sh, L.q_sb, C::kAtom, C::kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (rc) return rc;
   // With no keys the kernel never reads K/V, but a tensor map needs extents >= 1.
   const int n_map = L.N > 0 ? L.N : 1;
@@ -577,18 +616,77 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   kp.l_sm = L.l_ss;
   kp.B = L.B;
   kp.Hq = L.Hq;
-  kp.M = L.M;
+  kp.M = rows;
   kp.N = L.N;
   kp.D = L.D;
-  kp.group = L.Hq / L.Hkv;
+  kp.group = group;
   kp.scale_log2 = L.sm_scale * 1.4426950408889634f;
   kp.causal = L.causal;
-  kp.num_m_blocks = (L.M + kNQ * C::kBM - 1) / (kNQ * C::kBM);
-  const long long grid = static_cast<long long>(kp.num_m_blocks) * L.B * L.Hq;
+  kp.num_m_blocks = (rows + kNQ * C::kBM - 1) / (kNQ * C::kBM);
+  const int splits = L.num_splits > 0 ? L.num_splits : 1;
+  kp.split_len = L.num_splits > 0 ? L.split_len : (L.N > 0 ? L.N : 1);
+  kp.pack_gqa = L.pack_gqa;
+  kp.Mq = L.M;
+  kp.o_part = L.o_part;
+  kp.lse_part = L.lse_part;
+  const long long grid = static_cast<long long>(kp.num_m_blocks) * L.B * (L.pack_gqa ? L.Hkv : L.Hq);
   if (grid <= 0) return 0;
-  if (grid > 0x7fffffffLL) return kErrInvalidArg;
-  kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, stream>>>(kp, tq, tk, tv);
+  if (grid > 0x7fffffffLL || splits > 65535) return kErrInvalidArg;
+  kern<<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(splits)), C::kThreads, C::kSmemBytes, stream>>>(
+      kp, tq, tk, tv);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+}
+
+// Merges the key splits of every output row: with split s holding the
+// normalised O_s and LSE_s of its keys, O = sum_s w_s O_s / sum_s w_s and
+// LSE = max + log(sum_s w_s), w_s = exp(LSE_s - max).  One warp per row.
+template <typename T>
+__global__ void __launch_bounds__(128) fa_split_combine_kernel(const float* __restrict__ o_part,
+                                                               const float* __restrict__ lse_part, T* o, float* lse,
+                                                               int64_t o_sb, int64_t o_sh, int64_t o_sm, int64_t l_sb,
+                                                               int64_t l_sh, int64_t l_sm, int Hq, int M, int D,
+                                                               int splits, int64_t rows) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int m = static_cast<int>(row % M);
+  const int h = static_cast<int>((row / M) % Hq);
+  const int64_t b = row / (static_cast<int64_t>(M) * Hq);
+  T* orow = o + b * o_sb + h * o_sh + m * o_sm;
+  float mx = -INFINITY;
+  for (int sp = lane; sp < splits; sp += 32) mx = fmaxf(mx, lse_part[sp * rows + row]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (mx == -INFINITY) {
+    // No split saw a key: 0/0 like the single-pass kernel.
+    for (int d = lane; d < D; d += 32) orow[d] = static_cast<T>(NAN);
+    if (lse != nullptr && lane == 0) lse[b * l_sb + h * l_sh + m * l_sm] = -INFINITY;
+    return;
+  }
+  constexpr int kMaxPerLane = 8;  // head dims up to 256
+  float acc[kMaxPerLane];
+#pragma unroll
+  for (int e = 0; e < kMaxPerLane; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const float ls = lse_part[sp * rows + row];
+    if (ls == -INFINITY) continue;
+    const float w = expf(ls - mx);
+    wsum += w;
+    const float* src = o_part + (sp * rows + row) * D;
+#pragma unroll
+    for (int e = 0; e < kMaxPerLane; ++e) {
+      const int d = lane + 32 * e;
+      if (d < D) acc[e] = fmaf(w, src[d], acc[e]);
+    }
+  }
+  const float inv = 1.f / wsum;
+#pragma unroll
+  for (int e = 0; e < kMaxPerLane; ++e) {
+    const int d = lane + 32 * e;
+    if (d < D) orow[d] = static_cast<T>(acc[e] * inv);
+  }
+  if (lse != nullptr && lane == 0) lse[b * l_sb + h * l_sh + m * l_sm] = mx + logf(wsum);
 }
 
 // The sm_100a tile table: one instantiation per (element size, padded head dim).
@@ -658,6 +756,105 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream) {
   FAB_FA_TABLE(FAB_FA_LAUNCH)
 #undef FAB_FA_LAUNCH
   return kErrUnsupported;
+}
+
+// Tiles for split-KV launches (short query blocks against long key ranges):
+// one 128-row query tile per CTA with two S buffers, so S(j+1) is computed
+// while the softmax of tile j runs and the CTA streams K/V at the rate the
+// memory system gives it.
+#define FAB_FA_SPLIT_TABLE(X)                              \
+  X(2, 64, 1, 128, 3, 2)    /* 16-bit, head dim <= 64 */    \
+  X(2, 128, 1, 128, 2, 2)   /* 16-bit, head dim <= 128 */   \
+  X(2, 256, 1, 64, 2, 2)    /* 16-bit, head dim <= 256 */   \
+  X(4, 64, 1, 128, 2, 2)    /* fp32/tf32, head dim <= 64 */ \
+  X(4, 128, 1, 64, 2, 2)    /* fp32/tf32, head dim <= 128 */
+
+int fa_select_split_config(int dtype, int D, FaConfigInfo* out) {
+  if (D <= 0) return kErrInvalidArg;
+  if (dtype != kDtypeF16 && dtype != kDtypeBF16 && dtype != kDtypeF32) return kErrInvalidArg;
+  const int elt = dtype == kDtypeF32 ? 4 : 2;
+  int best = 0;
+#define FAB_FA_SPICK(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && D <= DP && (best == 0 || DP < best)) best = DP;
+  FAB_FA_SPLIT_TABLE(FAB_FA_SPICK)
+#undef FAB_FA_SPICK
+  if (best == 0) return kErrUnsupported;
+#define FAB_FA_SFILL(E, DP, NQ, BN, ST, SB)                                                      \
+  if (elt == E && best == DP) {                                                                 \
+    using Cf = FaCfg<E, DP, NQ, BN, ST, SB>;                                                    \
+    *out = FaConfigInfo{DP, NQ, BN, ST, Cf::kThreads, Cf::kSmemBytes, Cf::kTmemAlloc, SB};      \
+    return 0;                                                                                   \
+  }
+  FAB_FA_SPLIT_TABLE(FAB_FA_SFILL)
+#undef FAB_FA_SFILL
+  return kErrUnsupported;
+}
+
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
+  FaConfigInfo cfg;
+  int rc = fa_select_split_config(L.dtype, L.D, &cfg);
+  if (rc) return rc;
+  const int group = L.Hq / L.Hkv;
+  // Pack a key/value head's query heads into one tile when their rows are
+  // evenly spaced: every query position of a head, then the next head.
+  const bool even = L.M == 1 || L.q_sh == static_cast<int64_t>(L.M) * L.q_ss;
+  plan->pack_gqa = (group > 1 && even) ? 1 : 0;
+  const int64_t rows = plan->pack_gqa ? static_cast<int64_t>(group) * L.M : L.M;
+  const int64_t rows_per_cta = static_cast<int64_t>(cfg.nq) * 128;
+  const int64_t base_ctas = (rows + rows_per_cta - 1) / rows_per_cta * L.B * (plan->pack_gqa ? L.Hkv : L.Hq);
+  const int tiles = L.N > 0 ? (L.N + cfg.bn - 1) / cfg.bn : 0;
+  int splits = num_splits;
+  if (splits <= 0) {
+    // Enough CTAs for one per SM.
+    const int sms = num_sms();
+    if (sms <= 0) return kErrCuda;
+    splits = static_cast<int>((sms + base_ctas - 1) / (base_ctas > 0 ? base_ctas : 1));
+  }
+  splits = std::max(1, std::min({splits, std::max(tiles, 1), 65535}));
+  const int tiles_per_split = tiles > 0 ? (tiles + splits - 1) / splits : 1;
+  plan->split_len = tiles_per_split * cfg.bn;
+  plan->num_splits = L.N > 0 ? (L.N + plan->split_len - 1) / plan->split_len : 1;
+  plan->rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
+  plan->workspace_bytes = 0;
+  plan->lse_offset = 0;
+  if (plan->num_splits > 1) {
+    plan->lse_offset = align256(sizeof(float) * plan->num_splits * plan->rows * L.D);
+    plan->workspace_bytes = plan->lse_offset + align256(sizeof(float) * plan->num_splits * plan->rows);
+  }
+  return 0;
+}
+
+int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
+  FaConfigInfo c;
+  int rc = fa_select_split_config(L.dtype, L.D, &c);
+  if (rc) return rc;
+  const int elt = L.dtype == kDtypeF32 ? 4 : 2;
+  rc = kErrUnsupported;
+#define FAB_FA_SLAUNCH(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && c.d_pad == DP) rc = launch_entry<E, DP, NQ, BN, ST, SB>(L, stream);
+  FAB_FA_SPLIT_TABLE(FAB_FA_SLAUNCH)
+#undef FAB_FA_SLAUNCH
+  if (rc || L.num_splits <= 1 || L.o_part == nullptr) return rc;
+  const int64_t rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
+  const long long blocks = (rows + 3) / 4;
+  if (blocks > 0x7fffffffLL) return kErrInvalidArg;
+  const unsigned g = static_cast<unsigned>(blocks);
+  if (L.dtype == kDtypeBF16) {
+    fa_split_combine_kernel<__nv_bfloat16><<<g, 128, 0, stream>>>(
+        L.o_part, L.lse_part, static_cast<__nv_bfloat16*>(L.o), L.lse, L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss,
+        L.Hq, L.M, L.D, L.num_splits, rows);
+  } else if (L.dtype == kDtypeF16) {
+    fa_split_combine_kernel<__half><<<g, 128, 0, stream>>>(L.o_part, L.lse_part, static_cast<__half*>(L.o), L.lse,
+                                                           L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss, L.Hq, L.M,
+                                                           L.D, L.num_splits, rows);
+  } else {
+    fa_split_combine_kernel<float><<<g, 128, 0, stream>>>(L.o_part, L.lse_part, static_cast<float*>(L.o), L.lse,
+                                                          L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss, L.Hq, L.M,
+                                                          L.D, L.num_splits, rows);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads) {

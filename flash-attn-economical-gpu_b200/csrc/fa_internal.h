@@ -16,6 +16,7 @@ enum : int {
   kErrLaunch = 3,
   kErrDeviceTimeout = 4,
   kErrCuda = 5,
+  kErrWorkspace = 6,
 };
 
 enum : int { kDtypeF16 = 0, kDtypeBF16 = 1, kDtypeF32 = 2 };
@@ -31,6 +32,17 @@ struct FaKernelParams {
   float scale_log2;
   int causal;
   int num_m_blocks;
+  // Key splits: CTA (x, y) attends to keys [y * split_len, (y + 1) * split_len).
+  // Without splitting split_len >= N and gridDim.y == 1.
+  int split_len;
+  // pack_gqa: the M rows are (query head, position) pairs of the `group`
+  // query heads that share one key/value head, position = row % Mq.
+  int pack_gqa;
+  int Mq;
+  // With key splits each CTA writes its split's normalised O (fp32,
+  // [split][B][Hq][Mq][D]) and LSE ([split][B][Hq][Mq]) here instead of o/lse.
+  float* o_part;
+  float* lse_part;
 };
 
 // A fully validated attention launch (element strides, unit stride on D).
@@ -49,6 +61,22 @@ struct FaLaunch {
   int dtype;
   float sm_scale;
   int causal;
+  // Split-KV launches only (zero for the single-pass path).
+  int num_splits;
+  int split_len;
+  int pack_gqa;
+  float* o_part;
+  float* lse_part;
+};
+
+// Plan of a split-KV launch: the tile config it runs and the workspace it needs.
+struct FaSplitPlan {
+  int num_splits;
+  int split_len;
+  int pack_gqa;
+  int64_t rows;            // B * Hq * M output rows
+  size_t workspace_bytes;  // o_part then lse_part, each 256-byte aligned
+  size_t lse_offset;       // byte offset of lse_part in the workspace
 };
 
 struct FaConfigInfo {
@@ -83,6 +111,11 @@ struct GemmLaunch {
 
 int fa_select_config(int dtype, int D, FaConfigInfo* out);
 int fa_forward(const FaLaunch& L, cudaStream_t stream);
+int fa_select_split_config(int dtype, int D, FaConfigInfo* out);
+// num_splits <= 0 picks a split count from the SM count (needs a device).
+int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
+// Launches the split kernel and the combine kernel; L carries the plan.
+int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads);
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
 int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads);

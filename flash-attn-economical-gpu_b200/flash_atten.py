@@ -97,12 +97,17 @@ def _launch_attention(
     sm_scale: float,
     what: str,
     entry: str = "general",
+    num_splits: int = 0,
+    workspace: torch.Tensor | None = None,
 ) -> None:
     """Validate, conform and launch one attention forward through the C ABI.
 
     `entry` picks the C entry point: "basic" / "optimize_shared_mem" /
-    "nomask" for the reference-named kernels, "general" (`fab_attention_fwd`,
-    grouped-query heads) otherwise.
+    "nomask" for the reference-named kernels, "splitkv"
+    (`fab_attention_fwd_splitkv`, key splits merged by a second kernel;
+    `num_splits` 0 = one CTA per SM) or "general" (`fab_attention_fwd`,
+    grouped-query heads) otherwise.  `workspace` (uint8, CUDA) is used for the
+    split partials when it is large enough, else one is allocated.
 
     q/o: [B, Hq, M, D]; k/v: [B, Hkv, N, D]; lse: [B, Hq, M] fp32 or None.
     """
@@ -169,7 +174,17 @@ def _launch_attention(
             p.dtype = dt
             p.sm_scale = sm_scale
             p.causal = 1 if causal else 0
-            rc = _native.lib.fab_attention_fwd(ctypes.byref(p), stream)
+            if entry == "splitkv":
+                need = ctypes.c_size_t(0)
+                _native.check(_native.lib.fab_attention_fwd_splitkv_workspace(
+                    ctypes.byref(p), int(num_splits), ctypes.byref(need), None), what)
+                ws = workspace
+                if need.value and (ws is None or ws.numel() < need.value or ws.data_ptr() % 256):
+                    ws = torch.empty(need.value, device=q.device, dtype=torch.uint8)
+                rc = _native.lib.fab_attention_fwd_splitkv(
+                    ctypes.byref(p), int(num_splits), ws.data_ptr() if need.value else None, need.value, stream)
+            else:
+                rc = _native.lib.fab_attention_fwd(ctypes.byref(p), stream)
     _native.check(rc, what)
     if oc is not o:
         o.copy_(oc)
@@ -337,10 +352,63 @@ def attention_forward(
     return (o, lse) if return_lse else o
 
 
+def attention_forward_splitkv(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = False,
+    sm_scale: float | None = None,
+    return_lse: bool = False,
+    out: torch.Tensor | None = None,
+    num_splits: int = 0,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """attention_forward with the keys cut into `num_splits` ranges (flash-decoding).
+
+    For short query blocks (decode steps, speculative blocks) against long
+    key ranges: each range is attended to by its own CTAs and a second kernel
+    merges the ranges by their LSE.  `num_splits` 0 gives one CTA per SM.
+    Query heads that share a key/value head are packed into one query tile
+    when q is laid out [batch, head, seq, dim] contiguously (or seq == 1).
+    """
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("attention_forward_splitkv expects q, k, v with shape [batch, heads, seq, head_dim]")
+    if sm_scale is None:
+        sm_scale = q.shape[-1] ** -0.5
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    lse = torch.empty(q.shape[:3], device=q.device, dtype=torch.float32) if return_lse else None
+    _launch_attention(q, k, v, o, lse, causal=causal, sm_scale=sm_scale, what="attention_forward_splitkv",
+                      entry="splitkv", num_splits=num_splits, workspace=workspace)
+    return (o, lse) if return_lse else o
+
+
+def splitkv_workspace_bytes(q_shape, k_shape, dtype, *, num_splits: int = 0, causal: bool = False) -> tuple[int, int]:
+    """(workspace bytes, splits used) that attention_forward_splitkv needs for contiguous inputs of these shapes."""
+    B, Hq, M, D = q_shape
+    _, Hkv, N, _ = k_shape
+    p = _native.FabAttentionParams()
+    p.q = p.k = p.v = p.o = 256  # only shapes and strides are read
+    p.q_stride_b, p.q_stride_h, p.q_stride_s = Hq * M * D, M * D, D
+    p.k_stride_b, p.k_stride_h, p.k_stride_s = Hkv * N * D, N * D, D
+    p.v_stride_b, p.v_stride_h, p.v_stride_s = Hkv * N * D, N * D, D
+    p.o_stride_b, p.o_stride_h, p.o_stride_s = Hq * M * D, M * D, D
+    p.batch, p.heads_q, p.heads_kv, p.seqlen_q, p.seqlen_k, p.head_dim = B, Hq, Hkv, M, N, D
+    p.dtype = _native.dtype_code(dtype)
+    p.sm_scale = 1.0
+    p.causal = 1 if causal else 0
+    need, used = ctypes.c_size_t(0), ctypes.c_int(0)
+    _native.check(_native.lib.fab_attention_fwd_splitkv_workspace(
+        ctypes.byref(p), int(num_splits), ctypes.byref(need), ctypes.byref(used)), "splitkv_workspace_bytes")
+    return need.value, used.value
+
+
 __all__ = [
     "flash_attention_kernel_mapping",
     "flash_attention",
     "attention_forward",
+    "attention_forward_splitkv",
+    "splitkv_workspace_bytes",
     "_flash_attn_fwd_kernel_basic",
     "_flash_attn_fwd_kernel_optimize_shared_mem",
     "_flash_attn_fwd_kernel_block_d_nomask_contiguous",

@@ -19,6 +19,7 @@
 #ifndef FA_B200_H_
 #define FA_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -32,6 +33,7 @@ extern "C" {
 #define FAB_ERR_LAUNCH 3          /* the CUDA launch itself failed */
 #define FAB_ERR_DEVICE_TIMEOUT 4  /* a kernel gave up on a bounded wait (see fab_get_device_error) */
 #define FAB_ERR_CUDA 5            /* another CUDA runtime error */
+#define FAB_ERR_WORKSPACE 6       /* split-KV workspace missing, not 256-byte aligned, or too small */
 
 /* Element types. */
 #define FAB_DTYPE_F16 0
@@ -109,6 +111,33 @@ typedef struct fab_attention_params {
 } fab_attention_params;
 
 int fab_attention_fwd(const fab_attention_params* params, void* stream);
+
+/*
+ * Split-KV ("flash-decoding") form of fab_attention_fwd for short query blocks
+ * against long key ranges, where (batch x heads x query tiles) alone would
+ * leave most SMs idle.  No counterpart in the reference: it is the split-KV
+ * variant its LSE path allows (an extension of the ttft.py:169-219 SDPA
+ * replacement to decode-shaped calls).  Same parameters, same results within
+ * fp32 rounding of the merge.
+ *
+ * The keys are cut into num_splits ranges (num_splits <= 0: enough ranges for
+ * one CTA per SM).  Each range's attention (normalised O in fp32 and its LSE)
+ * goes to the workspace; a second kernel merges the ranges into o (and lse,
+ * when not NULL) with weights exp(LSE_split - LSE).  When the query heads of a
+ * key/value head are evenly spaced in memory (q_stride_h == seqlen_q *
+ * q_stride_s, or seqlen_q == 1) they share one query tile, so every K/V tile
+ * is read once per key/value head.
+ *
+ * fab_attention_fwd_splitkv_workspace writes the workspace size the call
+ * needs (0 when a single range suffices) and, if splits_used is not NULL, the
+ * number of ranges it will use.  The workspace is caller-owned device memory,
+ * 256-byte aligned; calls that share a workspace must be ordered on one
+ * stream.  FAB_ERR_WORKSPACE when it is missing, misaligned or too small.
+ */
+int fab_attention_fwd_splitkv_workspace(const fab_attention_params* params, int num_splits, size_t* bytes,
+                                        int* splits_used);
+int fab_attention_fwd_splitkv(const fab_attention_params* params, int num_splits, void* workspace,
+                              size_t workspace_bytes, void* stream);
 
 /*
  * Replaces `_matmul_contiguous_kernel[grid](a, b, c, M, N, K, BLOCK_M=..., ...)`

@@ -53,7 +53,7 @@ def test_python_binding_covers_every_declared_symbol():
 def test_abi_version_and_error_strings():
     assert _native.lib.fab_abi_version() == _native.ABI_VERSION
     assert _native.error_string(_native.FAB_OK) == "ok"
-    for rc in range(1, 6):
+    for rc in range(1, 7):
         assert _native.error_string(rc) != "unknown error"
     assert _native.error_string(99) == "unknown error"
 
@@ -68,6 +68,8 @@ def test_return_code_mapping():
         _native.check(_native.FAB_ERR_DEVICE_TIMEOUT, "x")
     with pytest.raises(RuntimeError):
         _native.check(_native.FAB_ERR_LAUNCH, "x")
+    with pytest.raises(ValueError, match="workspace"):
+        _native.check(_native.FAB_ERR_WORKSPACE, "x")
 
 
 @pytest.mark.parametrize(
@@ -140,3 +142,50 @@ def test_strided_entry_requires_unit_head_dim_stride():
     strides[3] = 1
     rc = lib.fab_flash_attn_fwd_basic(*args, *strides, 1, 4, 4, 4, 64, 0.125, 0, 1, 1, None)
     assert rc == _native.FAB_ERR_INVALID_ARG
+
+
+def _decode_params(B=1, Hq=28, Hkv=4, M=1, N=32768, D=128, dtype=_native.FAB_DTYPE_BF16):
+    a = _native.FabAttentionParams()
+    a.q = a.k = a.v = a.o = 4096  # never dereferenced by these calls
+    a.q_stride_b, a.q_stride_h, a.q_stride_s = Hq * M * D, M * D, D
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = Hkv * N * D, N * D, D
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = Hkv * N * D, N * D, D
+    a.o_stride_b, a.o_stride_h, a.o_stride_s = Hq * M * D, M * D, D
+    a.batch, a.heads_q, a.heads_kv, a.seqlen_q, a.seqlen_k, a.head_dim, a.dtype = B, Hq, Hkv, M, N, D, dtype
+    a.sm_scale = D ** -0.5
+    return a
+
+
+def _round256(x):
+    return (x + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("splits, expect_used", [(8, 8), (1, 1), (1000, 256), (300, 256)])
+def test_splitkv_workspace_size(splits, expect_used):
+    """Workspace = fp32 partial O of every split and row, then the partial LSEs, each 256-byte aligned; the
+    split count is capped by the number of 128-key tiles."""
+    lib = _native.lib
+    a = _decode_params()
+    need, used = ctypes.c_size_t(0), ctypes.c_int(0)
+    assert lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(a), splits, ctypes.byref(need), ctypes.byref(used)) == 0
+    assert used.value == expect_used
+    rows = 1 * 28 * 1
+    want = 0 if expect_used == 1 else _round256(4 * expect_used * rows * 128) + _round256(4 * expect_used * rows)
+    assert need.value == want
+
+
+def test_splitkv_rejects_bad_workspace_before_any_launch():
+    lib = _native.lib
+    a = _decode_params()
+    need = ctypes.c_size_t(0)
+    assert lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(a), 8, ctypes.byref(need), None) == 0
+    assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, None, need.value, None) == _native.FAB_ERR_WORKSPACE
+    assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, 1 << 20, need.value - 1, None) == _native.FAB_ERR_WORKSPACE
+    assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, (1 << 20) + 16, need.value, None) == _native.FAB_ERR_WORKSPACE
+    assert lib.fab_attention_fwd_splitkv_workspace(None, 8, ctypes.byref(need), None) == _native.FAB_ERR_INVALID_ARG
+    a.heads_kv = 3
+    assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, 1 << 20, 1 << 30, None) == _native.FAB_ERR_INVALID_ARG
+    a.heads_kv, a.seqlen_q = 4, 0  # nothing to compute: no workspace, no launch
+    assert lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(a), 8, ctypes.byref(need), None) == 0
+    assert need.value == 0
+    assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, None, 0, None) == _native.FAB_OK
