@@ -90,6 +90,7 @@ PROTOTYPES = {
     "fab_attention_fwd_splitkv_workspace": (
         _i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32)]),
     "fab_attention_fwd_splitkv": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp, ctypes.c_size_t, _vp]),
+    "fab_attention_fwd_splitkv_static": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
     "fab_matmul_contiguous": (_i32, [_vp] * 3 + [_i32] * 6 + [_vp]),
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),

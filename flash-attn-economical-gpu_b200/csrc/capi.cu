@@ -217,6 +217,35 @@ static int splitkv_prepare(const fab_attention_params* p, int num_splits, FaLaun
   return kOk;
 }
 
+// ---------------------------------------------------------------------------
+// Static split-KV scratch, for callers that cannot allocate device memory.
+//
+// fab_attention_fwd_splitkv_static runs the split-KV path with its partial
+// results in this file-scope device array instead of a caller-owned
+// workspace.  It is part of the library's device image, so using it needs no
+// cudaMalloc, cudaFree or any other allocating call.  Its address is looked
+// up with cudaGetSymbolAddress once per device, at the first call on that
+// device.  Requests whose partials need more than kStaticScratchBytes are
+// rejected with FAB_ERR_WORKSPACE.  Every call on a device uses the same
+// array, so two calls whose executions overlap (different streams, or host
+// threads launching concurrently) race on it; calls ordered on one stream do
+// not.
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_splitkv_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxScratchDevices = 64;
+
+static void* static_scratch_address(int device) {
+  static std::once_flag once[kMaxScratchDevices];
+  static void* addr[kMaxScratchDevices] = {};
+  if (device < 0 || device >= kMaxScratchDevices) return nullptr;
+  std::call_once(once[device], [device] {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_splitkv_static_scratch) == cudaSuccess) addr[device] = p;
+  });
+  return addr[device];
+}
+
 }  // namespace fab
 
 using namespace fab;
@@ -354,6 +383,25 @@ int fab_attention_fwd_splitkv(const fab_attention_params* p, int num_splits, voi
         workspace_bytes < plan.workspace_bytes)
       return kErrWorkspace;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    L.o_part = reinterpret_cast<float*>(ws);
+    L.lse_part = reinterpret_cast<float*>(ws + plan.lse_offset);
+  }
+  return fa_forward_split(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_attention_fwd_splitkv_static(const fab_attention_params* p, int num_splits, void* stream) {
+  FaLaunch L;
+  FaSplitPlan plan{};
+  bool empty = false;
+  int rc = splitkv_prepare(p, num_splits, &L, &plan, &empty);
+  if (rc || empty) return rc;
+  if (plan.num_splits > 1) {
+    if (plan.workspace_bytes > kStaticScratchBytes) return kErrWorkspace;
+    uint8_t* ws = static_cast<uint8_t*>(static_scratch_address(current_device()));
+    if (ws == nullptr) return kErrCuda;
+    // Nothing in the scratch has to start at zero: every split writes all of
+    // its partial rows (an empty split writes zeros and LSE -inf) before the
+    // merge kernel, launched after it on the same stream, reads them.
     L.o_part = reinterpret_cast<float*>(ws);
     L.lse_part = reinterpret_cast<float*>(ws + plan.lse_offset);
   }

@@ -140,6 +140,19 @@ int fab_attention_fwd_splitkv(const fab_attention_params* params, int num_splits
                               size_t workspace_bytes, void* stream);
 
 /*
+ * fab_attention_fwd_splitkv for callers that cannot allocate device memory.
+ * No counterpart in the reference.  The split partials live in an 8 MiB
+ * array inside the library's device image (looked up once per device with
+ * cudaGetSymbolAddress), so the call allocates nothing.  A request whose
+ * partials need more than 8 MiB (fab_attention_fwd_splitkv_workspace reports
+ * the size) returns FAB_ERR_WORKSPACE; fewer splits make it smaller.  All
+ * calls on a device share the array: calls whose executions overlap
+ * (different streams, or concurrent host threads) race on it, calls ordered
+ * on one stream do not.
+ */
+int fab_attention_fwd_splitkv_static(const fab_attention_params* params, int num_splits, void* stream);
+
+/*
  * Replaces `_matmul_contiguous_kernel[grid](a, b, c, M, N, K, BLOCK_M=..., ...)`
  * (mma.py:8-21, launched as in test_mma.py:318-332): row-major contiguous
  * A[M,K], B[K,N], C[M,N], fp32 accumulation.  round_f16 != 0 rounds the
