@@ -61,6 +61,21 @@ class FabGemmParams(ctypes.Structure):
     ]
 
 
+class FabAttentionVarlenParams(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("k", _vp), ("v", _vp), ("o", _vp), ("lse", _vp),
+        ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp),
+        ("q_stride_t", _i64), ("q_stride_h", _i64),
+        ("k_stride_t", _i64), ("k_stride_h", _i64),
+        ("v_stride_t", _i64), ("v_stride_h", _i64),
+        ("o_stride_t", _i64), ("o_stride_h", _i64),
+        ("lse_stride_h", _i64), ("lse_stride_t", _i64),
+        ("batch", _i32), ("heads_q", _i32), ("heads_kv", _i32), ("total_q", _i32), ("total_k", _i32),
+        ("max_seqlen_q", _i32), ("max_seqlen_k", _i32), ("head_dim", _i32), ("dtype", _i32),
+        ("sm_scale", _f32), ("causal", _i32),
+    ]
+
+
 class FabFaConfig(ctypes.Structure):
     _fields_ = [
         ("head_dim_padded", _i32), ("q_tiles_per_cta", _i32), ("block_n", _i32), ("stages", _i32),
@@ -87,6 +102,7 @@ PROTOTYPES = {
     "fab_flash_attn_fwd_optimize_shared_mem": (_i32, _STRIDED_FA_ARGS),
     "fab_flash_attn_fwd_block_d_nomask_contiguous": (_i32, [_vp] * 4 + [_i32] * 5 + [_f32, _i32, _vp]),
     "fab_attention_fwd": (_i32, [ctypes.POINTER(FabAttentionParams), _vp]),
+    "fab_attention_fwd_varlen": (_i32, [ctypes.POINTER(FabAttentionVarlenParams), _vp]),
     "fab_attention_fwd_splitkv_workspace": (
         _i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32)]),
     "fab_attention_fwd_splitkv": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp, ctypes.c_size_t, _vp]),

@@ -358,6 +358,59 @@ int fab_attention_fwd(const fab_attention_params* p, void* stream) {
   return attention_launch(launch_from_params(p), static_cast<cudaStream_t>(stream));
 }
 
+int fab_attention_fwd_varlen(const fab_attention_varlen_params* p, void* stream) {
+  if (p == nullptr) return kErrInvalidArg;
+  if (p->batch < 0 || p->total_q < 0 || p->total_k < 0 || p->max_seqlen_q < 0 || p->max_seqlen_k < 0)
+    return kErrInvalidArg;
+  if (p->batch == 0 || p->total_q == 0 || p->max_seqlen_q == 0 || p->heads_q == 0) return kOk;
+  if (p->cu_seqlens_q == nullptr || p->cu_seqlens_k == nullptr ||
+      (reinterpret_cast<uintptr_t>(p->cu_seqlens_q) & 3u) != 0 || (reinterpret_cast<uintptr_t>(p->cu_seqlens_k) & 3u) != 0)
+    return kErrInvalidArg;
+  FaLaunch L{};
+  L.q = p->q;
+  L.k = p->k;
+  L.v = p->v;
+  L.o = p->o;
+  L.lse = p->lse;
+  L.q_sh = p->q_stride_h;
+  L.q_ss = p->q_stride_t;
+  L.k_sh = p->k_stride_h;
+  L.k_ss = p->k_stride_t;
+  L.v_sh = p->v_stride_h;
+  L.v_ss = p->v_stride_t;
+  L.o_sh = p->o_stride_h;
+  L.o_ss = p->o_stride_t;
+  L.l_sh = p->lse_stride_h;
+  L.l_ss = p->lse_stride_t;
+  L.B = p->batch;
+  L.Hq = p->heads_q;
+  L.Hkv = p->heads_kv;
+  L.M = p->max_seqlen_q;
+  L.N = p->max_seqlen_k;
+  L.D = p->head_dim;
+  L.dtype = p->dtype;
+  L.sm_scale = p->sm_scale;
+  L.causal = p->causal ? 1 : 0;
+  L.cu_q = p->cu_seqlens_q;
+  L.cu_k = p->cu_seqlens_k;
+  L.total_q = p->total_q;
+  L.total_k = p->total_k;
+  bool empty = false;
+  int rc = attention_validate(L, &empty);
+  if (rc || empty) return rc;
+  if (p->total_k == 0) {
+    // No keys in any sequence: the kernel only writes NaN rows; the K/V maps
+    // (never read) point at Q.
+    L.k = L.q;
+    L.v = L.q;
+    L.k_sh = L.v_sh = L.q_sh;
+    L.k_ss = L.v_ss = L.q_ss;
+    L.Hkv = L.Hq;
+    L.total_k = L.total_q;
+  }
+  return fa_forward(L, static_cast<cudaStream_t>(stream));
+}
+
 int fab_attention_fwd_splitkv_workspace(const fab_attention_params* p, int num_splits, size_t* bytes,
                                         int* splits_used) {
   if (bytes == nullptr) return kErrInvalidArg;

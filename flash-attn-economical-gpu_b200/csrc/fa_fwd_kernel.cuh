@@ -180,10 +180,26 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
   const int h = bh % heads;  // query head; key/value head when packed
   const int hk = p.pack_gqa ? h : h / p.group;
   const int m0 = mblk * kNQ * C::kBM;
+  // Lengths and first rows of this batch entry; packed variable-length
+  // batches read them from the cumulative offsets and index one flat tensor.
+  int seq_m = p.M, seq_n = p.N, q_row0 = 0, k_row0 = 0, map_b = b;
+  int64_t o_boff = b * p.o_sb, l_boff = b * p.l_sb;
+  if (p.cu_q != nullptr) {
+    q_row0 = p.cu_q[b];
+    seq_m = p.cu_q[b + 1] - q_row0;
+    k_row0 = p.cu_k[b];
+    seq_n = p.cu_k[b + 1] - k_row0;
+    map_b = 0;
+    o_boff = static_cast<int64_t>(q_row0) * p.o_sm;
+    l_boff = static_cast<int64_t>(q_row0) * p.l_sm;
+    // The grid covers the longest sequence; row blocks past this one's end
+    // leave before touching shared memory, TMEM or a barrier.
+    if (m0 >= seq_m) return;
+  }
   const int n_begin = static_cast<int>(blockIdx.y) * p.split_len;
-  const int n_key_end = min(p.N, n_begin + p.split_len);  // keys of this split
-  int n_end = n_key_end;                                    // keys any row of this CTA may see
-  if (p.causal) n_end = min(n_end, p.pack_gqa ? p.Mq : min(p.M, m0 + kNQ * C::kBM));
+  const int n_key_end = min(seq_n, n_begin + p.split_len);  // keys of this split
+  int n_end = n_key_end;                                      // keys any row of this CTA may see
+  if (p.causal) n_end = min(n_end, p.pack_gqa ? p.Mq : min(seq_m, m0 + kNQ * C::kBM));
   const int nt = n_end > n_begin ? (n_end - n_begin + kBN - 1) / kBN : 0;
 
   if (threadIdx.x == 0) {
@@ -228,7 +244,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     for (int i = 0; i < kNQ; ++i)
       for (int a = 0; a < C::kNumAtoms; ++a)
         tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full, a * C::kAtom,
-                    m0 + i * C::kBM, h, b);
+                    q_row0 + m0 + i * C::kBM, h, map_b);
     int issued = 0;
     for (int j = 0; j < nt; ++j) {
       const int s = j % kStages;
@@ -236,16 +252,16 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       if (!mbar_wait(bar_k_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
       mbar_arrive_expect_tx(bar_k_full + s, C::kKVTileBytes);
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, n_begin + j * kBN,
-                    hk, b);
+        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, k_row0 + n_begin + j * kBN,
+                    hk, map_b);
       if (!mbar_wait(bar_v_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) {
         issued = 2 * j + 1;
         break;
       }
       mbar_arrive_expect_tx(bar_v_full + s, C::kKVTileBytes);
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, n_begin + j * kBN,
-                    hk, b);
+        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, k_row0 + n_begin + j * kBN,
+                    hk, map_b);
       issued = 2 * j + 2;
     }
     // Never leave this CTA with bulk copies still landing in its smem: wait
@@ -503,13 +519,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     // Single pass: O in the input dtype and LSE at the caller's strides.  Key
     // splits: this split's normalised O in fp32 and its LSE, in the partial
     // buffers the combine kernel reads.
-    const bool row_ok = row < p.M;
+    const bool row_ok = row < (p.cu_q != nullptr ? seq_m : p.M);
     const int64_t part_row = (static_cast<int64_t>(blockIdx.y) * p.B + b) * p.Hq * static_cast<int64_t>(p.Mq) +
                              static_cast<int64_t>(oh) * p.Mq + qpos;
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm;
+    T* orow = reinterpret_cast<T*>(p.o) + o_boff + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm;
     float* prow = p.o_part != nullptr ? p.o_part + part_row * p.D : nullptr;
     float* lse_out = p.o_part != nullptr ? p.lse_part + part_row
-                     : p.lse != nullptr  ? p.lse + b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm
+                     : p.lse != nullptr  ? p.lse + l_boff + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm
                                          : nullptr;
     if (ok && nt > 0) {
       // One S buffer: O's only commit comes after the last product (phase 0);
@@ -589,7 +605,12 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   // the (head, position) pairs of one key/value head's query heads, which the
   // caller has checked are evenly spaced in memory.
   const int rows = L.pack_gqa ? group * L.M : L.M;
-  if (L.pack_gqa) {
+  const bool varlen = L.cu_q != nullptr;
+  if (varlen) {
+    // One flat [total, heads, D] tensor per operand; batch extent 1.
+    rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, L.total_q, L.Hq, 1, L.q_ss, L.q_sh, 0, C::kAtom, C::kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  } else if (L.pack_gqa) {
     const int64_t row_stride = L.M == 1 ? L.q_sh : L.q_ss;
     rc = make_bhsd_map(&tq, L.q, dt, elt, L.D, rows, L.Hkv, L.B, row_stride, group * L.q_sh, L.q_sb, C::kAtom,
                        C::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -599,11 +620,13 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   }
   if (rc) return rc;
   // With no keys the kernel never reads K/V, but a tensor map needs extents >= 1.
-  const int n_map = L.N > 0 ? L.N : 1;
-  rc = make_bhsd_map(&tk, L.k, dt, elt, L.D, n_map, L.Hkv, L.B, L.k_ss, L.k_sh, L.k_sb, C::kAtom, kBN,
+  const int n_rows = varlen ? L.total_k : L.N;
+  const int n_map = n_rows > 0 ? n_rows : 1;
+  const int kv_b = varlen ? 1 : L.B;
+  rc = make_bhsd_map(&tk, L.k, dt, elt, L.D, n_map, L.Hkv, kv_b, L.k_ss, L.k_sh, L.k_sb, C::kAtom, kBN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_bhsd_map(&tv, L.v, dt, elt, L.D, n_map, L.Hkv, L.B, L.v_ss, L.v_sh, L.v_sb, C::kAtom, kBN, v_swz);
+  rc = make_bhsd_map(&tv, L.v, dt, elt, L.D, n_map, L.Hkv, kv_b, L.v_ss, L.v_sh, L.v_sb, C::kAtom, kBN, v_swz);
   if (rc) return rc;
   FaKernelParams kp;
   kp.o = L.o;
@@ -629,6 +652,8 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   kp.Mq = L.M;
   kp.o_part = L.o_part;
   kp.lse_part = L.lse_part;
+  kp.cu_q = L.cu_q;
+  kp.cu_k = L.cu_k;
   const long long grid = static_cast<long long>(kp.num_m_blocks) * L.B * (L.pack_gqa ? L.Hkv : L.Hq);
   if (grid <= 0) return 0;
   if (grid > 0x7fffffffLL || splits > 65535) return kErrInvalidArg;

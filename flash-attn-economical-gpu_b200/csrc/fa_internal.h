@@ -43,6 +43,11 @@ struct FaKernelParams {
   // [split][B][Hq][Mq][D]) and LSE ([split][B][Hq][Mq]) here instead of o/lse.
   float* o_part;
   float* lse_part;
+  // Packed variable-length batches: sequence b's query rows are
+  // [cu_q[b], cu_q[b+1]) of a [total, heads, D] tensor (keys likewise with
+  // cu_k); M and N are then the longest lengths.  NULL for dense batches.
+  const int* cu_q;
+  const int* cu_k;
 };
 
 // A fully validated attention launch (element strides, unit stride on D).
@@ -67,6 +72,12 @@ struct FaLaunch {
   int pack_gqa;
   float* o_part;
   float* lse_part;
+  // Packed variable-length batches (see FaKernelParams); the tensor maps
+  // then span total_q / total_k rows with batch extent 1.
+  const int* cu_q;
+  const int* cu_k;
+  int total_q;
+  int total_k;
 };
 
 // Plan of a split-KV launch: the tile config it runs and the workspace it needs.

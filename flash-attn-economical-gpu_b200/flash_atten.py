@@ -383,6 +383,88 @@ def attention_forward_splitkv(
     return (o, lse) if return_lse else o
 
 
+def attention_forward_varlen(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_k: torch.Tensor,
+    max_seqlen_q: int,
+    max_seqlen_k: int,
+    *,
+    causal: bool = False,
+    sm_scale: float | None = None,
+    return_lse: bool = False,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+    """Attention over a packed batch of variable-length sequences.
+
+    q: [total_q, Hq, D], k/v: [total_k, Hkv, D]; sequence b owns query rows
+    cu_seqlens_q[b]:cu_seqlens_q[b+1] and key rows cu_seqlens_k[b]:cu_seqlens_k[b+1]
+    (int32 CUDA tensors of batch + 1 offsets).  Returns o like q and, with
+    return_lse, lse [Hq, total_q] in fp32.  Causal masking is top-left inside
+    each sequence, as the reference's kernels mask a dense block.
+    """
+    what = "attention_forward_varlen"
+    if q.ndim != 3 or k.ndim != 3 or v.ndim != 3:
+        raise ValueError(f"{what} expects q, k, v with shape [total_tokens, heads, head_dim]")
+    for name, t in (("q", q), ("k", k), ("v", v), ("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        _require_cuda_tensor(name, t)
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError(f"{what}: q, k and v must share one dtype")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+        raise ValueError(f"{what}: cu_seqlens_q / cu_seqlens_k must be int32")
+    if cu_seqlens_q.ndim != 1 or cu_seqlens_q.shape != cu_seqlens_k.shape or cu_seqlens_q.numel() < 1:
+        raise ValueError(f"{what}: cu_seqlens_q and cu_seqlens_k must both have batch + 1 entries")
+    total_q, Hq, D = q.shape
+    total_k, Hkv, Dk = k.shape
+    if tuple(v.shape) != tuple(k.shape) or Dk != D:
+        raise ValueError(f"{what}: inconsistent shapes q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    if Hkv == 0 or Hq % Hkv:
+        raise ValueError(f"{what}: query heads ({Hq}) must be a multiple of key/value heads ({Hkv})")
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    if tuple(o.shape) != tuple(q.shape) or o.dtype != q.dtype:
+        raise ValueError(f"{what}: out must match q's shape and dtype")
+    lse = torch.empty(Hq, total_q, device=q.device, dtype=torch.float32) if return_lse else None
+    batch = cu_seqlens_q.numel() - 1
+    if batch == 0 or total_q == 0:
+        return (o, lse) if return_lse else o
+    sm_scale = float(sm_scale)
+    if sm_scale < 0:
+        q, sm_scale = -q, -sm_scale
+    elif sm_scale == 0:
+        sm_scale = 1e-30
+    dt = _native.dtype_code(q.dtype)
+    # [total, heads, D] viewed as [1, total, heads, D] -> conform as [1, heads, total, D] views.
+    qc, kc, vc = (_conform(t.unsqueeze(0).transpose(1, 2)).transpose(1, 2).squeeze(0) for t in (q, k, v))
+    o4 = o.unsqueeze(0).transpose(1, 2)
+    oc = o if _tma_ready(o4, tuple(o4.stride())) else _padded_like(o4).transpose(1, 2).squeeze(0)
+    cq, ck = cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous()
+    p = _native.FabAttentionVarlenParams()
+    p.q, p.k, p.v, p.o = qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.cu_seqlens_q, p.cu_seqlens_k = cq.data_ptr(), ck.data_ptr()
+    p.q_stride_t, p.q_stride_h = qc.stride()[:2]
+    p.k_stride_t, p.k_stride_h = kc.stride()[:2]
+    p.v_stride_t, p.v_stride_h = vc.stride()[:2]
+    p.o_stride_t, p.o_stride_h = oc.stride()[:2]
+    if lse is not None:
+        p.lse_stride_h, p.lse_stride_t = lse.stride()
+    p.batch, p.heads_q, p.heads_kv = batch, Hq, Hkv
+    p.total_q, p.total_k = total_q, total_k
+    p.max_seqlen_q, p.max_seqlen_k = int(max_seqlen_q), int(max_seqlen_k)
+    p.head_dim, p.dtype, p.sm_scale, p.causal = D, dt, sm_scale, 1 if causal else 0
+    with torch.cuda.device(q.device):
+        stream = ctypes.c_void_p(_native.current_stream_handle(q.device))
+        rc = _native.lib.fab_attention_fwd_varlen(ctypes.byref(p), stream)
+    _native.check(rc, what)
+    if oc is not o:
+        o.copy_(oc)
+    return (o, lse) if return_lse else o
+
+
 def splitkv_workspace_bytes(q_shape, k_shape, dtype, *, num_splits: int = 0, causal: bool = False) -> tuple[int, int]:
     """(workspace bytes, splits used) that attention_forward_splitkv needs for contiguous inputs of these shapes."""
     B, Hq, M, D = q_shape
@@ -408,6 +490,7 @@ __all__ = [
     "flash_attention",
     "attention_forward",
     "attention_forward_splitkv",
+    "attention_forward_varlen",
     "splitkv_workspace_bytes",
     "_flash_attn_fwd_kernel_basic",
     "_flash_attn_fwd_kernel_optimize_shared_mem",

@@ -113,6 +113,47 @@ typedef struct fab_attention_params {
 int fab_attention_fwd(const fab_attention_params* params, void* stream);
 
 /*
+ * fab_attention_fwd over a packed batch of variable-length sequences: q is
+ * [total_q, heads_q, head_dim] with sequence b's queries in rows
+ * [cu_seqlens_q[b], cu_seqlens_q[b+1]), k/v are [total_k, heads_kv, head_dim]
+ * likewise with cu_seqlens_k (int32 device arrays of batch + 1 offsets), o
+ * is laid out like q and lse (fp32, may be NULL) is indexed [head, token].
+ * max_seqlen_q / max_seqlen_k bound the per-sequence lengths.  Causal
+ * masking is top-left within each sequence, as in the reference (key n of a
+ * sequence visible to its query m iff m >= n); a sequence with queries but no
+ * keys gets NaN rows and lse -inf.  No counterpart in the reference, whose
+ * kernels take one dense [batch, head, seq, head_dim] block (the ragged case
+ * of its scope: flash_atten.py:21-39 strides, ttft.py:169-219 SDPA calls).
+ */
+typedef struct fab_attention_varlen_params {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t o_stride_t, o_stride_h;
+  int64_t lse_stride_h, lse_stride_t;
+  int batch;
+  int heads_q;
+  int heads_kv;
+  int total_q;
+  int total_k;
+  int max_seqlen_q;
+  int max_seqlen_k;
+  int head_dim;
+  int dtype;
+  float sm_scale;
+  int causal;
+} fab_attention_varlen_params;
+
+int fab_attention_fwd_varlen(const fab_attention_varlen_params* params, void* stream);
+
+/*
  * Split-KV ("flash-decoding") form of fab_attention_fwd for short query blocks
  * against long key ranges, where (batch x heads x query tiles) alone would
  * leave most SMs idle.  No counterpart in the reference: it is the split-KV

@@ -189,3 +189,26 @@ def test_splitkv_rejects_bad_workspace_before_any_launch():
     assert lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(a), 8, ctypes.byref(need), None) == 0
     assert need.value == 0
     assert lib.fab_attention_fwd_splitkv(ctypes.byref(a), 8, None, 0, None) == _native.FAB_OK
+
+
+def test_varlen_entry_validates_before_any_launch():
+    lib = _native.lib
+    assert lib.fab_attention_fwd_varlen(None, None) == _native.FAB_ERR_INVALID_ARG
+    p = _native.FabAttentionVarlenParams()
+    p.q = p.k = p.v = p.o = 4096
+    p.batch, p.heads_q, p.heads_kv, p.total_q, p.total_k = 2, 4, 2, 10, 12
+    p.max_seqlen_q, p.max_seqlen_k, p.head_dim, p.dtype, p.sm_scale = 6, 7, 64, _native.FAB_DTYPE_BF16, 0.125
+    p.q_stride_t, p.q_stride_h = 4 * 64, 64
+    p.k_stride_t, p.k_stride_h = 2 * 64, 64
+    p.v_stride_t, p.v_stride_h = 2 * 64, 64
+    p.o_stride_t, p.o_stride_h = 4 * 64, 64
+    assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG  # no cu_seqlens
+    p.cu_seqlens_q, p.cu_seqlens_k = 8192, 8194  # second one misaligned
+    assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
+    p.cu_seqlens_k = 8200
+    p.heads_kv = 3
+    assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
+    p.heads_kv, p.total_q = 2, -1
+    assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
+    p.total_q = 0  # nothing to compute
+    assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_OK
