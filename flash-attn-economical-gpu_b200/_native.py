@@ -28,8 +28,12 @@ FAB_DTYPE_F16 = 0
 FAB_DTYPE_BF16 = 1
 FAB_DTYPE_F32 = 2
 
+FAB_FA_VARIANT_TWO_TILES = 0
+FAB_FA_VARIANT_ONE_TILE = 1
+
 FAB_KERNEL_ATTENTION = 0
 FAB_KERNEL_MATMUL = 1
+FAB_KERNEL_ATTENTION_ONE_TILE = 2
 
 # Every symbol include/fa_b200.h declares, with its ctypes prototype.
 _i64 = ctypes.c_int64
@@ -103,6 +107,8 @@ PROTOTYPES = {
     "fab_flash_attn_fwd_block_d_nomask_contiguous": (_i32, [_vp] * 4 + [_i32] * 5 + [_f32, _i32, _vp]),
     "fab_attention_fwd": (_i32, [ctypes.POINTER(FabAttentionParams), _vp]),
     "fab_attention_fwd_varlen": (_i32, [ctypes.POINTER(FabAttentionVarlenParams), _vp]),
+    "fab_attention_fwd_variant": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
+    "fab_flash_attn_config_variant": (_i32, [_i32, _i32, _i32, ctypes.POINTER(FabFaConfig)]),
     "fab_attention_fwd_splitkv_workspace": (
         _i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32)]),
     "fab_attention_fwd_splitkv": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp, ctypes.c_size_t, _vp]),
@@ -191,6 +197,16 @@ def fa_config(dtype: int, head_dim: int) -> FabFaConfig | None:
     if rc == FAB_ERR_UNSUPPORTED:
         return None
     check(rc, "fab_flash_attn_config")
+    return cfg
+
+
+def fa_config_variant(dtype: int, head_dim: int, variant: int) -> FabFaConfig | None:
+    """Tile of one of the two compiled families (FAB_FA_VARIANT_*), or None when head_dim is out of range."""
+    cfg = FabFaConfig()
+    rc = lib.fab_flash_attn_config_variant(int(dtype), int(head_dim), int(variant), ctypes.byref(cfg))
+    if rc == FAB_ERR_UNSUPPORTED:
+        return None
+    check(rc, "fab_flash_attn_config_variant")
     return cfg
 
 

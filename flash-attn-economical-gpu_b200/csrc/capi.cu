@@ -358,6 +358,38 @@ int fab_attention_fwd(const fab_attention_params* p, void* stream) {
   return attention_launch(launch_from_params(p), static_cast<cudaStream_t>(stream));
 }
 
+int fab_attention_fwd_variant(const fab_attention_params* p, int variant, void* stream) {
+  if (p == nullptr) return kErrInvalidArg;
+  if (variant == FAB_FA_VARIANT_TWO_TILES) return fab_attention_fwd(p, stream);
+  if (variant != FAB_FA_VARIANT_ONE_TILE) return kErrInvalidArg;
+  FaLaunch L = launch_from_params(p);
+  bool empty = false;
+  const int rc = attention_validate(L, &empty);
+  if (rc || empty) return rc;
+  // The split-KV tile family run as a single pass: one key range, no merge.
+  L.num_splits = 1;
+  L.split_len = L.N > 0 ? L.N : 1;
+  return fa_forward_split(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_config* out) {
+  if (out == nullptr) return kErrInvalidArg;
+  if (variant == FAB_FA_VARIANT_TWO_TILES) return fab_flash_attn_config(dtype, head_dim, out);
+  if (variant != FAB_FA_VARIANT_ONE_TILE) return kErrInvalidArg;
+  FaConfigInfo c;
+  const int rc = fa_select_split_config(dtype, head_dim, &c);
+  if (rc) return rc;
+  out->head_dim_padded = c.d_pad;
+  out->q_tiles_per_cta = c.nq;
+  out->block_n = c.bn;
+  out->stages = c.stages;
+  out->threads = c.threads;
+  out->smem_bytes = c.smem_bytes;
+  out->tmem_columns = c.tmem_cols;
+  out->s_buffers = c.s_bufs;
+  return kOk;
+}
+
 int fab_attention_fwd_varlen(const fab_attention_varlen_params* p, void* stream) {
   if (p == nullptr) return kErrInvalidArg;
   if (p->batch < 0 || p->total_q < 0 || p->total_k < 0 || p->max_seqlen_q < 0 || p->max_seqlen_k < 0)
@@ -534,6 +566,8 @@ int fab_kernel_attrs_query(int which, int dtype, int head_dim, fab_kernel_attrs*
   int regs = 0, smem = 0, threads = 0, rc;
   if (which == FAB_KERNEL_ATTENTION)
     rc = fa_kernel_attrs(dtype, head_dim, &regs, &smem, &threads);
+  else if (which == FAB_KERNEL_ATTENTION_ONE_TILE)
+    rc = fa_kernel_attrs(dtype, head_dim, &regs, &smem, &threads, true);
   else if (which == FAB_KERNEL_MATMUL)
     rc = gemm_kernel_attrs(dtype, &regs, &smem, &threads);
   else

@@ -882,15 +882,19 @@ int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 
-int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads) {
+int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile) {
   FaConfigInfo c;
-  int rc = fa_select_config(dtype, D, &c);
+  int rc = one_tile ? fa_select_split_config(dtype, D, &c) : fa_select_config(dtype, D, &c);
   if (rc) return rc;
   const int elt = dtype == kDtypeF32 ? 4 : 2;
   const void* k = nullptr;
 #define FAB_FA_ATTR(E, DP, NQ, BN, ST, SB) \
   if (elt == E && c.d_pad == DP) k = kernel_entry<E, DP, NQ, BN, ST, SB>(dtype);
-  FAB_FA_TABLE(FAB_FA_ATTR)
+  if (one_tile) {
+    FAB_FA_SPLIT_TABLE(FAB_FA_ATTR)
+  } else {
+    FAB_FA_TABLE(FAB_FA_ATTR)
+  }
 #undef FAB_FA_ATTR
   if (k == nullptr) return kErrUnsupported;
   cudaFuncAttributes a{};

@@ -127,7 +127,7 @@ int fa_select_split_config(int dtype, int D, FaConfigInfo* out);
 int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
 // Launches the split kernel and the combine kernel; L carries the plan.
 int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
-int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads);
+int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile = false);
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
 int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads);
 

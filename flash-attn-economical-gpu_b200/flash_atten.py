@@ -22,6 +22,7 @@ from dataclasses import dataclass
 import torch
 
 import _native
+import tune_table
 from tuner import FlashAttentionLaunchSpec
 
 logger = logging.getLogger(__name__)
@@ -99,6 +100,7 @@ def _launch_attention(
     entry: str = "general",
     num_splits: int = 0,
     workspace: torch.Tensor | None = None,
+    variant: int = 0,
 ) -> None:
     """Validate, conform and launch one attention forward through the C ABI.
 
@@ -108,6 +110,8 @@ def _launch_attention(
     `num_splits` 0 = one CTA per SM) or "general" (`fab_attention_fwd`,
     grouped-query heads) otherwise.  `workspace` (uint8, CUDA) is used for the
     split partials when it is large enough, else one is allocated.
+    `variant` 1 runs the one-query-tile family (`fab_attention_fwd_variant`)
+    instead of the default table, whatever `entry` names.
 
     q/o: [B, Hq, M, D]; k/v: [B, Hkv, N, D]; lse: [B, Hq, M] fp32 or None.
     """
@@ -143,11 +147,11 @@ def _launch_attention(
         lc = torch.empty_like(lse, memory_format=torch.contiguous_format)
     with torch.cuda.device(q.device):
         stream = ctypes.c_void_p(_native.current_stream_handle(q.device))
-        if entry == "nomask" and all(t.is_contiguous() for t in (qc, kc, vc, oc)):
+        if variant == 0 and entry == "nomask" and all(t.is_contiguous() for t in (qc, kc, vc, oc)):
             rc = _native.lib.fab_flash_attn_fwd_block_d_nomask_contiguous(
                 qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), oc.data_ptr(), B, Hq, M, N, D, sm_scale, dt, stream
             )
-        elif entry in ("basic", "optimize_shared_mem") and Hq == Hkv:
+        elif variant == 0 and entry in ("basic", "optimize_shared_mem") and Hq == Hkv:
             fn = (
                 _native.lib.fab_flash_attn_fwd_basic
                 if entry == "basic"
@@ -174,7 +178,9 @@ def _launch_attention(
             p.dtype = dt
             p.sm_scale = sm_scale
             p.causal = 1 if causal else 0
-            if entry == "splitkv":
+            if variant != 0:
+                rc = _native.lib.fab_attention_fwd_variant(ctypes.byref(p), int(variant), stream)
+            elif entry == "splitkv":
                 need = ctypes.c_size_t(0)
                 _native.check(_native.lib.fab_attention_fwd_splitkv_workspace(
                     ctypes.byref(p), int(num_splits), ctypes.byref(need), None), what)
@@ -192,14 +198,23 @@ def _launch_attention(
         lse.copy_(lc)
 
 
+def _compiled_info(q: torch.Tensor, D: int, variant: int) -> _CompiledKernelInfo:
+    """Resource facts of the compiled kernel a launch with this dtype, head dim and tile family runs."""
+    dt = _native.dtype_code(q.dtype)
+    which = _native.FAB_KERNEL_ATTENTION_ONE_TILE if variant else _native.FAB_KERNEL_ATTENTION
+    return _CompiledKernelInfo(_native.kernel_attrs(which, dt, D),
+                               int(_native.fa_config_variant(dt, D, variant).tmem_columns))
+
+
 class _StridedAttentionKernel:
     """Stands in for `_flash_attn_fwd_kernel_basic` / `_optimize_shared_mem` (Triton JITFunctions).
 
     Positional arguments (flash_atten.py:15-44): q, k, v, o, lse (tensor or 0),
     19 element strides, H, M, N, D, sm_scale.  Keyword arguments: causal,
     HAS_LSE and the Triton tiling knobs (BLOCK_*, num_warps, num_stages,
-    debug), which the sm_100a kernel does not need and ignores.  The batch
-    size is grid[1] // H, as in the Triton launch.
+    debug), which the sm_100a kernel does not need and ignores, plus
+    `sm100_variant` (0 or 1, the tile family a measured tuning chose).  The
+    batch size is grid[1] // H, as in the Triton launch.
     """
 
     def __init__(self, name: str):
@@ -245,15 +260,11 @@ class _StridedAttentionKernel:
                 raise ValueError(f"{self.__name__}: HAS_LSE=True needs an lse tensor")
             lv = _as_view(lse, (B, H, M), tuple(st[16:19]))
         entry = "basic" if self.__name__.endswith("_basic") else "optimize_shared_mem"
-        _launch_attention(qv, kv, vv, ov, lv, causal=causal, sm_scale=sm_scale, what=self.__name__, entry=entry)
+        _launch_attention(qv, kv, vv, ov, lv, causal=causal, sm_scale=sm_scale, what=self.__name__, entry=entry,
+                          variant=int(kwargs.get("sm100_variant", 0)))
 
     def warmup(self, *args, grid, **kwargs):
-        q = args[0]
-        D = int(args[27])
-        return _CompiledKernelInfo(
-            _native.kernel_attrs(_native.FAB_KERNEL_ATTENTION, _native.dtype_code(q.dtype), D),
-            int(_native.fa_config(_native.dtype_code(q.dtype), D).tmem_columns),
-        )
+        return _compiled_info(args[0], int(args[27]), int(kwargs.get("sm100_variant", 0)))
 
 
 class _ContiguousAttentionKernel(_StridedAttentionKernel):
@@ -287,15 +298,11 @@ class _ContiguousAttentionKernel(_StridedAttentionKernel):
             sm_scale=sm_scale,
             what=self.__name__,
             entry="nomask",
+            variant=int(kwargs.get("sm100_variant", 0)),
         )
 
     def warmup(self, *args, grid, **kwargs):
-        q = args[0]
-        D = int(args[7])
-        return _CompiledKernelInfo(
-            _native.kernel_attrs(_native.FAB_KERNEL_ATTENTION, _native.dtype_code(q.dtype), D),
-            int(_native.fa_config(_native.dtype_code(q.dtype), D).tmem_columns),
-        )
+        return _compiled_info(args[0], int(args[7]), int(kwargs.get("sm100_variant", 0)))
 
 
 _flash_attn_fwd_kernel_basic = _StridedAttentionKernel("_flash_attn_fwd_kernel_basic")
@@ -348,7 +355,12 @@ def attention_forward(
         sm_scale = q.shape[-1] ** -0.5
     o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=q.dtype)
     lse = torch.empty(q.shape[:3], device=q.device, dtype=torch.float32) if return_lse else None
-    _launch_attention(q, k, v, o, lse, causal=causal, sm_scale=sm_scale, what="attention_forward")
+    variant = 0
+    if q.dtype in (torch.float16, torch.bfloat16, torch.float32) and q.numel() and k.shape[2]:
+        # the tile family the shipped measurements favour for this shape
+        variant = tune_table.measured_variant(_native.dtype_code(q.dtype), q.shape[-1], causal,
+                                              q.shape[0] * q.shape[1], q.shape[2], k.shape[2])
+    _launch_attention(q, k, v, o, lse, causal=causal, sm_scale=sm_scale, what="attention_forward", variant=variant)
     return (o, lse) if return_lse else o
 
 

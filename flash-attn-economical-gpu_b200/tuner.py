@@ -11,11 +11,14 @@ allocation of `o` and fp32 `lse` (tuner.py:563-590).
 
 What differs is the search.  The reference compiles every Triton candidate
 tile and keeps the largest one that fits an SM (tuner.py:414-561).  On
-sm_100a the tile is fixed per (dtype, head_dim) by a static table inside the
-native library (`fab_flash_attn_config`): 128-row query tiles (two per CTA
-where TMEM allows), 64- or 128-key tiles, a 2-3 stage K/V ring.  That table
-entry is the single candidate; user tune arguments are validated exactly as
-the reference validates them and take part in the cache key, but the tile
+sm_100a two tile families are compiled per (dtype, head_dim) into the native
+library: two 128-row query tiles per CTA with one S buffer each (the default
+table, `fab_flash_attn_config`) and one query tile with two S buffers
+(`fab_flash_attn_config_variant`).  The candidates are those families; the
+choice is by measured time -- on the caller's tensors with
+`tune_by_time=True`, otherwise from the sweep shipped with the library
+(`tune_table.measured_variant`).  User tune arguments are validated exactly
+as the reference validates them and take part in the cache key; the tile
 reported in `FlashAttentionLaunchSpec.tune_args` is the one the kernel runs.
 """
 from __future__ import annotations
@@ -27,6 +30,7 @@ from dataclasses import dataclass
 import torch
 
 import _native
+import tune_table
 from exceptions import OutOfResourcesWithDetail, get_sm_resource_limits
 
 
@@ -130,6 +134,7 @@ class FlashAttentionTuner(Tuner):
         causal: bool,
         return_lse: bool,
         tune_args: FlashAttenTuneArguments | None = None,
+        tune_by_time: bool = False,
     ) -> None:
         if len(q_shape) != 4 or len(k_shape) != 4 or len(v_shape) != 4:
             raise ValueError("q_shape, k_shape, and v_shape must all be 4D")
@@ -146,6 +151,7 @@ class FlashAttentionTuner(Tuner):
         self.causal = causal
         self.return_lse = return_lse
         self.tune_args = tune_args or FlashAttenTuneArguments()
+        self.tune_by_time = bool(tune_by_time)
         self.B, self.H, self.M, self.D = self.q_shape
         _, _, self.N, _ = self.k_shape
         if (
@@ -180,6 +186,7 @@ class FlashAttentionTuner(Tuner):
             self.tune_args.BLOCK_DMODEL,
             self.tune_args.NUM_WARPS,
             self.tune_args.NUM_STAGES,
+            self.tune_by_time,
         )
 
     def _allow_block_dmodel_smaller_than_d(self) -> bool:
@@ -200,8 +207,9 @@ class FlashAttentionTuner(Tuner):
         """Q tile + one K and one V tile, the reference's estimate (tuner.py:237-245)."""
         return element_size * block_dmodel * (block_m + 2 * block_n_pad)
 
-    def _config_from_entry(self, cfg: _native.FabFaConfig) -> dict[str, int | bool]:
+    def _config_from_entry(self, cfg: _native.FabFaConfig, variant: int = 0) -> dict[str, int | bool]:
         return {
+            "variant": int(variant),
             "BLOCK_M": 128 * int(cfg.q_tiles_per_cta),
             "BLOCK_N": int(cfg.block_n),
             "BLOCK_N_PAD": int(cfg.block_n),
@@ -214,11 +222,29 @@ class FlashAttentionTuner(Tuner):
         }
 
     def _candidate_configs(self, dtype_code: int | None = None) -> list[dict[str, int | bool]]:
-        """The sm_100a table entry for this shape, or nothing if the head dim is out of range."""
+        """The compiled tile families that cover this head dim (default family first); empty if none does."""
         if dtype_code is None:
             dtype_code = _native.FAB_DTYPE_F16 if self.dtype_size == 2 else _native.FAB_DTYPE_F32
-        cfg = self._table_entry(dtype_code)
-        return [] if cfg is None else [self._config_from_entry(cfg)]
+        if self._table_entry(dtype_code) is None:
+            return []
+        return [self._config_from_entry(_native.fa_config_variant(dtype_code, self.D, variant), variant)
+                for variant in tune_table.candidate_variants(dtype_code, self.D)]
+
+    def _effective_causal(self) -> bool:
+        return self.causal
+
+    def _choose(self, candidates, q, k, v, sm_scale) -> dict[str, int | bool]:
+        """The candidate with the least measured time: timed here, or from the shipped sweep."""
+        if len(candidates) == 1:
+            return candidates[0]
+        if self.tune_by_time:
+            times = tune_table.time_variants(q, k, v, causal=self._effective_causal(), sm_scale=sm_scale,
+                                             variants=[int(c["variant"]) for c in candidates])
+            best = min(times, key=times.get)
+        else:
+            best = tune_table.measured_variant(_native.dtype_code(q.dtype), self.D, self._effective_causal(),
+                                               self.B * self.H, self.M, self.N)
+        return next((c for c in candidates if int(c["variant"]) == best), candidates[0])
 
     # ------------------------------------------------------- launch building
     def _kernel(self):
@@ -285,6 +311,7 @@ class FlashAttentionTuner(Tuner):
             "BLOCK_DMODEL": int(config["BLOCK_DMODEL"]),
             "num_warps": int(config["num_warps"]),
             "num_stages": int(config["num_stages"]),
+            "sm100_variant": int(config.get("variant", 0)),
         }
         if launch_context is None:
             launch_context = self.build_compiling_context(
@@ -388,7 +415,7 @@ class FlashAttentionTuner(Tuner):
                 launch_context=context,
                 extra_detail=f"No sm_100a attention tile covers head_dim={self.D} for dtype {q.dtype}",
             )
-        config = candidates[0]
+        config = self._choose(candidates, q, k, v, sm_scale)
         feasible, spec = self.evaluate_candidate(q, k, v, sm_scale=sm_scale, o=o, lse=lse, config=config)
         if not feasible:
             ctx = spec.launch_context
@@ -445,6 +472,9 @@ class FlashAttentionBlockDNomaskTuner(FlashAttentionTuner):
     def _allow_block_dmodel_smaller_than_d(self) -> bool:
         return True
 
+    def _effective_causal(self) -> bool:
+        return False  # the kernel takes no causal flag
+
     def _block_dmodel_outer_candidates(self) -> list[int]:
         if self.tune_args.BLOCK_DMODEL_OUTER is not None:
             return [self.tune_args.BLOCK_DMODEL_OUTER]
@@ -482,6 +512,7 @@ class FlashAttentionBlockDNomaskTuner(FlashAttentionTuner):
             "BLOCK_DMODEL_OUTER": int(config["BLOCK_DMODEL_OUTER"]),
             "num_warps": int(config["num_warps"]),
             "num_stages": int(config["num_stages"]),
+            "sm100_variant": int(config.get("variant", 0)),
         }
         if launch_context is None:
             launch_context = self.build_compiling_context(

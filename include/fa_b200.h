@@ -239,12 +239,28 @@ typedef struct fab_fa_config {
 int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out);
 
 /*
+ * Tile families for fab_attention_fwd_variant / fab_flash_attn_config_variant.
+ * TWO_TILES is the table fab_attention_fwd uses (two 128-row query tiles per
+ * CTA where TMEM allows, one S buffer each); ONE_TILE is one 128-row query
+ * tile with two S buffers (more CTAs for the same rows: better for short or
+ * few sequences).  Which is faster depends on the shape; the Python tuner
+ * picks by measured time (the reference picks the largest tile that fits,
+ * tuner.py:503-517).
+ */
+#define FAB_FA_VARIANT_TWO_TILES 0
+#define FAB_FA_VARIANT_ONE_TILE 1
+
+int fab_attention_fwd_variant(const fab_attention_params* params, int variant, void* stream);
+int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_config* out);
+
+/*
  * Compiled-kernel facts that replace Triton's `kernel.warmup(...)` metadata
  * (tuner.py:355-368: metadata.shared, metadata.num_warps, n_regs).
  * which: 0 = attention kernel for (dtype, head_dim), 1 = matmul kernel for dtype.
  */
 #define FAB_KERNEL_ATTENTION 0
 #define FAB_KERNEL_MATMUL 1
+#define FAB_KERNEL_ATTENTION_ONE_TILE 2 /* the FAB_FA_VARIANT_ONE_TILE attention family */
 typedef struct fab_kernel_attrs {
   int registers_per_thread;
   int shared_bytes;

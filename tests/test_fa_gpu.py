@@ -315,3 +315,41 @@ def test_config3_gqa_full_size_sampled(cuda_device):
     v = torch.randn(B, Hkv, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16)
     o = attention_forward(q, k, v, causal=True)
     _sampled_rows_check(q, k, v, o, True, torch.bfloat16, [(0, 3, 0, 128), (1, 12, 6000, 6128), (1, 15, 8064, 8192)])
+
+
+# ----------------------------------------------- the second compiled tile family
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+@pytest.mark.parametrize("shape, dtype", [((1, 2, 2, 257, 300, 64), torch.bfloat16),
+                                          ((2, 4, 2, 384, 200, 128), torch.float16),
+                                          ((1, 2, 2, 129, 513, 128), torch.bfloat16),
+                                          ((1, 2, 2, 150, 130, 64), torch.float32),
+                                          ((1, 2, 2, 100, 33, 80), torch.bfloat16)],
+                         ids=lambda x: "B{}H{}/{}M{}N{}D{}".format(*x) if isinstance(x, tuple) else str(x)[6:])
+def test_one_tile_family_matches_oracle(shape, dtype, causal, cuda_device):
+    """FAB_FA_VARIANT_ONE_TILE (one query tile, two S buffers) through the reference-named launcher."""
+    q, k, v, qd, kd, vd = _inputs(shape, dtype, seed=zlib.crc32(repr(("one", shape, str(dtype), causal)).encode()),
+                                  dev=cuda_device)
+    B, Hq, M, D = q.shape
+    o = torch.empty_like(qd)
+    lse = torch.empty(B, Hq, M, device=cuda_device, dtype=torch.float32)
+    if Hq == k.shape[1]:
+        args = (qd, kd, vd, o, lse, *qd.stride(), *kd.stride(), *vd.stride(), *o.stride(), *lse.stride(), Hq, M,
+                k.shape[2], D, D ** -0.5)
+        flash_atten._flash_attn_fwd_kernel_basic[(1, B * Hq)](*args, causal=causal, HAS_LSE=True, sm100_variant=1)
+    else:
+        flash_atten._launch_attention(qd, kd, vd, o, lse, causal=causal, sm_scale=D ** -0.5, what="test", variant=1)
+    ro, rl = _oracle(q, k, v, causal, dtype)
+    _close(o, ro)
+    _close(lse, rl, rtol=1e-3 if dtype == torch.float32 else 1e-4, atol=1e-2 if dtype == torch.float32 else LSE_ATOL)
+
+
+def test_tuner_times_both_families(cuda_device):
+    """tune_by_time=True measures the compiled families on the caller's tensors and launches the faster."""
+    _, _, _, qd, kd, vd = _inputs((1, 4, 4, 512, 512, 128), torch.bfloat16, seed=61, dev=cuda_device)
+    spec = FlashAttentionTuner(tuple(qd.shape), tuple(kd.shape), tuple(vd.shape), 2, causal=True, return_lse=False,
+                               tune_by_time=True).build_flash_attention_launch_spec(qd, kd, vd)
+    assert spec.kernel_kwargs["sm100_variant"] in (0, 1)
+    assert spec.tune_args.BLOCK_M == (256 if spec.kernel_kwargs["sm100_variant"] == 0 else 128)
+    o = flash_attention(spec)
+    ro, _ = _oracle(qd.cpu(), kd.cpu(), vd.cpu(), True, torch.bfloat16)
+    _close(o, ro)

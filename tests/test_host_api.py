@@ -74,11 +74,14 @@ def test_tuner_shape_validation(fake_limits):
                                     tune_args=FlashAttenTuneArguments(BLOCK_DMODEL=32))
 
 
-def test_tuner_candidates_come_from_the_sm100_table(fake_limits):
+def test_tuner_candidates_are_the_compiled_tile_families(fake_limits):
     t = FlashAttentionTuner((4, 32, 8192, 128), (4, 32, 8192, 128), (4, 32, 8192, 128), 2, causal=True, return_lse=False)
-    (cfg,) = t._candidate_configs()
-    assert cfg["BLOCK_M"] == 256 and cfg["BLOCK_N"] == 128 and cfg["BLOCK_DMODEL"] == 128
-    assert cfg["num_warps"] == 12 and cfg["num_stages"] == 2
+    two, one = t._candidate_configs()
+    assert two["variant"] == 0 and one["variant"] == 1
+    assert two["BLOCK_M"] == 256 and two["BLOCK_N"] == 128 and two["BLOCK_DMODEL"] == 128
+    assert two["num_warps"] == 12 and two["num_stages"] == 2
+    assert one["BLOCK_M"] == 128 and one["BLOCK_N"] == 128 and one["num_warps"] == 8
+    # D=256: both families name the same tile, so it is the only candidate
     t256 = FlashAttentionOptimizeSharedMemTuner((2, 16, 64, 256), (2, 16, 64, 256), (2, 16, 64, 256), 2,
                                                 causal=True, return_lse=False)
     (cfg,) = t256._candidate_configs()
@@ -209,3 +212,28 @@ def test_resource_usage_summary_format():
     assert s.startswith("k tuner resources: \nshared=197728/232448 bytes per block/SM, ")
     assert "registers=64512/65536 per block/SM" in s
     assert "tune_args=BLOCK_M=256" in s and "input_shapes=q=(1, 2, 3, 4)" in s
+
+
+def test_measured_variant_lookup(tmp_path):
+    """Nearest measured shape with the same dtype width, padded head dim and causality decides; shapes with
+    nothing measured, or head dims with a single family, get the default family."""
+    import json
+
+    import _native
+    import tune_table
+
+    table = tmp_path / "t.json"
+    entries = [
+        {"width": 2, "head_dim_padded": 128, "causal": False, "batch_heads": 8, "seqlen_q": 512, "seqlen_k": 512,
+         "ms": {"0": 0.02, "1": 0.015}, "best_variant": 1},
+        {"width": 2, "head_dim_padded": 128, "causal": False, "batch_heads": 128, "seqlen_q": 8192,
+         "seqlen_k": 8192, "ms": {"0": 3.6, "1": 4.3}, "best_variant": 0},
+    ]
+    table.write_text(json.dumps({"entries": entries}))
+    bf16 = _native.FAB_DTYPE_BF16
+    assert tune_table.measured_variant(bf16, 128, False, 8, 600, 600, path=table) == 1
+    assert tune_table.measured_variant(bf16, 128, False, 128, 4096, 4096, path=table) == 0
+    assert tune_table.measured_variant(bf16, 96, False, 8, 600, 600, path=table) == 1  # pads to 128
+    assert tune_table.measured_variant(bf16, 128, True, 8, 600, 600, path=table) == 0  # nothing causal measured
+    assert tune_table.measured_variant(bf16, 256, False, 8, 600, 600, path=table) == 0  # one family only
+    assert tune_table.measured_variant(bf16, 128, False, 8, 600, 600, path=tmp_path / "missing.json") == 0
