@@ -59,6 +59,12 @@ WORKLOADS = {
     "fa_gqa_s8192_causal": (2, 16, 4, 8192, 128, True),
 }
 GEMM_WORKLOADS = {"gemm_8192": 8192, "gemm_16384": 16384, "gemm_4096": 4096}
+# Split-KV decode steps (not a BASELINE config; K/V cache resident on the device):
+# name: (B, Hq, Hkv, query rows, keys, D)
+DECODE_WORKLOADS = {
+    "decode_n131072": (1, 28, 4, 1, 131072, 128),
+    "decode_n32768_b8": (8, 28, 4, 1, 32768, 128),
+}
 
 
 def attention_flops(B, H, S, D, causal):
@@ -249,6 +255,16 @@ def cpu_attention_sample(S, D, causal, target_s=10.0, max_heads=64):
     }
 
 
+def measured_hbm_gbs():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
 def peaks_entry(achieved_tflops, workload):
     burst, sustained, source = measured_peaks()
     traffic = committed_traffic(workload)
@@ -411,6 +427,128 @@ def run_attention(args, world, rank, local):
         cpu.pop("seconds", None)
         result["cpu_baseline"] = cpu
     return result
+
+
+# ---------------------------------------------------------------- decode
+def run_decode(args, world, rank, local):
+    """Split-KV decode step: one query row per head against a long resident K/V cache (HBM-bound)."""
+    import _native
+    from flash_atten import attention_forward_splitkv, splitkv_workspace_bytes
+
+    B, Hq, Hkv, M, N, D = DECODE_WORKLOADS[args.workload]
+    dev = torch.device("cuda", local)
+    dtype = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    q = torch.randn(B, Hq, M, D, generator=g, device=dev, dtype=dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g, device=dev, dtype=dtype)
+    v = torch.randn(B, Hkv, N, D, generator=g, device=dev, dtype=dtype)
+    o = torch.empty_like(q)
+    need, splits = splitkv_workspace_bytes(tuple(q.shape), tuple(k.shape), dtype)
+    ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+    kv_bytes = 2 * k.numel() * k.element_size()
+    algo_bytes = kv_bytes + 2 * q.numel() * q.element_size()  # K, V read once; q read, o written
+    stream = torch.cuda.current_stream(dev)
+
+    def step(qq):
+        return attention_forward_splitkv(qq, k, v, out=o, workspace=ws)
+
+    for _ in range(args.warmup):
+        step(q)
+    torch.cuda.synchronize(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step(q)
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    elapsed_ms = max_over_ranks(t0.elapsed_time(t1), world)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends))
+    if _native.device_error():
+        raise RuntimeError("device error during the timed region")
+    value = sum_over_ranks(algo_bytes * args.steps, world) / (elapsed_ms / 1e3) / 1e9
+
+    # e2e: each step's new query rows come from pinned host memory and its output goes back
+    qh = q.cpu().pin_memory()
+    oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    for _ in range(2):
+        oh.copy_(step(qh.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        oh.copy_(step(qh.to(dev, non_blocking=True)), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = sum_over_ranks(algo_bytes * args.steps, world) / (e2e_ms / 1e3) / 1e9
+
+    comparators = {}
+    if rank == 0 and not args.no_compare:
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        for name, be in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+            try:
+                with sdpa_kernel([be]):
+                    for _ in range(3):
+                        F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+                    torch.cuda.synchronize(dev)
+                    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    c0.record(stream)
+                    for _ in range(20):
+                        F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+                    c1.record(stream)
+                    torch.cuda.synchronize(dev)
+                comparators[name + "_gbs"] = round(algo_bytes * 20 / (c0.elapsed_time(c1) / 1e3) / 1e9, 1)
+            except Exception as exc:
+                comparators[name + "_gbs"] = f"unavailable: {type(exc).__name__}"
+    peak, source = measured_hbm_gbs()
+    achieved = algo_bytes / (launch_ms / 1e3) / 1e9
+    return {
+        "metric": "split-KV decode attention, K/V cache bytes read per second",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q and K/V cache per rank",
+        "config": {
+            "workload": f"decode step B{B} Hq{Hq} Hkv{Hkv} {M} query row(s) against {N} cached keys D{D} bf16 "
+                        f"per GPU, {splits} key splits",
+            "global_batch": B * world,
+            "seq_len": N,
+            "parallelism": f"dp{world} (no collective)",
+            "l2_policy": f"K/V cache {kv_bytes / 1e6:.0f} MB per step > 126 MB L2; no flush",
+        },
+        "e2e": {
+            "value": round(e2e_value, 1),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": q.numel() * q.element_size(),
+            "d2h_bytes_per_step": o.numel() * o.element_size(),
+            "api": "flash_atten.attention_forward_splitkv with the query rows copied from pinned host memory and "
+                   "the output copied back each step (the K/V cache stays resident)",
+        },
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{source} HBM copy bandwidth",
+                     "traffic": committed_traffic(args.workload)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+        "comparators": comparators,
+    }
 
 
 # ------------------------------------------------------------------- ttft
@@ -580,7 +718,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fa_s8192_noncausal", choices=sorted(WORKLOADS) + sorted(GEMM_WORKLOADS))
+    ap.add_argument("--workload", default="fa_s8192_noncausal",
+                    choices=sorted(WORKLOADS) + sorted(GEMM_WORKLOADS) + sorted(DECODE_WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch comparators")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
@@ -601,6 +740,8 @@ def main():
     try:
         if args.workload in GEMM_WORKLOADS:
             result = run_gemm(args, world, rank, local)
+        elif args.workload in DECODE_WORKLOADS:
+            result = run_decode(args, world, rank, local)
         else:
             result = run_attention(args, world, rank, local)
             torch.cuda.empty_cache()

@@ -664,39 +664,58 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
 
 // Merges the key splits of every output row: with split s holding the
 // normalised O_s and LSE_s of its keys, O = sum_s w_s O_s / sum_s w_s and
-// LSE = max + log(sum_s w_s), w_s = exp(LSE_s - max).  One warp per row.
+// LSE = max + log(sum_s w_s), w_s = exp(LSE_s - max).  One CTA per row: the
+// weights are computed once, one split per thread, into shared memory; then
+// each of the eight warps adds every eighth split's O_s (several loads in
+// flight per warp) and the warps' sums meet in shared memory.
+constexpr int kCombineWarps = 8;
+constexpr int kCombineSmemSplits = 1024;  // more splits recompute their weight from the LSE
+
 template <typename T>
-__global__ void __launch_bounds__(128) fa_split_combine_kernel(const float* __restrict__ o_part,
-                                                               const float* __restrict__ lse_part, T* o, float* lse,
-                                                               int64_t o_sb, int64_t o_sh, int64_t o_sm, int64_t l_sb,
-                                                               int64_t l_sh, int64_t l_sm, int Hq, int M, int D,
-                                                               int splits, int64_t rows) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+__global__ void __launch_bounds__(kCombineWarps * 32) fa_split_combine_kernel(
+    const float* __restrict__ o_part, const float* __restrict__ lse_part, T* o, float* lse, int64_t o_sb,
+    int64_t o_sh, int64_t o_sm, int64_t l_sb, int64_t l_sh, int64_t l_sm, int Hq, int M, int D, int splits,
+    int64_t rows) {
+  constexpr int kMaxPerLane = 8;  // head dims up to 256
+  __shared__ float s_red[kCombineWarps];
+  __shared__ float s_w[kCombineSmemSplits];
+  __shared__ float s_acc[kCombineWarps][kMaxPerLane * 32];
+  const int64_t row = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
   const int m = static_cast<int>(row % M);
   const int h = static_cast<int>((row / M) % Hq);
   const int64_t b = row / (static_cast<int64_t>(M) * Hq);
   T* orow = o + b * o_sb + h * o_sh + m * o_sm;
+
   float mx = -INFINITY;
-  for (int sp = lane; sp < splits; sp += 32) mx = fmaxf(mx, lse_part[sp * rows + row]);
+  for (int sp = threadIdx.x; sp < splits; sp += blockDim.x) mx = fmaxf(mx, lse_part[sp * rows + row]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) s_red[warp] = mx;
+  __syncthreads();
+  mx = s_red[0];
+#pragma unroll
+  for (int w = 1; w < kCombineWarps; ++w) mx = fmaxf(mx, s_red[w]);
   if (mx == -INFINITY) {
     // No split saw a key: 0/0 like the single-pass kernel.
-    for (int d = lane; d < D; d += 32) orow[d] = static_cast<T>(NAN);
-    if (lse != nullptr && lane == 0) lse[b * l_sb + h * l_sh + m * l_sm] = -INFINITY;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) orow[d] = static_cast<T>(NAN);
+    if (lse != nullptr && threadIdx.x == 0) lse[b * l_sb + h * l_sh + m * l_sm] = -INFINITY;
     return;
   }
-  constexpr int kMaxPerLane = 8;  // head dims up to 256
+  auto weight = [&](int sp) {
+    const float ls = lse_part[sp * rows + row];
+    return ls == -INFINITY ? 0.f : expf(ls - mx);  // an empty split carries zeros
+  };
+  for (int sp = threadIdx.x; sp < min(splits, kCombineSmemSplits); sp += blockDim.x) s_w[sp] = weight(sp);
+  __syncthreads();
   float acc[kMaxPerLane];
 #pragma unroll
   for (int e = 0; e < kMaxPerLane; ++e) acc[e] = 0.f;
   float wsum = 0.f;
-  for (int sp = 0; sp < splits; ++sp) {
-    const float ls = lse_part[sp * rows + row];
-    if (ls == -INFINITY) continue;
-    const float w = expf(ls - mx);
+#pragma unroll 4
+  for (int sp = warp; sp < splits; sp += kCombineWarps) {
+    const float w = sp < kCombineSmemSplits ? s_w[sp] : weight(sp);
     wsum += w;
     const float* src = o_part + (sp * rows + row) * D;
 #pragma unroll
@@ -705,13 +724,22 @@ __global__ void __launch_bounds__(128) fa_split_combine_kernel(const float* __re
       if (d < D) acc[e] = fmaf(w, src[d], acc[e]);
     }
   }
-  const float inv = 1.f / wsum;
+  __syncthreads();  // every warp is done with s_red before it is reused for the weight sums
 #pragma unroll
-  for (int e = 0; e < kMaxPerLane; ++e) {
-    const int d = lane + 32 * e;
-    if (d < D) orow[d] = static_cast<T>(acc[e] * inv);
+  for (int e = 0; e < kMaxPerLane; ++e) s_acc[warp][lane + 32 * e] = acc[e];
+  if (lane == 0) s_red[warp] = wsum;
+  __syncthreads();
+  float total_w = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCombineWarps; ++w) total_w += s_red[w];
+  const float inv = 1.f / total_w;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) sum += s_acc[w][d];
+    orow[d] = static_cast<T>(sum * inv);
   }
-  if (lse != nullptr && lane == 0) lse[b * l_sb + h * l_sh + m * l_sm] = mx + logf(wsum);
+  if (lse != nullptr && threadIdx.x == 0) lse[b * l_sb + h * l_sh + m * l_sm] = mx + logf(total_w);
 }
 
 // The sm_100a tile table: one instantiation per (element size, padded head dim).
@@ -863,19 +891,19 @@ int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
 #undef FAB_FA_SLAUNCH
   if (rc || L.num_splits <= 1 || L.o_part == nullptr) return rc;
   const int64_t rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
-  const long long blocks = (rows + 3) / 4;
+  const long long blocks = rows;  // one CTA per output row
   if (blocks > 0x7fffffffLL) return kErrInvalidArg;
   const unsigned g = static_cast<unsigned>(blocks);
   if (L.dtype == kDtypeBF16) {
-    fa_split_combine_kernel<__nv_bfloat16><<<g, 128, 0, stream>>>(
+    fa_split_combine_kernel<__nv_bfloat16><<<g, kCombineWarps * 32, 0, stream>>>(
         L.o_part, L.lse_part, static_cast<__nv_bfloat16*>(L.o), L.lse, L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss,
         L.Hq, L.M, L.D, L.num_splits, rows);
   } else if (L.dtype == kDtypeF16) {
-    fa_split_combine_kernel<__half><<<g, 128, 0, stream>>>(L.o_part, L.lse_part, static_cast<__half*>(L.o), L.lse,
+    fa_split_combine_kernel<__half><<<g, kCombineWarps * 32, 0, stream>>>(L.o_part, L.lse_part, static_cast<__half*>(L.o), L.lse,
                                                            L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss, L.Hq, L.M,
                                                            L.D, L.num_splits, rows);
   } else {
-    fa_split_combine_kernel<float><<<g, 128, 0, stream>>>(L.o_part, L.lse_part, static_cast<float*>(L.o), L.lse,
+    fa_split_combine_kernel<float><<<g, kCombineWarps * 32, 0, stream>>>(L.o_part, L.lse_part, static_cast<float*>(L.o), L.lse,
                                                           L.o_sb, L.o_sh, L.o_ss, L.l_sb, L.l_sh, L.l_ss, L.Hq, L.M,
                                                           L.D, L.num_splits, rows);
   }
