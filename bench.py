@@ -571,6 +571,15 @@ def run_ttft(args, world, rank, local):
         "ours_attention_cublas_gemm": ttft.Backends(attention="native", gemm="cublas"),
         "torch_cudnn_sdpa_cublas": ttft.Backends(attention="cudnn", gemm="cublas"),
     }
+    fused = None
+    if world > 1:
+        # o_proj / down_proj GEMMs fused with their all-reduce over NVLink peer memory
+        import _native
+        from tp_allreduce import FusedGemmAllReduce
+
+        fused = FusedGemmAllReduce(None, max_rows=max(args.ttft_lengths), cols=arch.hidden_size,
+                                   dtype=torch.bfloat16, device=dev)
+        builds["ours_fused_allreduce"] = ttft.Backends(attention="native", gemm="native", fused_allreduce=fused)
     for S in args.ttft_lengths:
         ids = ttft._make_random_input_ids(S, arch.vocab_size, dev, seed=S)
         row = {}
@@ -580,7 +589,21 @@ def run_ttft(args, world, rank, local):
                 row[name] = round(statistics.median(samples), 2)
             except Exception as exc:
                 row[name] = f"unavailable: {type(exc).__name__}: {str(exc)[:80]}"
+            if be.fused_allreduce is not None:
+                # every rank learns whether any rank's fused call gave up on a bounded wait
+                import torch.distributed as dist
+
+                err = torch.tensor([float(_native.device_error())], device=dev)
+                dist.all_reduce(err, op=dist.ReduceOp.MAX)
+                if err.item():
+                    row[name] = "unavailable: a fused all-reduce wait timed out"
+                    del builds[name]
+                    break
         out[f"prompt_{S}"] = row
+    if fused is not None:
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        fused.close()
     del shard
     torch.cuda.empty_cache()
     return out

@@ -80,6 +80,18 @@ class FabAttentionVarlenParams(ctypes.Structure):
     ]
 
 
+MAX_TP_RANKS = 8
+
+
+class FabGemmAllreduceParams(ctypes.Structure):
+    _fields_ = [
+        ("a", _vp), ("b", _vp),
+        ("lda", _i64), ("ldb", _i64), ("ldo", _i64),
+        ("M", _i32), ("N", _i32), ("K", _i32), ("in_dtype", _i32), ("world", _i32), ("rank", _i32),
+        ("inbox", _vp * MAX_TP_RANKS), ("out", _vp * MAX_TP_RANKS), ("counters", _vp * MAX_TP_RANKS),
+    ]
+
+
 class FabFaConfig(ctypes.Structure):
     _fields_ = [
         ("head_dim_padded", _i32), ("q_tiles_per_cta", _i32), ("block_n", _i32), ("stages", _i32),
@@ -115,6 +127,12 @@ PROTOTYPES = {
     "fab_attention_fwd_splitkv_static": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
     "fab_matmul_contiguous": (_i32, [_vp] * 3 + [_i32] * 6 + [_vp]),
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
+    "fab_gemm_allreduce_layout": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_size_t),
+                                         ctypes.POINTER(ctypes.c_size_t)]),
+    "fab_gemm_allreduce": (_i32, [ctypes.POINTER(FabGemmAllreduceParams), _vp]),
+    "fab_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),
+    "fab_ipc_import": (_i32, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "fab_ipc_close": (_i32, [_vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),
     "fab_kernel_attrs_query": (_i32, [_i32, _i32, _i32, ctypes.POINTER(FabKernelAttrs)]),
     "fab_device_limits_query": (_i32, [_i32, ctypes.POINTER(FabDeviceLimits)]),

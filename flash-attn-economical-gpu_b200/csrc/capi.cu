@@ -6,6 +6,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -524,6 +525,107 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   L.round_f16 = p->round_f16;
   L.group_m = p->group_m;
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_gemm_allreduce_layout(int M, int N, int world, int* tiles_per_owner, size_t* inbox_bytes,
+                              size_t* counter_bytes) {
+  if (M <= 0 || N <= 0 || world < 1 || world > kMaxTpRanks || tiles_per_owner == nullptr || inbox_bytes == nullptr ||
+      counter_bytes == nullptr)
+    return kErrInvalidArg;
+  const int tiles = gemm_ar_tiles(M, N);
+  const int per_owner = (tiles + world - 1) / world;
+  *tiles_per_owner = per_owner;
+  *inbox_bytes = static_cast<size_t>(world) * per_owner * 128 * 256 * 2;
+  *counter_bytes = (static_cast<size_t>(per_owner) + 1) * sizeof(unsigned long long);
+  return kOk;
+}
+
+int fab_gemm_allreduce(const fab_gemm_allreduce_params* p, void* stream) {
+  if (p == nullptr) return kErrInvalidArg;
+  if (p->world < 1 || p->world > kMaxTpRanks || p->rank < 0 || p->rank >= p->world) return kErrInvalidArg;
+  if (p->in_dtype != FAB_DTYPE_BF16 && p->in_dtype != FAB_DTYPE_F16) return kErrUnsupported;
+  if (p->M <= 0 || p->N <= 0 || p->K <= 0 || p->lda < p->K || p->ldb < p->N || p->ldo < p->N) return kErrInvalidArg;
+  if ((p->N * 2) % 16 != 0 || (p->ldo * 2) % 16 != 0) return kErrInvalidArg;
+  int per_owner = 0;
+  size_t inbox_bytes = 0, counter_bytes = 0;
+  int rc = fab_gemm_allreduce_layout(p->M, p->N, p->world, &per_owner, &inbox_bytes, &counter_bytes);
+  if (rc) return rc;
+  GemmArParams ar{};
+  for (int r = 0; r < p->world; ++r) {
+    if (p->inbox[r] == nullptr || p->out[r] == nullptr || p->counters[r] == nullptr) return kErrInvalidArg;
+    if ((reinterpret_cast<uintptr_t>(p->inbox[r]) & 15u) || (reinterpret_cast<uintptr_t>(p->out[r]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(p->counters[r]) & 7u))
+      return kErrInvalidArg;
+    ar.inbox[r] = p->inbox[r];
+    ar.out[r] = p->out[r];
+    // counters: [tiles_per_owner] arrivals, then the done counter
+    ar.arrive[r] = static_cast<unsigned long long*>(p->counters[r]);
+    ar.done[r] = static_cast<unsigned long long*>(p->counters[r]) + per_owner;
+  }
+  ar.ldo = p->ldo;
+  ar.world = p->world;
+  ar.rank = p->rank;
+  ar.tiles_per_owner = per_owner;
+  GemmLaunch L{};
+  L.a = p->a;
+  L.b = p->b;
+  L.c = p->out[p->rank];
+  L.lda = p->lda;
+  L.ldb = p->ldb;
+  L.ldc = p->ldo;
+  L.M = p->M;
+  L.N = p->N;
+  L.K = p->K;
+  L.in_dtype = L.out_dtype = p->in_dtype;
+  L.group_m = 8;
+  return gemm_allreduce(L, ar, static_cast<cudaStream_t>(stream));
+}
+
+// Peer memory: export a device pointer so another process can map it, and
+// map / unmap what a peer exported.  Handles are cudaIpcMemHandle_t bytes.
+static int ipc_base(const void* ptr, void** base, size_t* offset) {
+  static PFN_cuMemGetAddressRange_v3020 get_range = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  }();
+  if (get_range == nullptr) return kErrCuda;
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  if (get_range(&b, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return kErrInvalidArg;
+  *base = reinterpret_cast<void*>(b);
+  *offset = static_cast<size_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(b));
+  return kOk;
+}
+
+int fab_ipc_export(const void* ptr, void* handle, size_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return kErrInvalidArg;
+  void* base = nullptr;
+  int rc = ipc_base(ptr, &base, offset);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, base) != cudaSuccess) return kErrCuda;
+  memcpy(handle, &h, sizeof(h));
+  return kOk;
+}
+
+int fab_ipc_import(const void* handle, size_t offset, void** base, void** ptr) {
+  if (handle == nullptr || base == nullptr || ptr == nullptr) return kErrInvalidArg;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  if (cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return kErrCuda;
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return kOk;
+}
+
+int fab_ipc_close(void* base) {
+  if (base == nullptr) return kErrInvalidArg;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? kOk : kErrCuda;
 }
 
 int fab_matmul_contiguous(const void* a, const void* b, void* c, int M, int N, int K, int in_dtype, int out_dtype,

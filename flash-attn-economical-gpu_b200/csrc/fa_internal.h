@@ -109,6 +109,20 @@ struct GemmKernelParams {
   int round_f16;
 };
 
+// Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output
+// projections).  Pointers index by rank; this rank's own entries are local.
+constexpr int kMaxTpRanks = 8;
+struct GemmArParams {
+  void* inbox[kMaxTpRanks];                 // [world][tiles_per_owner][128][256] partial tiles, per rank
+  void* out[kMaxTpRanks];                   // [M][ldo] reduced output, per rank
+  unsigned long long* arrive[kMaxTpRanks];  // [tiles_per_owner] partial-tile arrivals, per rank
+  unsigned long long* done[kMaxTpRanks];    // reduced tiles landed, one counter per rank
+  int64_t ldo;
+  int world;
+  int rank;
+  int tiles_per_owner;
+};
+
 struct GemmLaunch {
   const void* a;
   const void* b;
@@ -129,6 +143,9 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
 int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile = false);
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
+// Output tiles of the fused GEMM + all-reduce: tile t belongs to rank t % world.
+int gemm_ar_tiles(int M, int N);
+int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t stream);
 int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads);
 
 // Helpers implemented in capi.cu.

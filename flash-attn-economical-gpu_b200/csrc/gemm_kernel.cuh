@@ -11,6 +11,25 @@
 // tcgen05.mma (M=128, N=256) into a double-buffered TMEM accumulator, and a
 // 128-thread epilogue that drains one accumulator while the next tile's main
 // loop runs.
+//
+// With kAR the same kernel also all-reduces C over the ranks of a
+// tensor-parallel group through NVLink peer memory (GemmArParams):
+//   1. each finished partial tile is stored straight into the inbox of the
+//      rank that owns it (tile t -> rank t % world) and counted there with a
+//      system-scope release, while the next tile's MMAs run;
+//   2. after its last tile every CTA takes the tiles its rank owns, waits
+//      (bounded) until all ranks' partials are in, sums them in fp32 and
+//      writes the result into every rank's output buffer, then counts it in
+//      each rank's done counter;
+//   3. CTA 0 waits (bounded) until every tile of C has landed locally.
+// Each counter is reset to zero by the one thread that waits on it, once it
+// has seen the count it waits for; no rank can add to it again before that
+// (its next call's partials go out only after its previous call saw every
+// tile land, which the owners signal after their resets).  Nothing waits on
+// a step that waits on it, and the CTAs of one rank are all resident
+// (cooperative launch), so the only failure mode is a missing rank, which
+// ends every wait at its time limit with a device error code; the counters
+// are then left mid-count and the buffers must be replaced.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -34,7 +53,7 @@ struct GemmCfg {
   static constexpr int kThreads = 256;
   static constexpr int kTmemCols = 512;              // 2 x 256 fp32 accumulators
   static constexpr int kNumBars = 2 * kStages + 4 + 1;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 16;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 32;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -108,10 +127,59 @@ __device__ __forceinline__ void gemm_store_chunk(Tout* dst, const float (&v)[32]
   }
 }
 
-template <typename Tin, typename Tout>
+// 32 fp32 values as four 16-byte groups of 16-bit values.
+template <typename Tout>
+__device__ __forceinline__ void pack_chunk(const float (&v)[32], uint4 (&out)[4]) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    if constexpr (std::is_same<Tout, __nv_bfloat16>::value) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+      pk[e] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+      pk[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) out[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+}
+
+// Partial tiles in the inboxes are stored column-group major: the 16-byte
+// group g (8 columns) of row r sits at 16-byte index g * 128 + r, so the 32
+// lanes of a warp (32 consecutive rows) write and read 512 contiguous bytes.
+__device__ __forceinline__ int inbox_index(int group, int row) { return group * 128 + row; }
+
+// Sums 32 columns (16-byte groups 4*cc .. 4*cc+3) of row r over the ranks' inbox slots.
+template <typename Tout>
+__device__ __forceinline__ void sum_partials(const uint4* slot0, int64_t src_stride16, int world, int cc, int r,
+                                             float (&acc)[32]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+  for (int src = 0; src < world; ++src) {
+    const uint4* s4 = slot0 + src * src_stride16;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 x = __ldcg(s4 + inbox_index(4 * cc + q, r));  // L2: written by another GPU
+      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f;
+        if constexpr (std::is_same<Tout, __nv_bfloat16>::value)
+          f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+        else
+          f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+        acc[8 * q + 2 * e] += f.x;
+        acc[8 * q + 2 * e + 1] += f.y;
+      }
+    }
+  }
+}
+
+template <typename Tin, typename Tout, bool kAR>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
-                const __grid_constant__ CUtensorMap tm_b) {
+                const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ GemmArParams ar) {
   using C = GemmCfg<sizeof(Tin)>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -124,6 +192,10 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* bar_teardown = bar_acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_teardown + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Epilogue-warpgroup agreement words (fused all-reduce only).
+  volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [4], one per epilogue warp
+  volatile int* ep_go = reinterpret_cast<volatile int*>(tmem_slot + 6);
+  volatile int* ep_have = reinterpret_cast<volatile int*>(tmem_slot + 7);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -226,30 +298,141 @@ __global__ void __launch_bounds__(256, 1)
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    int tcount = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
-      const int buf = tcount & 1;
-      const uint32_t use = tcount >> 1;
-      if (!mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc)) break;
-      tc_fence_after();
-      int pm, pn;
-      gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
-      const int row = pm * C::kBM + r;
-      const int n0 = pn * C::kBN;
-      Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
+    if constexpr (!kAR) {
+      int tcount = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t use = tcount >> 1;
+        if (!mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc)) break;
+        tc_fence_after();
+        int pm, pn;
+        gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+        const int row = pm * C::kBM + r;
+        const int n0 = pn * C::kBN;
+        Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
 #pragma unroll 1
-      for (int cc = 0; cc < C::kBN / 32; ++cc) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_base + buf * C::kBN + cc * 32, rr);
-        tmem_wait_ld();
-        float v[32];
+        for (int cc = 0; cc < C::kBN / 32; ++cc) {
+          uint32_t rr[32];
+          tmem_ld32(tmem + lane_base + buf * C::kBN + cc * 32, rr);
+          tmem_wait_ld();
+          float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
-        const int ncols = min(32, p.N - n0 - cc * 32);
-        if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+          const int ncols = min(32, p.N - n0 - cc * 32);
+          if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
+        }
+        tc_fence_before();
+        mbar_arrive(bar_acc_empty + buf);
       }
-      tc_fence_before();
-      mbar_arrive(bar_acc_empty + buf);
+    } else {
+      // The epilogue warpgroup synchronises with a named barrier, which has
+      // no time limit, so no warp leaves these loops early: a failed wait
+      // only clears `ok`, and decisions every warp must share are taken by
+      // thread 0 and read back after a barrier.
+      const int64_t slot_elems = static_cast<int64_t>(C::kBM) * C::kBN;
+      const int64_t src_stride = static_cast<int64_t>(ar.tiles_per_owner) * slot_elems;
+      bool ok = true;
+      int tcount = 0;
+      // 1. partial tiles into their owners' inboxes
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t use = tcount >> 1;
+        if (ok) ok = mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc);
+        const int owner = t % ar.world;
+        const int j = t / ar.world;
+        if (ok) {
+          tc_fence_after();
+          uint4* slot = reinterpret_cast<uint4*>(ar.inbox[owner]) + (ar.rank * src_stride + j * slot_elems) / 8;
+#pragma unroll 1
+          for (int cc = 0; cc < C::kBN / 32; ++cc) {
+            uint32_t rr[32];
+            tmem_ld32(tmem + lane_base + buf * C::kBN + cc * 32, rr);
+            tmem_wait_ld();
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+            uint4 g[4];
+            pack_chunk<Tout>(v, g);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) slot[inbox_index(4 * cc + q, r)] = g[q];
+          }
+          tc_fence_before();
+          mbar_arrive(bar_acc_empty + buf);
+        }
+        if (lane == 0) ep_ok[wq] = ok ? 1 : 0;
+        named_barrier_sync(1, 128);
+        if (r == 0 && ep_ok[0] && ep_ok[1] && ep_ok[2] && ep_ok[3]) {
+          fence_acq_rel_sys();
+          red_release_sys_add(ar.arrive[owner] + j, 1ull);
+        }
+        named_barrier_sync(1, 128);  // ep_ok is rewritten next iteration
+      }
+      if (lane == 0) ep_ok[wq] = ok ? 1 : 0;
+      named_barrier_sync(1, 128);
+      if (r == 0) *ep_go = (ep_ok[0] && ep_ok[1] && ep_ok[2] && ep_ok[3] && !*abort_flag) ? 1 : 0;
+      named_barrier_sync(1, 128);
+      const bool go = *ep_go != 0;
+      // 2. reduce the tiles this rank owns and hand them to every rank.  The
+      // reduced tile is staged in shared memory (the K/V stages are idle now:
+      // this CTA's last MMAs completed before its last accumulator was
+      // drained) so each warp then writes whole 512-byte rows, 16-byte groups
+      // XOR-swizzled by row against bank conflicts.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      uint4* stage = reinterpret_cast<uint4*>(smem);  // [128 rows][32 groups]
+      const uint4* inbox = reinterpret_cast<const uint4*>(ar.inbox[ar.rank]);
+      const int64_t src_stride16 = src_stride / 8;
+      for (int j = blockIdx.x; j < ar.tiles_per_owner; j += gridDim.x) {
+        const int t = j * ar.world + ar.rank;
+        if (r == 0)
+          *ep_have = (go && t < num_tiles &&
+                      wait_counter_at_least(ar.arrive[ar.rank] + j, static_cast<unsigned long long>(ar.world),
+                                            abort_flag, kDevTimeoutPeerTile))
+                         ? 1 : 0;
+        named_barrier_sync(1, 128);
+        const bool have = *ep_have != 0;
+        int pm = 0, pn = 0;
+        if (have) {
+          gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+          const uint4* slot0 = inbox + j * slot_elems / 8;
+#pragma unroll 1
+          for (int cc = 0; cc < C::kBN / 32; ++cc) {
+            float acc[32];
+            sum_partials<Tout>(slot0, src_stride16, ar.world, cc, r, acc);
+            uint4 g[4];
+            pack_chunk<Tout>(acc, g);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) stage[r * 32 + ((4 * cc + q) ^ (r & 31))] = g[q];
+          }
+        }
+        named_barrier_sync(1, 128);
+        if (have) {
+          // warp wq writes rows 32*wq .. 32*wq+31; lane l the 16-byte group l of each
+          const int n0 = pn * C::kBN;
+          const int col = n0 + lane * 8;
+#pragma unroll 1
+          for (int i = wq * 32; i < wq * 32 + 32; ++i) {
+            const int row = pm * C::kBM + i;
+            if (row >= p.M) break;  // rows past M end the tile for this warp alone; no barrier inside
+            const uint4 val = stage[i * 32 + (lane ^ (i & 31))];
+            if (col < p.N) {
+              for (int dst = 0; dst < ar.world; ++dst)
+                reinterpret_cast<uint4*>(reinterpret_cast<Tout*>(ar.out[dst]) + static_cast<int64_t>(row) * ar.ldo +
+                                         col)[0] = val;
+            }
+          }
+        }
+        named_barrier_sync(1, 128);
+        if (r == 0 && have) {
+          atomicExch(ar.arrive[ar.rank] + j, 0ull);  // every partial of tile j has been read
+          fence_acq_rel_sys();
+          for (int dst = 0; dst < ar.world; ++dst) red_release_sys_add(ar.done[dst], 1ull);
+        }
+      }
+      // 3. every tile of C has landed in this rank's output
+      if (go && blockIdx.x == 0 && r == 0 &&
+          wait_counter_at_least(ar.done[ar.rank], static_cast<unsigned long long>(num_tiles), abort_flag,
+                                kDevTimeoutPeerDone))
+        atomicExch(ar.done[ar.rank], 0ull);
     }
   }
 
@@ -261,10 +444,10 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-template <typename Tin, typename Tout>
-static int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
+template <typename Tin, typename Tout, bool kAR = false>
+static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArParams* ar = nullptr) {
   using C = GemmCfg<sizeof(Tin)>;
-  auto kern = gemm_kernel<Tin, Tout>;
+  auto kern = gemm_kernel<Tin, Tout, kAR>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
   const int elt = sizeof(Tin);
@@ -291,8 +474,30 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   int sms = num_sms();
   if (sms <= 0) return kErrLaunch;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
-  return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+  GemmArParams arp{};
+  if constexpr (kAR) {
+    // CTAs wait on one another's tiles: launch them all resident together.
+    arp = *ar;
+    void* args[] = {&kp, &ta, &tb, &arp};
+    const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid),
+                                                      dim3(C::kThreads), args, C::kSmemBytes, stream);
+    return e == cudaSuccess ? 0 : kErrLaunch;
+  } else {
+    kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb, arp);
+    return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+  }
+}
+
+int gemm_ar_tiles(int M, int N) {
+  return ((M + GemmCfg<2>::kBM - 1) / GemmCfg<2>::kBM) * ((N + GemmCfg<2>::kBN - 1) / GemmCfg<2>::kBN);
+}
+
+int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t stream) {
+  if (L.M <= 0 || L.N <= 0 || L.K <= 0) return kErrInvalidArg;
+  if (L.in_dtype != L.out_dtype) return kErrUnsupported;
+  if (L.in_dtype == kDtypeBF16) return launch_gemm<__nv_bfloat16, __nv_bfloat16, true>(L, stream, &ar);
+  if (L.in_dtype == kDtypeF16) return launch_gemm<__half, __half, true>(L, stream, &ar);
+  return kErrUnsupported;
 }
 
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
@@ -317,9 +522,9 @@ int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
 
 int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads) {
   cudaFuncAttributes a{};
-  const void* k = in_dtype == kDtypeF32    ? reinterpret_cast<const void*>(gemm_kernel<float, __half>)
-                  : in_dtype == kDtypeBF16 ? reinterpret_cast<const void*>(gemm_kernel<__nv_bfloat16, __half>)
-                                           : reinterpret_cast<const void*>(gemm_kernel<__half, __half>);
+  const void* k = in_dtype == kDtypeF32    ? reinterpret_cast<const void*>(gemm_kernel<float, __half, false>)
+                  : in_dtype == kDtypeBF16 ? reinterpret_cast<const void*>(gemm_kernel<__nv_bfloat16, __half, false>)
+                                           : reinterpret_cast<const void*>(gemm_kernel<__half, __half, false>);
   if (cudaFuncGetAttributes(&a, k) != cudaSuccess) return kErrLaunch;
   *regs = a.numRegs;
   *smem = in_dtype == kDtypeF32 ? GemmCfg<4>::kSmemBytes : GemmCfg<2>::kSmemBytes;

@@ -24,6 +24,8 @@ enum DeviceError : int {
   kDevTimeoutEmpty = 6,
   kDevTimeoutAcc = 7,
   kDevTimeoutTeardown = 8,
+  kDevTimeoutPeerTile = 9,   // a tile's partial sums from every rank never all arrived
+  kDevTimeoutPeerDone = 10,  // the reduced tiles from every owner never all arrived
 };
 
 // Device-global status word shared by all kernels of this library (the
@@ -104,6 +106,49 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
   const bool ok = mbar_wait(bar, parity, abort, code);
   return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
+// It has no time limit: every thread that can reach one must reach it.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ------------------------------------------------- cross-GPU signalling ---
+// Counters in (possibly peer) global memory, ordered at system scope so that
+// NVLink peer stores issued before a release are visible after the matching
+// acquire on the other GPU.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void red_release_sys_add(unsigned long long* addr, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Bounded spin until *counter >= target.  Returns false (after recording
+// `code`) when the limit passes or another thread of the CTA gave up.
+__device__ __forceinline__ bool wait_counter_at_least(const unsigned long long* counter, unsigned long long target,
+                                                      volatile int* abort, int code) {
+  if (ld_acquire_sys(counter) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(counter) >= target) return true;
+    if ((++spins & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------------------- TMA ---

@@ -476,6 +476,10 @@ class Backends:
 
     attention: str = "native"       # "native" (this repository's kernel) or a torch SDPA backend name
     gemm: str = "native"            # "native" (this repository's GEMM) or "cublas"
+    # o_proj / down_proj + all-reduce: None = the matmul backend, then an NCCL
+    # all-reduce; a tp_allreduce.FusedGemmAllReduce = one fused kernel over
+    # NVLink peer memory (same group, rows >= the prompt, cols = hidden).
+    fused_allreduce: object = None
 
 
 def _matmul(a: torch.Tensor, b: torch.Tensor, how: str) -> torch.Tensor:
@@ -541,15 +545,21 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
         _attention_segments(q.unsqueeze(0).transpose(1, 2), k.unsqueeze(0).transpose(1, 2),
                             v.unsqueeze(0).transpose(1, 2), attn_out.unsqueeze(0).transpose(1, 2), plan,
                             backends.attention)
-        o = _matmul(attn_out.view(S, nq * D), layer.w_o, backends.gemm)
-        _all_reduce(o, group)
+        if backends.fused_allreduce is not None:
+            o = backends.fused_allreduce(attn_out.view(S, nq * D), layer.w_o)  # valid until its next call
+        else:
+            o = _matmul(attn_out.view(S, nq * D), layer.w_o, backends.gemm)
+            _all_reduce(o, group)
         x = x + o
         h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
         gu = _matmul(h, layer.w_gate_up, backends.gemm)
         m = gu.shape[1] // 2
         a = F.silu(gu[:, :m]) * gu[:, m:]
-        d = _matmul(a, layer.w_down, backends.gemm)
-        _all_reduce(d, group)
+        if backends.fused_allreduce is not None:
+            d = backends.fused_allreduce(a, layer.w_down)
+        else:
+            d = _matmul(a, layer.w_down, backends.gemm)
+            _all_reduce(d, group)
         x = x + d
     last = _rms_norm(x[-1:], model.ln_final, arch.rms_norm_eps)
     return (last @ model.lm_head).float()

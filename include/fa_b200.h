@@ -221,6 +221,58 @@ typedef struct fab_gemm_params {
 int fab_gemm(const fab_gemm_params* params, void* stream);
 
 /*
+ * GEMM + all-reduce over the ranks of a tensor-parallel group in one kernel,
+ * through NVLink peer memory: out = sum over ranks of a_r[M,K] * b_r[K,N],
+ * on every rank.  Replaces the o_proj / down_proj matmul followed by an NCCL
+ * all-reduce in the tensor-parallel decoder (the reference runs the model on
+ * one GPU; ttft.py:401-412 is its forward).  No counterpart in the
+ * reference.
+ *
+ * Each rank owns the 128x256 output tiles t with t % world == rank.  While
+ * its MMAs run, a rank stores every partial tile straight into the owner's
+ * inbox and counts it there; each owner then sums the world partials in fp32
+ * and writes the result into every rank's output.  All waits are bounded: a
+ * rank that never joins makes the others return FAB_OK with
+ * fab_get_device_error reporting the timeout.
+ *
+ * Buffers (sizes from fab_gemm_allreduce_layout): per rank an inbox
+ * (16-byte aligned), an output [M, ldo] of the input dtype and a counter
+ * array (8-byte aligned, zero before the first call; every call leaves it
+ * zero again).  inbox[r], out[r] and counters[r] are rank r's buffers as
+ * this process sees them (its own, or peers' mapped with fab_ipc_import).
+ * Every rank makes the same sequence of calls with the same M, N and K, on
+ * one stream each.  After a timeout the counters are left mid-count: replace
+ * the buffers.  bf16 or fp16, row-major.
+ */
+#define FAB_MAX_TP_RANKS 8
+typedef struct fab_gemm_allreduce_params {
+  const void* a;
+  const void* b;
+  int64_t lda, ldb, ldo;
+  int M, N, K;
+  int in_dtype;
+  int world;
+  int rank;
+  void* inbox[FAB_MAX_TP_RANKS];
+  void* out[FAB_MAX_TP_RANKS];
+  void* counters[FAB_MAX_TP_RANKS];
+} fab_gemm_allreduce_params;
+
+int fab_gemm_allreduce_layout(int M, int N, int world, int* tiles_per_owner, size_t* inbox_bytes,
+                              size_t* counter_bytes);
+int fab_gemm_allreduce(const fab_gemm_allreduce_params* params, void* stream);
+
+/*
+ * CUDA IPC for the peer buffers above: fab_ipc_export writes the 64-byte
+ * handle of the allocation holding `ptr` and ptr's offset in it;
+ * fab_ipc_import maps a peer's handle in this process (base = the mapping,
+ * ptr = base + offset); fab_ipc_close unmaps `base`.
+ */
+int fab_ipc_export(const void* ptr, void* handle, size_t* offset);
+int fab_ipc_import(const void* handle, size_t offset, void** base, void** ptr);
+int fab_ipc_close(void* base);
+
+/*
  * Static sm_100a tile table that replaces the reference tuner's compile-and-rank
  * search (tuner.py:414-561): the configuration the attention kernel uses for a
  * dtype and head_dim.
