@@ -121,6 +121,7 @@ struct GemmArParams {
   int world;
   int rank;
   int tiles_per_owner;
+  int overlap;  // the two idle warps of each CTA reduce owned tiles during the GEMM
 };
 
 struct GemmLaunch {

@@ -17,10 +17,14 @@
 //   1. each finished partial tile is stored straight into the inbox of the
 //      rank that owns it (tile t -> rank t % world) and counted there with a
 //      system-scope release, while the next tile's MMAs run;
-//   2. after its last tile every CTA takes the tiles its rank owns, waits
-//      (bounded) until all ranks' partials are in, sums them in fp32 and
-//      writes the result into every rank's output buffer, then counts it in
-//      each rank's done counter;
+//   2. meanwhile the two otherwise idle warps of every CTA take the tiles its
+//      rank owns, wait (bounded) until all ranks' partials are in, sum them
+//      in fp32 and write the result into every rank's output buffer, then
+//      count it in each rank's done counter; once the CTA's own GEMM tiles
+//      are out, its four epilogue warps take owned tiles too (both groups
+//      claim them from one shared counter, so each is reduced once).  For
+//      GEMMs of fewer than three waves of tiles the two warps stay out: the
+//      overlap is too short to pay for their slower 64-thread reduction;
 //   3. CTA 0 waits (bounded) until every tile of C has landed locally.
 // Each counter is reset to zero by the one thread that waits on it, once it
 // has seen the count it waits for; no rank can add to it again before that
@@ -53,7 +57,7 @@ struct GemmCfg {
   static constexpr int kThreads = 256;
   static constexpr int kTmemCols = 512;              // 2 x 256 fp32 accumulators
   static constexpr int kNumBars = 2 * kStages + 4 + 1;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 32;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 64;  // + 16 status words
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -176,6 +180,41 @@ __device__ __forceinline__ void sum_partials(const uint4* slot0, int64_t src_str
   }
 }
 
+// Claims the next owned tile of this CTA (j = blockIdx.x + k * gridDim.x)
+// once all ranks' partials of it are in: the reducer warps and, after their
+// GEMM tiles, the epilogue warps call this, and whichever sees the tile ready
+// first takes it, so a tile is never held by a group that is slower to reduce
+// it while its partials are still missing.  Returns the tile, -1 when none is
+// left, or -2 when the wait ran out (device error recorded).
+__device__ __forceinline__ int claim_ready_tile(int* next, const GemmArParams& ar, int num_tiles,
+                                                volatile int* abort) {
+  uint64_t t0 = globaltimer_ns();
+  int seen = -1;
+  uint32_t spins = 0;
+  while (true) {
+    const int k = *reinterpret_cast<volatile int*>(next);
+    const int j = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+    if (j >= ar.tiles_per_owner || j * ar.world + ar.rank >= num_tiles) return -1;
+    if (k != seen) {  // a new tile to wait for: restart its clock
+      seen = k;
+      t0 = globaltimer_ns();
+    }
+    if (ld_acquire_sys(ar.arrive[ar.rank] + j) >= static_cast<unsigned long long>(ar.world)) {
+      if (atomicCAS(next, k, k + 1) == k) return j;
+      continue;  // the other group took it
+    }
+    __nanosleep(64);
+    if ((++spins & 63u) == 0u) {
+      if (*abort) return -2;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(kDevTimeoutPeerTile);
+        *abort = 1;
+        return -2;
+      }
+    }
+  }
+}
+
 template <typename Tin, typename Tout, bool kAR>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
@@ -194,8 +233,11 @@ __global__ void __launch_bounds__(256, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Epilogue-warpgroup agreement words (fused all-reduce only).
   volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [4], one per epilogue warp
-  volatile int* ep_go = reinterpret_cast<volatile int*>(tmem_slot + 6);
-  volatile int* ep_have = reinterpret_cast<volatile int*>(tmem_slot + 7);
+  volatile int* red_have = reinterpret_cast<volatile int*>(tmem_slot + 7);
+  int* red_next = reinterpret_cast<int*>(tmem_slot + 6);  // next unclaimed owned tile of this CTA
+  // Reducer staging: 32 rows x 32 16-byte groups, after the barrier words.
+  uint4* red_stage =
+      reinterpret_cast<uint4*>(smem + (C::kStages * C::kStageBytes + C::kNumBars * 8 + 64 + 127) / 128 * 128);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -214,6 +256,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(bar_acc_empty + b, 128);
     }
     mbar_init(bar_teardown, 1);
+    *red_next = 0;
     *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
     mbar_fence_init();
   }
@@ -367,32 +410,24 @@ __global__ void __launch_bounds__(256, 1)
         }
         named_barrier_sync(1, 128);  // ep_ok is rewritten next iteration
       }
-      if (lane == 0) ep_ok[wq] = ok ? 1 : 0;
-      named_barrier_sync(1, 128);
-      if (r == 0) *ep_go = (ep_ok[0] && ep_ok[1] && ep_ok[2] && ep_ok[3] && !*abort_flag) ? 1 : 0;
-      named_barrier_sync(1, 128);
-      const bool go = *ep_go != 0;
-      // 2. reduce the tiles this rank owns and hand them to every rank.  The
-      // reduced tile is staged in shared memory (the K/V stages are idle now:
-      // this CTA's last MMAs completed before its last accumulator was
-      // drained) so each warp then writes whole 512-byte rows, 16-byte groups
-      // XOR-swizzled by row against bank conflicts.
+      // 2b. help with the owned tiles the reducer warps have not claimed.  The
+      // K/V stages are idle now (this CTA's last MMAs completed before its last
+      // accumulator was drained): stage a whole reduced tile there so each
+      // warp writes 512-byte rows.
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       uint4* stage = reinterpret_cast<uint4*>(smem);  // [128 rows][32 groups]
       const uint4* inbox = reinterpret_cast<const uint4*>(ar.inbox[ar.rank]);
       const int64_t src_stride16 = src_stride / 8;
-      for (int j = blockIdx.x; j < ar.tiles_per_owner; j += gridDim.x) {
-        const int t = j * ar.world + ar.rank;
-        if (r == 0)
-          *ep_have = (go && t < num_tiles &&
-                      wait_counter_at_least(ar.arrive[ar.rank] + j, static_cast<unsigned long long>(ar.world),
-                                            abort_flag, kDevTimeoutPeerTile))
-                         ? 1 : 0;
+      volatile int* ep_claim = ep_ok;  // reused: ep_ok is no longer needed
+      while (true) {
+        if (r == 0) ep_claim[0] = claim_ready_tile(red_next, ar, num_tiles, abort_flag);
         named_barrier_sync(1, 128);
-        const bool have = *ep_have != 0;
+        const int j = ep_claim[0];
+        if (j < 0) break;  // read by all 128 threads after the barrier: the same for all
+        const bool have = true;
         int pm = 0, pn = 0;
         if (have) {
-          gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+          gemm_tile_coords(j * ar.world + ar.rank, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
           const uint4* slot0 = inbox + j * slot_elems / 8;
 #pragma unroll 1
           for (int cc = 0; cc < C::kBN / 32; ++cc) {
@@ -406,18 +441,15 @@ __global__ void __launch_bounds__(256, 1)
         }
         named_barrier_sync(1, 128);
         if (have) {
-          // warp wq writes rows 32*wq .. 32*wq+31; lane l the 16-byte group l of each
-          const int n0 = pn * C::kBN;
-          const int col = n0 + lane * 8;
+          const int col = pn * C::kBN + lane * 8;
 #pragma unroll 1
           for (int i = wq * 32; i < wq * 32 + 32; ++i) {
             const int row = pm * C::kBM + i;
-            if (row >= p.M) break;  // rows past M end the tile for this warp alone; no barrier inside
-            const uint4 val = stage[i * 32 + (lane ^ (i & 31))];
-            if (col < p.N) {
+            if (row < p.M && col < p.N) {
+              const uint4 val = stage[i * 32 + (lane ^ (i & 31))];
               for (int dst = 0; dst < ar.world; ++dst)
-                reinterpret_cast<uint4*>(reinterpret_cast<Tout*>(ar.out[dst]) + static_cast<int64_t>(row) * ar.ldo +
-                                         col)[0] = val;
+                *reinterpret_cast<uint4*>(reinterpret_cast<Tout*>(ar.out[dst]) + static_cast<int64_t>(row) * ar.ldo +
+                                          col) = val;
             }
           }
         }
@@ -429,10 +461,72 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
       // 3. every tile of C has landed in this rank's output
-      if (go && blockIdx.x == 0 && r == 0 &&
+      if (blockIdx.x == 0 && r == 0 &&
           wait_counter_at_least(ar.done[ar.rank], static_cast<unsigned long long>(num_tiles), abort_flag,
                                 kDevTimeoutPeerDone))
         atomicExch(ar.done[ar.rank], 0ull);
+    }
+  } else if constexpr (kAR) {
+    if (!skip && ar.overlap && (warp == 2 || warp == 3)) {
+      // ------------------------------------------------------------ reducer
+      // 2. reduce the tiles this rank owns as their partials arrive, while
+      // the GEMM runs.  32 rows at a time: each thread sums 128 columns of one
+      // row into the staging buffer (16-byte groups XOR-swizzled by row),
+      // then each warp writes 16 whole 512-byte rows to every rank.  Named
+      // barrier 2 spans these 64 threads; no thread leaves a loop early.
+      const int rr = threadIdx.x - 64;
+      const int half = rr >> 5;  // which 128 columns
+      const int64_t slot_elems = static_cast<int64_t>(C::kBM) * C::kBN;
+      const int64_t src_stride16 = static_cast<int64_t>(ar.tiles_per_owner) * slot_elems / 8;
+      const uint4* inbox = reinterpret_cast<const uint4*>(ar.inbox[ar.rank]);
+      volatile int* red_claim = red_have;  // the claimed tile, or < 0
+      while (true) {
+        if (rr == 0) *red_claim = claim_ready_tile(red_next, ar, num_tiles, abort_flag);
+        named_barrier_sync(2, 64);
+        const int j = *red_claim;
+        if (j < 0) break;  // read by all 64 threads after the barrier: the same for all
+        const int t = j * ar.world + ar.rank;
+        const bool have = true;
+        if (have) {
+          int pm, pn;
+          gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+          const int n0 = pn * C::kBN;
+          const uint4* slot0 = inbox + j * slot_elems / 8;
+#pragma unroll 1
+          for (int rb = 0; rb < C::kBM / 32; ++rb) {
+            const int r = rb * 32 + (rr & 31);
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {  // 32 columns = 4 groups at a time
+              const int cc = half * 4 + c4;
+              float acc[32];
+              sum_partials<Tout>(slot0, src_stride16, ar.world, cc, r, acc);
+              uint4 g[4];
+              pack_chunk<Tout>(acc, g);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) red_stage[(r & 31) * 32 + ((4 * cc + q) ^ (r & 31))] = g[q];
+            }
+            named_barrier_sync(2, 64);
+            const int col = n0 + (rr & 31) * 8;
+#pragma unroll 1
+            for (int i = half * 16; i < half * 16 + 16; ++i) {
+              const int row = pm * C::kBM + rb * 32 + i;
+              if (row < p.M && col < p.N) {
+                const uint4 val = red_stage[i * 32 + ((rr & 31) ^ i)];
+                for (int dst = 0; dst < ar.world; ++dst)
+                  *reinterpret_cast<uint4*>(reinterpret_cast<Tout*>(ar.out[dst]) + static_cast<int64_t>(row) * ar.ldo +
+                                            col) = val;
+              }
+            }
+            named_barrier_sync(2, 64);
+          }
+          if (rr == 0) {
+            atomicExch(ar.arrive[ar.rank] + j, 0ull);  // every partial of tile j has been read
+            fence_acq_rel_sys();
+            for (int dst = 0; dst < ar.world; ++dst) red_release_sys_add(ar.done[dst], 1ull);
+          }
+        }
+        named_barrier_sync(2, 64);  // red_claim is rewritten next iteration
+      }
     }
   }
 
@@ -448,7 +542,9 @@ template <typename Tin, typename Tout, bool kAR = false>
 static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArParams* ar = nullptr) {
   using C = GemmCfg<sizeof(Tin)>;
   auto kern = gemm_kernel<Tin, Tout, kAR>;
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  constexpr int kSmem = C::kSmemBytes + (kAR ? 128 + 32 * 32 * 16 : 0);  // reducer staging
+  static_assert(kSmem <= 232448, "shared memory budget");
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmem);
   if (rc) return rc;
   const int elt = sizeof(Tin);
   const CUtensorMapDataType dt = elt == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -478,12 +574,13 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   if constexpr (kAR) {
     // CTAs wait on one another's tiles: launch them all resident together.
     arp = *ar;
+    arp.overlap = tiles >= 3 * grid ? 1 : 0;
     void* args[] = {&kp, &ta, &tb, &arp};
     const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid),
-                                                      dim3(C::kThreads), args, C::kSmemBytes, stream);
+                                                      dim3(C::kThreads), args, kSmem, stream);
     return e == cudaSuccess ? 0 : kErrLaunch;
   } else {
-    kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb, arp);
+    kern<<<grid, C::kThreads, kSmem, stream>>>(kp, ta, tb, arp);
     return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
   }
 }

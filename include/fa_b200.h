@@ -240,8 +240,8 @@ int fab_gemm(const fab_gemm_params* params, void* stream);
  * array (8-byte aligned, zero before the first call; every call leaves it
  * zero again).  inbox[r], out[r] and counters[r] are rank r's buffers as
  * this process sees them (its own, or peers' mapped with fab_ipc_import).
- * Every rank makes the same sequence of calls with the same M, N and K, on
- * one stream each.  After a timeout the counters are left mid-count: replace
+ * Every rank makes the same sequence of calls with the same M and N (K may
+ * differ: each rank's GEMM is its own), on one stream each.  After a timeout the counters are left mid-count: replace
  * the buffers.  bf16 or fp16, row-major.
  */
 #define FAB_MAX_TP_RANKS 8

@@ -88,11 +88,14 @@ def _worker(rank, world, port, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_over_nvlink(tmp_path, cuda_device):
+def test_ranks_over_nvlink(tmp_path, cuda_device):
+    """As many ranks as the box has GPUs (2 to 8); at 8 the decoder's heads split 4,4,4,4,3,3,3,3, so the
+    ranks' o_proj GEMMs have different K over the same output tiles."""
     import torch.multiprocessing as mp
 
+    world = min(torch.cuda.device_count(), 8)
     out = str(tmp_path / "ar.pt")
-    mp.start_processes(_worker, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
     res = torch.load(out)
     # each rank checked out against sum_r a_r @ b_r (rtol 1e-2, atol 2e-2); |out| reaches ~6 here, where
     # one bf16 step is 0.03
