@@ -569,7 +569,7 @@ def run_ttft(args, world, rank, local):
     builds = {
         "ours": ttft.Backends(attention="native", gemm="native"),
         "ours_attention_cublas_gemm": ttft.Backends(attention="native", gemm="cublas"),
-        "torch_cudnn_sdpa_cublas": ttft.Backends(attention="cudnn", gemm="cublas"),
+        "torch_cudnn_sdpa_cublas": ttft.Backends(attention="cudnn", gemm="cublas", elementwise="torch"),
     }
     fused = None
     if world > 1:

@@ -133,6 +133,9 @@ PROTOTYPES = {
     "fab_ipc_export": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_size_t)]),
     "fab_ipc_import": (_i32, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "fab_ipc_close": (_i32, [_vp]),
+    "fab_rmsnorm": (_i32, [_vp] * 5 + [_i32, _i32] + [_i64] * 4 + [_f32, _i32, _vp]),
+    "fab_bias_rope": (_i32, [_vp] * 4 + [_i32] * 4 + [_i64, _i32, _vp]),
+    "fab_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),
     "fab_kernel_attrs_query": (_i32, [_i32, _i32, _i32, ctypes.POINTER(FabKernelAttrs)]),
     "fab_device_limits_query": (_i32, [_i32, ctypes.POINTER(FabDeviceLimits)]),

@@ -17,6 +17,7 @@
 
 #include "fa_fwd_kernel.cuh"
 #include "gemm_kernel.cuh"
+#include "decoder_ops.cuh"
 
 namespace fab {
 
@@ -626,6 +627,76 @@ int fab_ipc_import(const void* handle, size_t offset, void** base, void** ptr) {
 int fab_ipc_close(void* base) {
   if (base == nullptr) return kErrInvalidArg;
   return cudaIpcCloseMemHandle(base) == cudaSuccess ? kOk : kErrCuda;
+}
+
+static bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool ld16(int64_t ld) { return (ld * 2) % 16 == 0; }
+
+int fab_rmsnorm(const void* x, const void* residual, const void* w, void* h, void* x_out, int rows, int cols,
+                int64_t ld_x, int64_t ld_res, int64_t ld_h, int64_t ld_xo, float eps, int dtype, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 != 0 || cols > 8192) return kErrInvalidArg;
+  if (x == nullptr || w == nullptr || h == nullptr || (residual != nullptr && x_out == nullptr)) return kErrInvalidArg;
+  if (!al16(x) || !al16(residual) || !al16(w) || !al16(h) || !al16(x_out)) return kErrInvalidArg;
+  if (!ld16(ld_x) || !ld16(ld_h) || (residual != nullptr && (!ld16(ld_res) || !ld16(ld_xo)))) return kErrInvalidArg;
+  if (dtype != kDtypeBF16 && dtype != kDtypeF16) return kErrUnsupported;
+  if (rows == 0) return kOk;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (dtype == kDtypeBF16) {
+    using T = __nv_bfloat16;
+    rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual),
+                                            static_cast<const T*>(w), static_cast<T*>(h), static_cast<T*>(x_out), cols,
+                                            ld_x, ld_res, ld_h, ld_xo, eps);
+  } else {
+    using T = __half;
+    rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual),
+                                            static_cast<const T*>(w), static_cast<T*>(h), static_cast<T*>(x_out), cols,
+                                            ld_x, ld_res, ld_h, ld_xo, eps);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int fab_bias_rope(void* y, const void* bias, const void* cos, const void* sin, int rows, int heads, int rot_heads,
+                  int head_dim, int64_t ld, int dtype, void* stream) {
+  if (rows < 0 || heads <= 0 || rot_heads < 0 || rot_heads > heads || head_dim <= 0 || head_dim % 16 != 0)
+    return kErrInvalidArg;
+  if (y == nullptr || (rot_heads > 0 && (cos == nullptr || sin == nullptr))) return kErrInvalidArg;
+  if (!al16(y) || !al16(bias) || !al16(cos) || !al16(sin) || !ld16(ld) || ld < static_cast<int64_t>(heads) * head_dim)
+    return kErrInvalidArg;
+  if (dtype != kDtypeBF16 && dtype != kDtypeF16) return kErrUnsupported;
+  const int64_t threads = static_cast<int64_t>(rows) * heads * (head_dim / 16);
+  if (threads == 0) return kOk;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  auto st = static_cast<cudaStream_t>(stream);
+  if (dtype == kDtypeBF16) {
+    using T = __nv_bfloat16;
+    bias_rope_kernel<T><<<blocks, 256, 0, st>>>(static_cast<T*>(y), static_cast<const T*>(bias),
+                                                static_cast<const T*>(cos), static_cast<const T*>(sin), rows, heads,
+                                                rot_heads, head_dim, ld);
+  } else {
+    using T = __half;
+    bias_rope_kernel<T><<<blocks, 256, 0, st>>>(static_cast<T*>(y), static_cast<const T*>(bias),
+                                                static_cast<const T*>(cos), static_cast<const T*>(sin), rows, heads,
+                                                rot_heads, head_dim, ld);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int dtype, void* stream) {
+  if (rows < 0 || m <= 0 || m % 8 != 0 || gu == nullptr || a == nullptr) return kErrInvalidArg;
+  if (!al16(gu) || !al16(a) || !ld16(ld_gu) || !ld16(ld_a) || ld_gu < 2LL * m || ld_a < m) return kErrInvalidArg;
+  if (dtype != kDtypeBF16 && dtype != kDtypeF16) return kErrUnsupported;
+  const int64_t threads = static_cast<int64_t>(rows) * (m / 8);
+  if (threads == 0) return kOk;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  auto st = static_cast<cudaStream_t>(stream);
+  if (dtype == kDtypeBF16) {
+    using T = __nv_bfloat16;
+    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a);
+  } else {
+    using T = __half;
+    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 int fab_matmul_contiguous(const void* a, const void* b, void* c, int M, int N, int K, int in_dtype, int out_dtype,

@@ -476,6 +476,9 @@ class Backends:
 
     attention: str = "native"       # "native" (this repository's kernel) or a torch SDPA backend name
     gemm: str = "native"            # "native" (this repository's GEMM) or "cublas"
+    # residual + RMSNorm, bias + RoPE, SwiGLU: "native" (one fused kernel each,
+    # fab_rmsnorm / fab_bias_rope / fab_silu_mul) or "torch" (PyTorch ops)
+    elementwise: str = "native"
     # o_proj / down_proj + all-reduce: None = the matmul backend, then an NCCL
     # all-reduce; a tp_allreduce.FusedGemmAllReduce = one fused kernel over
     # NVLink peer memory (same group, rows >= the prompt, cols = hidden).
@@ -507,6 +510,51 @@ def _attention_segments(q, k, v, out, plan: RankPlan, how: str) -> None:
             os_.copy_(F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, enable_gqa=count > 1))
 
 
+def _native_rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+                    h: torch.Tensor | None = None) -> torch.Tensor:
+    """h = RMSNorm(x [+ residual]) * w; with a residual, x is updated in place to x + residual."""
+    import ctypes
+
+    import _native
+
+    rows, cols = x.shape
+    h = torch.empty_like(x) if h is None else h
+    stream = ctypes.c_void_p(_native.current_stream_handle(x.device))
+    rc = _native.lib.fab_rmsnorm(x.data_ptr(), residual.data_ptr() if residual is not None else None, w.data_ptr(),
+                                 h.data_ptr(), x.data_ptr() if residual is not None else None, rows, cols,
+                                 x.stride(0), residual.stride(0) if residual is not None else 0, h.stride(0),
+                                 x.stride(0), float(eps), _native.dtype_code(x.dtype), stream)
+    _native.check(rc, "fab_rmsnorm")
+    return h
+
+
+def _native_bias_rope(qkv: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor, sin: torch.Tensor,
+                      heads: int, rot_heads: int, head_dim: int) -> None:
+    import ctypes
+
+    import _native
+
+    stream = ctypes.c_void_p(_native.current_stream_handle(qkv.device))
+    rc = _native.lib.fab_bias_rope(qkv.data_ptr(), bias.data_ptr() if bias is not None else None, cos.data_ptr(),
+                                   sin.data_ptr(), qkv.shape[0], heads, rot_heads, head_dim, qkv.stride(0),
+                                   _native.dtype_code(qkv.dtype), stream)
+    _native.check(rc, "fab_bias_rope")
+
+
+def _native_silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    import ctypes
+
+    import _native
+
+    rows, two_m = gu.shape
+    a = torch.empty(rows, two_m // 2, device=gu.device, dtype=gu.dtype)
+    stream = ctypes.c_void_p(_native.current_stream_handle(gu.device))
+    rc = _native.lib.fab_silu_mul(gu.data_ptr(), a.data_ptr(), rows, two_m // 2, gu.stride(0), a.stride(0),
+                                  _native.dtype_code(gu.dtype), stream)
+    _native.check(rc, "fab_silu_mul")
+    return a
+
+
 def _all_reduce(x: torch.Tensor, group=None) -> None:
     import torch.distributed as dist
 
@@ -527,20 +575,33 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
     D = arch.head_dim
     nq = len(plan.q_heads)
     nkv = len(plan.kv_heads)
-    cos, sin = rope_tables(arch, S, input_ids.device)
-    cos, sin = cos[:, None, :], sin[:, None, :]
+    native = backends.elementwise == "native"
+    cos2, sin2 = rope_tables(arch, S, input_ids.device)
+    cos, sin = cos2[:, None, :], sin2[:, None, :]
     x = model.embed[input_ids[0]]                                  # [S, hidden]
     attn_out = torch.empty(S, nq, D, device=x.device, dtype=x.dtype)
+    h_buf = torch.empty_like(x) if native else None
+    pending = None  # the previous layer's down_proj output, not yet added to x
     for layer in model.layers:
-        h = _rms_norm(x, layer.ln_in, arch.rms_norm_eps)
+        if native:
+            h = _native_rmsnorm(x, layer.ln_in, arch.rms_norm_eps, residual=pending, h=h_buf)
+        else:
+            h = _rms_norm(x, layer.ln_in, arch.rms_norm_eps)
+        pending = None
         qkv = _matmul(h, layer.w_qkv, backends.gemm)
-        if layer.b_qkv is not None:
-            qkv += layer.b_qkv
-        q = qkv[:, : nq * D].view(S, nq, D)
-        k = qkv[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
-        v = qkv[:, (nq + nkv) * D:].view(S, nkv, D)
-        q = q * cos + _rotate_half(q) * sin
-        k = k * cos + _rotate_half(k) * sin
+        if native:
+            _native_bias_rope(qkv, layer.b_qkv, cos2, sin2, nq + 2 * nkv, nq + nkv, D)
+            q = qkv[:, : nq * D].view(S, nq, D)
+            k = qkv[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
+            v = qkv[:, (nq + nkv) * D:].view(S, nkv, D)
+        else:
+            if layer.b_qkv is not None:
+                qkv += layer.b_qkv
+            q = qkv[:, : nq * D].view(S, nq, D)
+            k = qkv[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
+            v = qkv[:, (nq + nkv) * D:].view(S, nkv, D)
+            q = q * cos + _rotate_half(q) * sin
+            k = k * cos + _rotate_half(k) * sin
         # [S, H, D] storage seen as [1, H, S, D]: the kernel reads and writes these strided views in place.
         _attention_segments(q.unsqueeze(0).transpose(1, 2), k.unsqueeze(0).transpose(1, 2),
                             v.unsqueeze(0).transpose(1, 2), attn_out.unsqueeze(0).transpose(1, 2), plan,
@@ -550,18 +611,29 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
         else:
             o = _matmul(attn_out.view(S, nq * D), layer.w_o, backends.gemm)
             _all_reduce(o, group)
-        x = x + o
-        h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
+        if native:
+            h = _native_rmsnorm(x, layer.ln_post, arch.rms_norm_eps, residual=o, h=h_buf)
+        else:
+            x = x + o
+            h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
         gu = _matmul(h, layer.w_gate_up, backends.gemm)
         m = gu.shape[1] // 2
-        a = F.silu(gu[:, :m]) * gu[:, m:]
+        a = _native_silu_mul(gu) if native else F.silu(gu[:, :m]) * gu[:, m:]
         if backends.fused_allreduce is not None:
             d = backends.fused_allreduce(a, layer.w_down)
         else:
             d = _matmul(a, layer.w_down, backends.gemm)
             _all_reduce(d, group)
-        x = x + d
-    last = _rms_norm(x[-1:], model.ln_final, arch.rms_norm_eps)
+        if native:
+            pending = d  # added to x by the next RMSNorm, before the fused output buffer is written again
+        else:
+            x = x + d
+    if native:
+        last = x[-1:].clone()
+        last = _native_rmsnorm(last, model.ln_final, arch.rms_norm_eps,
+                               residual=pending[-1:] if pending is not None else None)
+    else:
+        last = _rms_norm(x[-1:], model.ln_final, arch.rms_norm_eps)
     return (last @ model.lm_head).float()
 
 

@@ -273,6 +273,29 @@ int fab_ipc_import(const void* handle, size_t offset, void** base, void** ptr);
 int fab_ipc_close(void* base);
 
 /*
+ * The memory-bound steps of a Qwen2-style decoder layer between its GEMMs and
+ * its attention (the model the reference's TTFT benchmark prefills,
+ * ttft.py:401-412), each one pass with 16-byte accesses, rounding where the
+ * PyTorch expressions of that model round so bf16 results match them.  No
+ * counterpart in the reference (it runs them as PyTorch ops).  bf16 or fp16;
+ * leading dims in elements; 16-byte aligned pointers and rows.
+ *
+ * fab_rmsnorm: h = w * round(x' * rsqrt(mean(x'^2) + eps)) per row, where
+ *   x' = x, or round(x + residual) (written to x_out, which may alias x) when
+ *   residual is not NULL.  cols a multiple of 8, at most 8192.
+ * fab_bias_rope: in place on y [rows, heads, head_dim] (row stride ld): adds
+ *   bias [heads * head_dim] (may be NULL) to every head, then applies
+ *   rotate-half rotary embedding (cos/sin [rows, head_dim]) to the first
+ *   rot_heads heads: y = round(round(y * cos) + round(rotate_half(y) * sin)).
+ * fab_silu_mul: a[:, j] = round(round(silu(gu[:, j])) * gu[:, m + j]).
+ */
+int fab_rmsnorm(const void* x, const void* residual, const void* w, void* h, void* x_out, int rows, int cols,
+                int64_t ld_x, int64_t ld_res, int64_t ld_h, int64_t ld_xo, float eps, int dtype, void* stream);
+int fab_bias_rope(void* y, const void* bias, const void* cos, const void* sin, int rows, int heads, int rot_heads,
+                  int head_dim, int64_t ld, int dtype, void* stream);
+int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int dtype, void* stream);
+
+/*
  * Static sm_100a tile table that replaces the reference tuner's compile-and-rank
  * search (tuner.py:414-561): the configuration the attention kernel uses for a
  * dtype and head_dim.

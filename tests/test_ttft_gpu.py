@@ -48,8 +48,11 @@ def test_decoder_native_matches_torch(cuda_device):
     ids = ttft._make_random_input_ids(2048, SEVEN_B.vocab_size, cuda_device, seed=4)
     with torch.inference_mode():
         ours = ttft.decoder_forward(shard, ids, ttft.Backends(attention="native", gemm="native"))
-        ref = ttft.decoder_forward(shard, ids, ttft.Backends(attention="cudnn", gemm="cublas"))
+        ref = ttft.decoder_forward(shard, ids, ttft.Backends(attention="cudnn", gemm="cublas", elementwise="torch"))
         mixed = ttft.decoder_forward(shard, ids, ttft.Backends(attention="native", gemm="cublas"))
+        torch_ops = ttft.decoder_forward(shard, ids, ttft.Backends(attention="native", gemm="native",
+                                                                   elementwise="torch"))
+    torch.testing.assert_close(torch_ops, ours, rtol=0.1, atol=0.1)
     torch.testing.assert_close(ours, ref, rtol=0.1, atol=0.1)
     torch.testing.assert_close(mixed, ref, rtol=0.1, atol=0.1)
     assert ours.argmax() == ref.argmax()

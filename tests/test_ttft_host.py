@@ -14,7 +14,7 @@ import ttft
 SEVEN_B = ttft.KNOWN_ARCHS["Qwen/Qwen2.5-7B"]
 TINY = ttft.ArchConfig(hidden_size=256, num_attention_heads=8, num_key_value_heads=2, num_hidden_layers=2,
                        head_dim=32, intermediate_size=512, vocab_size=1024)
-TORCH = ttft.Backends(attention="math", gemm="cublas")
+TORCH = ttft.Backends(attention="math", gemm="cublas", elementwise="torch")
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
