@@ -3,7 +3,9 @@
 One GPU: a group of one (every tile owned locally) against torch.matmul, over several calls on the same
 buffers.  Two GPUs: two NCCL ranks, each with its own a_r and b_r, against sum_r a_r @ b_r computed in fp32,
 and the tensor-parallel decoder with the fused kernel against the same decoder on NCCL all-reduce.
-Tolerance: bf16 partial tiles summed in fp32 and rounded once more -- max-abs 2e-2 + rtol 1e-2 on O(1) outputs.
+Tolerance: each rank's partial tile is rounded to bf16 before the fp32 sum (as an NCCL bf16 all-reduce
+receives bf16 partials), so the error grows like sqrt(world) bf16 steps of O(1) partials: rtol 1e-2 and
+atol 0.015 * sqrt(world) against the exact fp32 sum.
 """
 from __future__ import annotations
 
@@ -66,7 +68,7 @@ def _worker(rank, world, port, out_path):
             ref = sum(x.float() @ y.float() for x, y in (_operands(r, M, K, 3584, dev, seed=10 * call)
                                                           for r in range(world)))
             errs.append(float((out.float() - ref).abs().max()))
-            torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=2e-2)
+            torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=0.015 * world ** 0.5)
         assert _native.device_error() == 0
         # the tensor-parallel decoder: fused kernel against NCCL all-reduce
         arch = ttft.KNOWN_ARCHS["Qwen/Qwen2.5-7B"]
@@ -94,11 +96,10 @@ def test_ranks_over_nvlink(tmp_path, cuda_device):
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 8)
-    out = str(tmp_path / "ar.pt")
+    out = str(tmp_path / "ar.pt")  # rank 0 saves its results here
     mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
     res = torch.load(out)
-    # each rank checked out against sum_r a_r @ b_r (rtol 1e-2, atol 2e-2); |out| reaches ~6 here, where
-    # one bf16 step is 0.03
-    assert max(res["errs"]) < 0.1
+    # each rank checked out against sum_r a_r @ b_r; |out| reaches ~3 sqrt(world) here
+    assert max(res["errs"]) < 0.05 * world ** 0.5
     torch.testing.assert_close(res["fused"], res["base"], rtol=0.1, atol=0.1)
     assert res["fused"].argmax() == res["base"].argmax()
