@@ -299,7 +299,12 @@ __global__ void __launch_bounds__(256, 1)
   } else if (!skip && warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = umma_idesc(GemmFmt<Tin>::kFmt, C::kBM, C::kBN, 0, 1);
-    const uint32_t base = smem_u32(smem);
+    // Descriptors from precomputed words (see umma_desc_lo): per MMA only the
+    // low word's address field moves.
+    constexpr uint32_t kHiA = umma_desc_hi(1024, kLayoutSw128);
+    constexpr uint32_t kHiB = sizeof(Tin) == 4 ? umma_desc_hi(512, kLayoutSw128Base32B) : umma_desc_hi(1024, kLayoutSw128);
+    const uint32_t a_lo0 = umma_desc_lo(smem_u32(smem), 16);
+    const uint32_t b_lo0 = umma_desc_lo(smem_u32(smem) + C::kABytes, C::kBAtomBytes);
     int it = 0, tcount = 0;
     bool ok = true, any = false;
     for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++tcount) {
@@ -313,12 +318,13 @@ __global__ void __launch_bounds__(256, 1)
         const uint32_t ph = (it / C::kStages) & 1;
         if (!(ok = mbar_wait(bar_full + s, ph, abort_flag, kDevTimeoutKV))) break;
         tc_fence_after();
-        const uint32_t sa = base + s * C::kStageBytes;
-        const uint32_t sb = sa + C::kABytes;
+        uint32_t a_lo = a_lo0 + s * (C::kStageBytes >> 4);
+        uint32_t b_lo = b_lo0 + s * (C::kStageBytes >> 4);
+        asm volatile("" : "+r"(a_lo), "+r"(b_lo));  // formed per stage, not hoisted into registers
 #pragma unroll
         for (int kk = 0; kk < C::kBK / C::kKInstr; ++kk) {
-          const uint64_t ad = umma_desc_sw128(sa + kk * 32, 16, 1024);
-          const uint64_t bd = umma_desc_mn<sizeof(Tin)>(sb + kk * C::kKInstr * 128, C::kBAtomBytes);
+          const uint64_t ad = umma_desc_join(a_lo + ((kk * 32) >> 4), kHiA);
+          const uint64_t bd = umma_desc_join(b_lo + ((kk * C::kKInstr * 128) >> 4), kHiB);
           const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
           if constexpr (sizeof(Tin) == 4)
             mma_ss_tf32(d, ad, bd, idesc, acc);
