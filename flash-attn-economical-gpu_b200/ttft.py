@@ -641,9 +641,44 @@ def first_token(model: ModelShard, input_ids: torch.Tensor, backends: Backends, 
     return decoder_forward(model, input_ids, backends, group=group).argmax(dim=-1)
 
 
+class GraphedDecoder:
+    """decoder_forward for one prompt length, captured once into a CUDA graph and replayed.
+
+    A prefill is a few hundred kernel launches (per layer: norms, GEMMs, RoPE, attention segments,
+    all-reduces); replaying them as one graph removes the host time between them.  Every kernel of the
+    forward (this repository's through the C ABI, cuBLAS, NCCL) is launched on torch's current stream, which
+    is the capture stream while capturing.  The prompt is copied into a fixed input buffer before each
+    replay; the returned logits live in the graph's output buffer until the next replay.  Release it
+    (`close`) before the process group it all-reduces over is destroyed."""
+
+    def __init__(self, model: ModelShard, seq_len: int, backends: Backends, *, group=None, device=None):
+        device = device if device is not None else model.embed.device
+        self.ids = torch.zeros(1, seq_len, dtype=torch.long, device=device)
+        with torch.inference_mode():
+            side = torch.cuda.Stream(device)
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                for _ in range(2):  # first-call set-up (kernel attributes, NCCL communicators) outside the capture
+                    decoder_forward(model, self.ids, backends, group=group)
+            torch.cuda.current_stream(device).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.logits = decoder_forward(model, self.ids, backends, group=group)
+
+    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+        self.ids.copy_(input_ids)
+        self.graph.replay()
+        return self.logits
+
+    def close(self) -> None:
+        self.graph.reset()
+
+
 def time_decoder_ttft_ms(model: ModelShard, input_ids: torch.Tensor, backends: Backends, *, repeats: int,
-                         warmups: int, group=None) -> tuple[float, ...]:
-    """Wall-clock TTFT per prefill, synchronised on both sides (as ttft.py:461-478); max over ranks."""
+                         warmups: int, group=None, graphed: GraphedDecoder | None = None) -> tuple[float, ...]:
+    """Wall-clock TTFT per prefill, synchronised on both sides (as ttft.py:461-478); max over ranks.
+
+    With `graphed`, each prefill is a replay of that captured forward (input copy included)."""
     import torch.distributed as dist
 
     samples = []
@@ -653,7 +688,10 @@ def time_decoder_ttft_ms(model: ModelShard, input_ids: torch.Tensor, backends: B
                 dist.barrier(group=group)
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            tok = first_token(model, input_ids, backends, group=group)
+            if graphed is not None:
+                tok = graphed(input_ids).argmax(dim=-1)
+            else:
+                tok = first_token(model, input_ids, backends, group=group)
             torch.cuda.synchronize()
             ms = (time.perf_counter() - t0) * 1e3
             if dist.is_available() and dist.is_initialized():

@@ -119,3 +119,20 @@ def test_tensor_parallel_nccl_two_gpus(tmp_path, cuda_device):
     with torch.inference_mode():
         tp1 = ttft.decoder_forward(single, ids, ttft.Backends()).cpu()
     torch.testing.assert_close(tp2, tp1, rtol=0.1, atol=0.1)
+
+
+def test_cuda_graph_replay_matches_eager(cuda_device):
+    """The captured prefill replays to the same logits as the eager forward, for two different prompts."""
+    shard = ttft.build_model_shard(SEVEN_B, 1, 0, seed=12, device=cuda_device, num_layers=2)
+    graphed = ttft.GraphedDecoder(shard, 1024, ttft.Backends(), device=cuda_device)
+    try:
+        for seed in (13, 14):
+            ids = ttft._make_random_input_ids(1024, SEVEN_B.vocab_size, cuda_device, seed=seed)
+            with torch.inference_mode():
+                eager = ttft.decoder_forward(shard, ids, ttft.Backends())
+                replay = graphed(ids).clone()
+            assert torch.equal(replay, eager)
+    finally:
+        graphed.close()
+    del shard
+    torch.cuda.empty_cache()
