@@ -24,6 +24,9 @@ FAB_ERR_DEVICE_TIMEOUT = 4
 FAB_ERR_CUDA = 5
 FAB_ERR_WORKSPACE = 6
 
+FAB_GEMM_EPILOGUE_STORE = 0
+FAB_GEMM_EPILOGUE_SWIGLU = 1
+
 FAB_DTYPE_F16 = 0
 FAB_DTYPE_BF16 = 1
 FAB_DTYPE_F32 = 2
@@ -61,7 +64,7 @@ class FabGemmParams(ctypes.Structure):
         ("a", _vp), ("b", _vp), ("c", _vp),
         ("lda", _i64), ("ldb", _i64), ("ldc", _i64),
         ("M", _i32), ("N", _i32), ("K", _i32),
-        ("in_dtype", _i32), ("out_dtype", _i32), ("round_f16", _i32), ("group_m", _i32),
+        ("in_dtype", _i32), ("out_dtype", _i32), ("round_f16", _i32), ("group_m", _i32), ("epilogue", _i32),
     ]
 
 
@@ -135,7 +138,7 @@ PROTOTYPES = {
     "fab_ipc_close": (_i32, [_vp]),
     "fab_rmsnorm": (_i32, [_vp] * 5 + [_i32, _i32] + [_i64] * 4 + [_f32, _i32, _vp]),
     "fab_bias_rope": (_i32, [_vp] * 4 + [_i32] * 4 + [_i64, _i32, _vp]),
-    "fab_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp]),
+    "fab_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _i64, _i64, _i32, _i32, _vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),
     "fab_kernel_attrs_query": (_i32, [_i32, _i32, _i32, ctypes.POINTER(FabKernelAttrs)]),
     "fab_device_limits_query": (_i32, [_i32, ctypes.POINTER(FabDeviceLimits)]),
@@ -144,7 +147,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 def _load() -> ctypes.CDLL:

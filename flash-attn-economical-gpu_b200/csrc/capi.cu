@@ -254,7 +254,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 3; }
+int fab_abi_version(void) { return 4; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -503,10 +503,14 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
     if (dt != kDtypeF16 && dt != kDtypeBF16 && dt != kDtypeF32) return kErrInvalidArg;
   if (p->c == nullptr || !aligned16(p->c)) return kErrInvalidArg;
   const int oe = elt_size(p->out_dtype);
-  if ((p->ldc * oe) % 16 != 0 || p->ldc < p->N) return kErrInvalidArg;
+  if (p->epilogue != FAB_GEMM_EPILOGUE_STORE && p->epilogue != FAB_GEMM_EPILOGUE_SWIGLU) return kErrInvalidArg;
+  const bool swiglu = p->epilogue == FAB_GEMM_EPILOGUE_SWIGLU;
+  if (swiglu && (p->N % 128 != 0 || oe != 2 || p->round_f16)) return kErrInvalidArg;
+  const int c_cols = swiglu ? p->N / 2 : p->N;
+  if ((p->ldc * oe) % 16 != 0 || p->ldc < c_cols) return kErrInvalidArg;
   if (p->K == 0) {
-    // Empty contraction: C = 0.
-    cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(p->N) * oe, size_t(p->M),
+    // Empty contraction: C = 0 (also under SwiGLU: silu(0) * 0 = 0).
+    cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(c_cols) * oe, size_t(p->M),
                                       static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? kOk : kErrCuda;
   }
@@ -525,6 +529,7 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   L.out_dtype = p->out_dtype;
   L.round_f16 = p->round_f16;
   L.group_m = p->group_m;
+  L.swiglu = swiglu ? 1 : 0;
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
 }
 
@@ -681,8 +686,10 @@ int fab_bias_rope(void* y, const void* bias, const void* cos, const void* sin, i
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
-int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int dtype, void* stream) {
+int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int interleave, int dtype,
+                 void* stream) {
   if (rows < 0 || m <= 0 || m % 8 != 0 || gu == nullptr || a == nullptr) return kErrInvalidArg;
+  if (interleave != 0 && (interleave % 8 != 0 || m % interleave != 0)) return kErrInvalidArg;
   if (!al16(gu) || !al16(a) || !ld16(ld_gu) || !ld16(ld_a) || ld_gu < 2LL * m || ld_a < m) return kErrInvalidArg;
   if (dtype != kDtypeBF16 && dtype != kDtypeF16) return kErrUnsupported;
   const int64_t threads = static_cast<int64_t>(rows) * (m / 8);
@@ -691,10 +698,12 @@ int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_
   auto st = static_cast<cudaStream_t>(stream);
   if (dtype == kDtypeBF16) {
     using T = __nv_bfloat16;
-    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a);
+    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a,
+                                               interleave);
   } else {
     using T = __half;
-    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a);
+    silu_mul_kernel<T><<<blocks, 256, 0, st>>>(static_cast<const T*>(gu), static_cast<T*>(a), rows, m, ld_gu, ld_a,
+                                               interleave);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }

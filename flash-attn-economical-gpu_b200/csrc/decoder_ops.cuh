@@ -152,18 +152,22 @@ __global__ void __launch_bounds__(256) bias_rope_kernel(T* y, const T* __restric
   }
 }
 
-// a[s, j] = bf16(bf16(silu(g)) * u) with g = gu[s, j], u = gu[s, m + j].
+// a[s, j] = bf16(bf16(silu(g)) * u).  interleave 0: g = gu[s, j], u = gu[s, m + j];
+// interleave b: gu's columns alternate b gate and b up columns.
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ a, int rows, int m,
-                                                       int64_t ld_gu, int64_t ld_a) {
+                                                       int64_t ld_gu, int64_t ld_a, int interleave) {
   const int mv = m / 8;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(rows) * mv) return;
   const int64_t s = idx / mv;
   const int j = static_cast<int>(idx % mv);
+  const int col = j * 8;
+  const int gcol = interleave ? (col / interleave) * 2 * interleave + col % interleave : col;
+  const int ucol = interleave ? gcol + interleave : m + col;
   float g[8], u[8], o[8];
-  unpack8<T>(reinterpret_cast<const uint4*>(gu + s * ld_gu)[j], g);
-  unpack8<T>(reinterpret_cast<const uint4*>(gu + s * ld_gu + m)[j], u);
+  unpack8<T>(*reinterpret_cast<const uint4*>(gu + s * ld_gu + gcol), g);
+  unpack8<T>(*reinterpret_cast<const uint4*>(gu + s * ld_gu + ucol), u);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float sg = rnd<T>(g[e] / (1.0f + expf(-g[e])));

@@ -107,6 +107,9 @@ struct GemmKernelParams {
   int M, N, K;
   int group_m;
   int round_f16;
+  // SwiGLU epilogue: B's columns alternate 64 gate / 64 up columns, and C
+  // receives round(round(silu(round(g))) * round(u)), N / 2 columns.
+  int swiglu;
 };
 
 // Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output
@@ -133,6 +136,7 @@ struct GemmLaunch {
   int in_dtype, out_dtype;
   int round_f16;
   int group_m;
+  int swiglu;
 };
 
 int fa_select_config(int dtype, int D, FaConfigInfo* out);

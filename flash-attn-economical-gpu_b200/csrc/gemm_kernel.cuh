@@ -131,6 +131,15 @@ __device__ __forceinline__ void gemm_store_chunk(Tout* dst, const float (&v)[32]
   }
 }
 
+// x rounded to T's precision and back.
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return __bfloat162float(__float2bfloat16_rn(x));
+  else
+    return __half2float(__float2half_rn(x));
+}
+
 // 32 fp32 values as four 16-byte groups of 16-bit values.
 template <typename Tout>
 __device__ __forceinline__ void pack_chunk(const float (&v)[32], uint4 (&out)[4]) {
@@ -357,6 +366,34 @@ __global__ void __launch_bounds__(256, 1)
         int pm, pn;
         gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
         const int row = pm * C::kBM + r;
+        if constexpr (sizeof(Tout) == 2) {
+          if (p.swiglu) {
+            // Tile columns: gate 0-63, up 0-63, gate 64-127, up 64-127 of the
+            // 128 output columns starting at pn * 128.
+            const int o0 = pn * (C::kBN / 2);
+            Tout* orow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + o0;
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {  // 32 output columns each
+              const int cg = (q >> 1) * 4 + (q & 1);
+              uint32_t rg[32], ru[32];
+              tmem_ld32(tmem + lane_base + buf * C::kBN + cg * 32, rg);
+              tmem_ld32(tmem + lane_base + buf * C::kBN + (cg + 2) * 32, ru);
+              tmem_wait_ld();
+              float v[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const float g = round_to<Tout>(__uint_as_float(rg[e]));
+                const float u = round_to<Tout>(__uint_as_float(ru[e]));
+                v[e] = round_to<Tout>(g / (1.0f + expf(-g))) * u;
+              }
+              const int ncols = min(32, p.N / 2 - o0 - q * 32);
+              if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(orow + q * 32, v, ncols, false);
+            }
+            tc_fence_before();
+            mbar_arrive(bar_acc_empty + buf);
+            continue;
+          }
+        }
         const int n0 = pn * C::kBN;
         Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
 #pragma unroll 1
@@ -571,6 +608,7 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   kp.K = L.K;
   kp.group_m = L.group_m > 0 ? L.group_m : 8;
   kp.round_f16 = L.round_f16;
+  kp.swiglu = L.swiglu;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   int sms = num_sms();

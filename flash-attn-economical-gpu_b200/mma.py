@@ -55,9 +55,12 @@ def _gemm(
     ldc: int,
     round_f16: bool,
     group_m: int = 8,
+    epilogue: int = _native.FAB_GEMM_EPILOGUE_STORE,
     what: str = "gemm",
 ) -> None:
-    """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements)."""
+    """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements).
+
+    With the SwiGLU epilogue C is [M, N/2] (see `matmul_swiglu`)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         _require_cuda_tensor(name, t)
     if a.dtype != b.dtype:
@@ -70,6 +73,7 @@ def _gemm(
     p.out_dtype = _native.dtype_code(c.dtype)
     p.round_f16 = 1 if round_f16 else 0
     p.group_m = int(group_m)
+    p.epilogue = int(epilogue)
     with torch.cuda.device(a.device):
         rc = _native.lib.fab_gemm(ctypes.byref(p), ctypes.c_void_p(_native.current_stream_handle(a.device)))
     _native.check(rc, what)
@@ -172,10 +176,59 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, out_dtype: torch.dtype | None = 
     return c
 
 
+SWIGLU_BLOCK = 64  # gate/up column interleave of the SwiGLU epilogue
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """[K, 2m] weight whose columns alternate `block` gate and `block` up columns (m a multiple of block)."""
+    if w_gate.shape != w_up.shape or w_gate.ndim != 2 or w_gate.shape[1] % block != 0:
+        raise ValueError(f"interleave_gate_up expects two [K, m] weights with m % {block} == 0, "
+                         f"got {tuple(w_gate.shape)} and {tuple(w_up.shape)}")
+    K, m = w_gate.shape
+    return torch.stack([w_gate.reshape(K, m // block, block), w_up.reshape(K, m // block, block)],
+                       dim=2).reshape(K, 2 * m).contiguous()
+
+
+def split_gate_up(gu: torch.Tensor, block: int = SWIGLU_BLOCK) -> tuple[torch.Tensor, torch.Tensor]:
+    """The gate and up halves [.., m] of an interleaved [.., 2m] product (copies)."""
+    *lead, two_m = gu.shape
+    v = gu.reshape(*lead, two_m // (2 * block), 2, block)
+    return v[..., 0, :].reshape(*lead, two_m // 2), v[..., 1, :].reshape(*lead, two_m // 2)
+
+
+def matmul_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(a @ W_gate) * (a @ W_up) [M, m] in one kernel, for w_gate_up = interleave_gate_up(W_gate, W_up).
+
+    No counterpart in the reference (its matmul has one epilogue).  The tcgen05 GEMM's epilogue warps read
+    each 64-column gate block and its up block from the same accumulator tile and store only the product,
+    rounding as the PyTorch expression does in a's 16-bit dtype: silu of the rounded gate product, rounded,
+    times the rounded up product, rounded."""
+    if a.ndim != 2 or w_gate_up.ndim != 2 or a.shape[1] != w_gate_up.shape[0]:
+        raise ValueError(f"matmul_swiglu expects a [M, K] and w [K, 2m], got {tuple(a.shape)} and "
+                         f"{tuple(w_gate_up.shape)}")
+    if a.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"matmul_swiglu needs float16 or bfloat16 operands, got {a.dtype}")
+    M, K = a.shape
+    N = w_gate_up.shape[1]
+    if N % (2 * SWIGLU_BLOCK) != 0:
+        raise ValueError(f"matmul_swiglu needs 2m a multiple of {2 * SWIGLU_BLOCK}, got {N}")
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if w_gate_up.stride(1) != 1:
+        w_gate_up = w_gate_up.contiguous()
+    c = torch.empty((M, N // 2), device=a.device, dtype=a.dtype) if out is None else out
+    _gemm(a, w_gate_up, c, M, N, K, lda=a.stride(0), ldb=w_gate_up.stride(0), ldc=c.stride(0), round_f16=False,
+          epilogue=_native.FAB_GEMM_EPILOGUE_SWIGLU, what="matmul_swiglu")
+    return c
+
+
 __all__ = [
     "_select_2d_contiguous_config",
     "_supports_contiguous_cache_eviction_hints",
     "_matmul_contiguous_kernel",
     "matmul",
+    "matmul_swiglu",
+    "interleave_gate_up",
+    "split_gate_up",
     "get_architecture",
 ]

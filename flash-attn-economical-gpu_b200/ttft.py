@@ -43,6 +43,7 @@ import torch
 import torch.nn.functional as F
 
 from flash_atten import attention_forward, flash_attention
+from mma import SWIGLU_BLOCK, interleave_gate_up, matmul_swiglu, split_gate_up
 from tuner import FlashAttentionBlockDNomaskTuner, FlashAttenTuneArguments
 
 try:
@@ -328,8 +329,10 @@ def head_partition(num_heads: int, world: int, rank: int) -> range:
     return range(start, start + base + (1 if rank < extra else 0))
 
 
-def column_partition(size: int, world: int, rank: int) -> range:
-    return head_partition(size, world, rank)
+def column_partition(size: int, world: int, rank: int, unit: int = 1) -> range:
+    """Contiguous columns of `rank` in whole `unit`s (size a multiple of unit)."""
+    r = head_partition(size // unit, world, rank)
+    return range(r.start * unit, r.stop * unit)
 
 
 @dataclass(frozen=True)
@@ -347,6 +350,8 @@ def rank_plan(arch: ArchConfig, world: int, rank: int) -> RankPlan:
         raise ValueError(f"bad rank {rank} of {world}")
     if world > arch.num_attention_heads:
         raise ValueError("more ranks than query heads")
+    if arch.intermediate_size % SWIGLU_BLOCK != 0:
+        raise ValueError(f"intermediate_size must be a multiple of {SWIGLU_BLOCK} (the gate/up interleave block)")
     group = arch.num_attention_heads // arch.num_key_value_heads
     q_heads = head_partition(arch.num_attention_heads, world, rank)
     kv_needed: list[int] = []
@@ -360,7 +365,7 @@ def rank_plan(arch: ArchConfig, world: int, rank: int) -> RankPlan:
             first, count, idx = segments[-1]
             segments[-1] = (first, count + 1, idx)
     return RankPlan(q_heads, tuple(kv_needed), tuple(segments),
-                    column_partition(arch.intermediate_size, world, rank))
+                    column_partition(arch.intermediate_size, world, rank, SWIGLU_BLOCK))
 
 
 def _seeded_normal(shape, seed: int, device, std: float = 0.02, dtype=DTYPE) -> torch.Tensor:
@@ -375,7 +380,7 @@ class LayerShard:
     b_qkv: torch.Tensor | None   # [(nq + 2*nkv) * head_dim]
     w_o: torch.Tensor            # [nq * head_dim, hidden]
     ln_post: torch.Tensor
-    w_gate_up: torch.Tensor      # [hidden, 2 * mlp_local]
+    w_gate_up: torch.Tensor      # [hidden, 2 * mlp_local]: 64 gate, 64 up columns alternating (mma.interleave_gate_up)
     w_down: torch.Tensor         # [mlp_local, hidden]
 
 
@@ -430,7 +435,7 @@ def shard_layer(arch: ArchConfig, plan: RankPlan, w: dict[str, torch.Tensor]) ->
         b_qkv=b_qkv,
         w_o=w["o"][qcols].contiguous(),
         ln_post=w["ln_post"],
-        w_gate_up=torch.cat([w["gate"][:, m], w["up"][:, m]], dim=1).contiguous(),
+        w_gate_up=interleave_gate_up(w["gate"][:, m], w["up"][:, m]),
         w_down=w["down"][m].contiguous(),
     )
 
@@ -550,7 +555,7 @@ def _native_silu_mul(gu: torch.Tensor) -> torch.Tensor:
     a = torch.empty(rows, two_m // 2, device=gu.device, dtype=gu.dtype)
     stream = ctypes.c_void_p(_native.current_stream_handle(gu.device))
     rc = _native.lib.fab_silu_mul(gu.data_ptr(), a.data_ptr(), rows, two_m // 2, gu.stride(0), a.stride(0),
-                                  _native.dtype_code(gu.dtype), stream)
+                                  SWIGLU_BLOCK, _native.dtype_code(gu.dtype), stream)
     _native.check(rc, "fab_silu_mul")
     return a
 
@@ -616,9 +621,15 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
         else:
             x = x + o
             h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
-        gu = _matmul(h, layer.w_gate_up, backends.gemm)
-        m = gu.shape[1] // 2
-        a = _native_silu_mul(gu) if native else F.silu(gu[:, :m]) * gu[:, m:]
+        if native and backends.gemm == "native":
+            a = matmul_swiglu(h, layer.w_gate_up)  # gate/up GEMM with SwiGLU in its epilogue
+        else:
+            gu = _matmul(h, layer.w_gate_up, backends.gemm)
+            if native:
+                a = _native_silu_mul(gu)
+            else:
+                g, u = split_gate_up(gu)
+                a = F.silu(g) * u
         if backends.fused_allreduce is not None:
             d = backends.fused_allreduce(a, layer.w_down)
         else:

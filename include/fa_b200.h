@@ -215,8 +215,20 @@ typedef struct fab_gemm_params {
   int in_dtype;
   int out_dtype;
   int round_f16;
-  int group_m; /* tile-row group for L2 reuse, 0 = default (8) */
+  int group_m;  /* tile-row group for L2 reuse, 0 = default (8) */
+  int epilogue; /* FAB_GEMM_EPILOGUE_*; 0 = store C */
 } fab_gemm_params;
+
+/*
+ * FAB_GEMM_EPILOGUE_SWIGLU (no counterpart in the reference): B's N columns
+ * alternate 64 gate and 64 up columns, and C [M, N/2] receives
+ * round(round(silu(round(gate))) * round(up)) for each pair -- a SwiGLU MLP's
+ * gate/up projection and activation in one kernel, rounding as the PyTorch
+ * expression silu(x @ W_gate) * (x @ W_up) does in the 16-bit output type.
+ * N a multiple of 128; 16-bit output; round_f16 0.
+ */
+#define FAB_GEMM_EPILOGUE_STORE 0
+#define FAB_GEMM_EPILOGUE_SWIGLU 1
 
 int fab_gemm(const fab_gemm_params* params, void* stream);
 
@@ -287,13 +299,16 @@ int fab_ipc_close(void* base);
  *   bias [heads * head_dim] (may be NULL) to every head, then applies
  *   rotate-half rotary embedding (cos/sin [rows, head_dim]) to the first
  *   rot_heads heads: y = round(round(y * cos) + round(rotate_half(y) * sin)).
- * fab_silu_mul: a[:, j] = round(round(silu(gu[:, j])) * gu[:, m + j]).
+ * fab_silu_mul: a[:, j] = round(round(silu(g_j)) * u_j) with g_j = gu[:, j],
+ *   u_j = gu[:, m + j] (interleave 0), or gu's columns alternating
+ *   `interleave` gate and `interleave` up columns (the SwiGLU GEMM layout).
  */
 int fab_rmsnorm(const void* x, const void* residual, const void* w, void* h, void* x_out, int rows, int cols,
                 int64_t ld_x, int64_t ld_res, int64_t ld_h, int64_t ld_xo, float eps, int dtype, void* stream);
 int fab_bias_rope(void* y, const void* bias, const void* cos, const void* sin, int rows, int heads, int rot_heads,
                   int head_dim, int64_t ld, int dtype, void* stream);
-int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int dtype, void* stream);
+int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int interleave, int dtype,
+                 void* stream);
 
 /*
  * Static sm_100a tile table that replaces the reference tuner's compile-and-rank

@@ -113,6 +113,14 @@ def test_null_and_bad_arguments_are_rejected_before_any_launch():
     # Empty problems are a no-op.
     p.M, p.N, p.in_dtype = 0, 8, 0
     assert lib.fab_gemm(ctypes.byref(p), None) == _native.FAB_OK
+    # SwiGLU epilogue: 2m a multiple of 128, 16-bit output, no fp16 pre-rounding, an unknown mode rejected.
+    p.M, p.N, p.K, p.in_dtype, p.out_dtype, p.c, p.ldc = 8, 256, 64, 1, 1, 4096, 128
+    for bad in (dict(epilogue=2), dict(epilogue=1, N=192), dict(epilogue=1, out_dtype=2, ldc=256),
+                dict(epilogue=1, round_f16=1), dict(epilogue=1, ldc=120)):
+        q = _native.FabGemmParams.from_buffer_copy(p)
+        for key, val in bad.items():
+            setattr(q, key, val)
+        assert lib.fab_gemm(ctypes.byref(q), None) == _native.FAB_ERR_INVALID_ARG, bad
     a = _native.FabAttentionParams()
     a.batch, a.heads_q, a.heads_kv, a.seqlen_q, a.seqlen_k, a.head_dim, a.dtype = 1, 4, 3, 16, 16, 64, 1
     a.sm_scale = 0.125

@@ -13,6 +13,7 @@ import torch.nn.functional as F
 
 import _native
 import ttft
+from mma import split_gate_up
 
 pytestmark = pytest.mark.gpu
 
@@ -63,9 +64,26 @@ def test_bias_rope_matches_torch_bit_for_bit(with_bias, cuda_device):
 
 
 def test_silu_mul_matches_torch_bit_for_bit(cuda_device):
+    """The interleaved gate/up layout the decoder's weights use."""
     g = torch.Generator(device=cuda_device).manual_seed(8)
     gu = (3 * torch.randn(777, 2 * 2368, generator=g, device=cuda_device)).to(torch.bfloat16)
-    m = gu.shape[1] // 2
-    ref = F.silu(gu[:, :m]) * gu[:, m:]
+    gate, up = split_gate_up(gu)
+    ref = F.silu(gate) * up
     out = ttft._native_silu_mul(gu)
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_silu_mul_concatenated_halves(dtype, cuda_device):
+    """interleave 0: gate in the first m columns, up in the last m (through the C ABI)."""
+    import ctypes
+
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    gu = (3 * torch.randn(300, 2 * 520, generator=g, device=cuda_device)).to(dtype)
+    m = gu.shape[1] // 2
+    out = torch.empty(300, m, device=cuda_device, dtype=dtype)
+    rc = _native.lib.fab_silu_mul(gu.data_ptr(), out.data_ptr(), 300, m, gu.stride(0), out.stride(0), 0,
+                                  _native.dtype_code(dtype),
+                                  ctypes.c_void_p(_native.current_stream_handle(gu.device)))
+    _native.check(rc, "fab_silu_mul")
+    assert torch.equal(out, F.silu(gu[:, :m]) * gu[:, m:])

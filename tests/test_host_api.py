@@ -237,3 +237,23 @@ def test_measured_variant_lookup(tmp_path):
     assert tune_table.measured_variant(bf16, 128, True, 8, 600, 600, path=table) == 0  # nothing causal measured
     assert tune_table.measured_variant(bf16, 256, False, 8, 600, 600, path=table) == 0  # one family only
     assert tune_table.measured_variant(bf16, 128, False, 8, 600, 600, path=tmp_path / "missing.json") == 0
+
+
+def test_gate_up_interleave_round_trip():
+    g = torch.Generator().manual_seed(4)
+    wg, wu = torch.randn(5, 192, generator=g), torch.randn(5, 192, generator=g)
+    w = mma.interleave_gate_up(wg, wu)
+    assert w.shape == (5, 384)
+    assert torch.equal(w[:, :64], wg[:, :64]) and torch.equal(w[:, 64:128], wu[:, :64])
+    assert torch.equal(w[:, 256:320], wg[:, 128:])
+    gate, up = mma.split_gate_up(w)
+    assert torch.equal(gate, wg) and torch.equal(up, wu)
+    with pytest.raises(ValueError):
+        mma.interleave_gate_up(torch.zeros(5, 100), torch.zeros(5, 100))
+
+
+def test_matmul_swiglu_refuses_cpu_and_odd_widths():
+    with pytest.raises(ValueError):
+        mma.matmul_swiglu(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(8, 192, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        mma.matmul_swiglu(torch.zeros(4, 8), torch.zeros(8, 256))

@@ -30,6 +30,7 @@ def test_rank_plan_covers_every_head_once(world):
             heads = p.q_heads[first:first + count]
             assert {h // group for h in heads} == {p.kv_heads[kv]}
         assert sum(c for _, c, _ in p.segments) == len(p.q_heads)
+        assert len(p.mlp_cols) % 64 == 0  # whole gate/up interleave blocks
     assert seen_q == list(range(SEVEN_B.num_attention_heads))
     assert mlp == list(range(SEVEN_B.intermediate_size))
 
