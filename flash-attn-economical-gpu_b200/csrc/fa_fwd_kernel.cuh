@@ -7,7 +7,10 @@
 // to the input dtype before the P*V product, final O = acc / l.
 //
 // B200 structure (one CTA per SM, 128 + NQ*128 threads):
-//   warp 0      TMA producer: Q tiles once, then a ring of K and V tiles.
+//   warp 0      TMA producer: Q tiles once, then K and V tiles alternating
+//               through one ring of kRing tile slots (K_j is ring tile 2j,
+//               V_j ring tile 2j+1), so every slot the Q tiles leave free in
+//               shared memory adds load lead time.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
 //   warps 4..   one 128-thread softmax group per 128-row Q tile; thread r of
 //               the group owns row r (TMEM lane r) for the whole kernel.
@@ -43,7 +46,7 @@
 
 namespace fab {
 
-template <int kElt, int kDP, int kNQ, int kBN, int kStages, int kSB>
+template <int kElt, int kDP, int kNQ, int kBN, int kRing, int kSB>
 struct FaCfg {
   static constexpr int kBM = 128;                    // rows per Q tile (TMEM lanes)
   static constexpr int kAtom = 128 / kElt;           // elements per 128-byte swizzle atom
@@ -67,8 +70,13 @@ struct FaCfg {
   static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                     : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 * kSlots + kNQ + 1;
-  static constexpr int kDataBytes = kNQ * kQTileBytes + 2 * kStages * kKVTileBytes;
+  static constexpr int kNumBars = 1 + 2 * kRing + 2 * kSlots + kNQ + 1;
+  static constexpr int kDataBytes = kNQ * kQTileBytes + kRing * kKVTileBytes;
+  // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
+  // ring tiles 2j+1 .. 2j+4 are resident together.
+  // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
+  // ring tiles 2j+1 .. 2j+4 are resident together.
+  static_assert(kRing >= 2 * kSB && kRing >= 2, "K/V ring too short for the S buffering");
   static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
   static_assert(kTmemUsed <= 512, "TMEM budget");
@@ -139,26 +147,23 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
   }
 }
 
-template <typename T, int kDP, int kNQ, int kBN, int kStages, int kSB>
+template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
 __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     fa_fwd_kernel(const __grid_constant__ FaKernelParams p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
-  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages, kSB>;
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kRing, kSB>;
   constexpr float kNegInf = -INFINITY;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kNQ * C::kQTileBytes;
-  uint8_t* sV = sK + kStages * C::kKVTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kStages * C::kKVTileBytes);
+  uint8_t* sKV = sQ + kNQ * C::kQTileBytes;  // [kRing] K or V tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kRing * C::kKVTileBytes);
   uint64_t* bar_q_full = bars;
-  uint64_t* bar_k_full = bars + 1;
-  uint64_t* bar_v_full = bar_k_full + kStages;
-  uint64_t* bar_k_empty = bar_v_full + kStages;
-  uint64_t* bar_v_empty = bar_k_empty + kStages;
-  uint64_t* bar_s_full = bar_v_empty + kStages;  // [kSlots]
+  uint64_t* bar_kv_full = bars + 1;               // [kRing]
+  uint64_t* bar_kv_empty = bar_kv_full + kRing;   // [kRing]
+  uint64_t* bar_s_full = bar_kv_empty + kRing;    // [kSlots]
   uint64_t* bar_p_full = bar_s_full + C::kSlots; // [kSlots]
   uint64_t* bar_o_done = bar_p_full + C::kSlots; // [kNQ]
   uint64_t* bar_teardown = bar_o_done + kNQ;
@@ -204,11 +209,9 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar_k_full + s, 1);
-      mbar_init(bar_v_full + s, 1);
-      mbar_init(bar_k_empty + s, 1);
-      mbar_init(bar_v_empty + s, 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(bar_kv_full + s, 1);
+      mbar_init(bar_kv_empty + s, 1);
     }
     for (int x = 0; x < C::kSlots; ++x) {
       mbar_init(bar_s_full + x, 1);
@@ -245,34 +248,26 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       for (int a = 0; a < C::kNumAtoms; ++a)
         tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full, a * C::kAtom,
                     q_row0 + m0 + i * C::kBM, h, map_b);
+    // Ring tile t: K_{t/2} for even t, V_{t/2} for odd t, in slot t % kRing.
     int issued = 0;
-    for (int j = 0; j < nt; ++j) {
-      const int s = j % kStages;
-      const uint32_t ph = (j / kStages) & 1;
-      if (!mbar_wait(bar_k_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
-      mbar_arrive_expect_tx(bar_k_full + s, C::kKVTileBytes);
+    for (int t = 0; t < 2 * nt; ++t) {
+      const int s = t % kRing;
+      const uint32_t ph = (t / kRing) & 1;
+      if (!mbar_wait(bar_kv_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
+      mbar_arrive_expect_tx(bar_kv_full + s, C::kKVTileBytes);
+      const CUtensorMap* map = (t & 1) ? &tm_v : &tm_k;
+      const int row = k_row0 + n_begin + (t >> 1) * kBN;
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sK + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_k, bar_k_full + s, a * C::kAtom, k_row0 + n_begin + j * kBN,
-                    hk, map_b);
-      if (!mbar_wait(bar_v_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) {
-        issued = 2 * j + 1;
-        break;
-      }
-      mbar_arrive_expect_tx(bar_v_full + s, C::kKVTileBytes);
-      for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sV + s * C::kKVTileBytes + a * C::kKVAtomBytes, &tm_v, bar_v_full + s, a * C::kAtom, k_row0 + n_begin + j * kBN,
-                    hk, map_b);
-      issued = 2 * j + 2;
+        tma_load_4d(sKV + s * C::kKVTileBytes + a * C::kKVAtomBytes, map, bar_kv_full + s, a * C::kAtom, row, hk,
+                    map_b);
+      issued = t + 1;
     }
     // Never leave this CTA with bulk copies still landing in its smem: wait
-    // (bounded) for the last load issued into every stage.
+    // (bounded) for the last load issued into every slot.
     volatile int no_abort = 0;
     mbar_wait(bar_q_full, 0, &no_abort, kDevTimeoutTeardown);
-    for (int x = max(0, issued - 2 * kStages); x < issued; ++x) {
-      const int j = x >> 1;
-      uint64_t* full = (x & 1) ? bar_v_full : bar_k_full;
-      mbar_wait(full + (j % kStages), (j / kStages) & 1, &no_abort, kDevTimeoutTeardown);
-    }
+    for (int x = max(0, issued - kRing); x < issued; ++x)
+      mbar_wait(bar_kv_full + (x % kRing), (x / kRing) & 1, &no_abort, kDevTimeoutTeardown);
   } else if (!skip && warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t kFmt = ElemOps<T>::kFmt;
@@ -285,8 +280,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     constexpr uint32_t kHiK = umma_desc_hi(1024, kLayoutSw128);
     constexpr uint32_t kHiV = sizeof(T) == 4 ? umma_desc_hi(512, kLayoutSw128Base32B) : umma_desc_hi(1024, kLayoutSw128);
     const uint32_t q_lo = umma_desc_lo(smem_u32(sQ), 16);
-    const uint32_t k_lo = umma_desc_lo(smem_u32(sK), 16);
-    const uint32_t v_lo = umma_desc_lo(smem_u32(sV), C::kKVAtomBytes);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(sKV), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(sKV), C::kKVAtomBytes);
+    // Ring slot and phase of K_j (tile 2j) and V_j (tile 2j+1).
+    auto kslot = [](int j) { return (2 * j) % kRing; };
+    auto kpar = [](int j) { return static_cast<uint32_t>(((2 * j) / kRing) & 1); };
+    auto vslot = [](int j) { return (2 * j + 1) % kRing; };
+    auto vpar = [](int j) { return static_cast<uint32_t>(((2 * j + 1) / kRing) & 1); };
     auto issue_qk = [&](int i, int slot, int s) {
       const uint32_t d = tmem + C::tmem_s(slot);
       uint32_t qa = q_lo + i * (C::kQTileBytes >> 4);
@@ -327,26 +327,26 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     bool any_issued = false;
     // Prologue: S for the first kSB KV tiles of every Q tile.
     for (int j = 0; ok && j < min(kSB, nt); ++j) {
-      if (!(ok = mbar_wait(bar_k_full + (j % kStages), (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+      if (!(ok = mbar_wait(bar_kv_full + kslot(j), kpar(j), abort_flag, kDevTimeoutKV))) break;
       tc_fence_after();
       for (int i = 0; i < kNQ; ++i) {
-        issue_qk(i, i * kSB + j, j % kStages);
+        issue_qk(i, i * kSB + j, kslot(j));
         mma_commit(bar_s_full + i * kSB + j);
       }
-      mma_commit(bar_k_empty + (j % kStages));
+      mma_commit(bar_kv_empty + kslot(j));
       any_issued = true;
     }
     for (int j = 0; ok && j < nt; ++j) {
-      const int s = j % kStages;
+      const int s = vslot(j);
       const int jn = j + kSB;  // the KV tile whose S product reuses this S buffer
-      const int sn = jn % kStages;
-      if (!(ok = mbar_wait(bar_v_full + s, (j / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+      const int sn = kslot(jn);
+      if (!(ok = mbar_wait(bar_kv_full + s, vpar(j), abort_flag, kDevTimeoutKV))) break;
       if constexpr (kSB == 1) {
         // Two Q tiles.  Each MMA burst is followed by a stall of a few hundred
         // cycles before the issuing thread's next instruction, so P_i*V(j)
         // and S_i(j+1) go out back to back: K(j+1) (loaded an iteration ago)
         // is waited for up front and the K/V release commits come last.
-        if (jn < nt && !(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+        if (jn < nt && !(ok = mbar_wait(bar_kv_full + sn, kpar(jn), abort_flag, kDevTimeoutKV))) break;
         for (int i = 0; i < kNQ; ++i) {
           const int slot = i;
           if (!(ok = mbar_wait(bar_p_full + slot, j & 1, abort_flag, kDevTimeoutP))) break;
@@ -357,8 +357,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
           if (jn < nt) mma_commit(bar_s_full + slot);
         }
         if (!ok) break;
-        mma_commit(bar_v_empty + s);
-        if (jn < nt) mma_commit(bar_k_empty + sn);
+        mma_commit(bar_kv_empty + s);
+        if (jn < nt) mma_commit(bar_kv_empty + sn);
       } else {
         // Two S buffers per Q tile: S_i(j+1) is already in TMEM while the
         // softmax works on tile j.  The softmax of tile j+1 waits for
@@ -374,16 +374,16 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
           mma_commit(bar_o_done + i);
         }
         if (!ok) break;
-        mma_commit(bar_v_empty + s);
+        mma_commit(bar_kv_empty + s);
         if (jn < nt) {
-          if (!(ok = mbar_wait(bar_k_full + sn, (jn / kStages) & 1, abort_flag, kDevTimeoutKV))) break;
+          if (!(ok = mbar_wait(bar_kv_full + sn, kpar(jn), abort_flag, kDevTimeoutKV))) break;
           tc_fence_after();
           for (int i = 0; i < kNQ; ++i) {
             const int slot = i * kSB + j % kSB;
             issue_qk(i, slot, sn);
             mma_commit(bar_s_full + slot);
           }
-          mma_commit(bar_k_empty + sn);
+          mma_commit(bar_kv_empty + sn);
         }
       }
     }
@@ -580,10 +580,10 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
 // ---------------------------------------------------------------- host side
 
-template <typename T, int kDP, int kNQ, int kBN, int kStages, int kSB>
+template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
 static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
-  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kStages, kSB>;
-  auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kStages, kSB>;
+  using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kRing, kSB>;
+  auto kern = fa_fwd_kernel<T, kDP, kNQ, kBN, kRing, kSB>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
   if constexpr (C::kSplitRegs) {
@@ -742,13 +742,15 @@ __global__ void __launch_bounds__(kCombineWarps * 32) fa_split_combine_kernel(
   if (lse != nullptr && threadIdx.x == 0) lse[b * l_sb + h * l_sh + m * l_sm] = mx + logf(total_w);
 }
 
-// The sm_100a tile table: one instantiation per (element size, padded head dim).
-#define FAB_FA_TABLE(X)                                  \
-  X(2, 64, 2, 128, 3, 1)    /* 16-bit, head dim <= 64 */  \
-  X(2, 128, 2, 128, 2, 1)   /* 16-bit, head dim <= 128 */ \
-  X(2, 256, 1, 64, 2, 2)    /* 16-bit, head dim <= 256 */ \
-  X(4, 64, 2, 128, 2, 1)    /* fp32/tf32, head dim <= 64 */ \
-  X(4, 128, 1, 64, 2, 2)    /* fp32/tf32, head dim <= 128 */
+// The sm_100a tile table: one instantiation per (element size, padded head
+// dim).  Columns: element size, padded head dim, Q tiles per CTA, BLOCK_N,
+// K/V ring slots (as many tiles as fit beside the Q tiles), S buffers.
+#define FAB_FA_TABLE(X)                                    \
+  X(2, 64, 2, 128, 10, 1)   /* 16-bit, head dim <= 64 */    \
+  X(2, 128, 2, 128, 5, 1)   /* 16-bit, head dim <= 128 */   \
+  X(2, 256, 1, 64, 5, 2)    /* 16-bit, head dim <= 256 */   \
+  X(4, 64, 2, 128, 5, 1)    /* fp32/tf32, head dim <= 64 */ \
+  X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
 
 static bool fa_table_lookup(int elt, int D, int* d_pad) {
   int best = 0;
@@ -816,11 +818,11 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream) {
 // while the softmax of tile j runs and the CTA streams K/V at the rate the
 // memory system gives it.
 #define FAB_FA_SPLIT_TABLE(X)                              \
-  X(2, 64, 1, 128, 3, 2)    /* 16-bit, head dim <= 64 */    \
-  X(2, 128, 1, 128, 2, 2)   /* 16-bit, head dim <= 128 */   \
-  X(2, 256, 1, 64, 2, 2)    /* 16-bit, head dim <= 256 */   \
-  X(4, 64, 1, 128, 2, 2)    /* fp32/tf32, head dim <= 64 */ \
-  X(4, 128, 1, 64, 2, 2)    /* fp32/tf32, head dim <= 128 */
+  X(2, 64, 1, 128, 8, 2)    /* 16-bit, head dim <= 64 */    \
+  X(2, 128, 1, 128, 6, 2)   /* 16-bit, head dim <= 128 */   \
+  X(2, 256, 1, 64, 5, 2)    /* 16-bit, head dim <= 256 */   \
+  X(4, 64, 1, 128, 6, 2)    /* fp32/tf32, head dim <= 64 */ \
+  X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
 
 int fa_select_split_config(int dtype, int D, FaConfigInfo* out) {
   if (D <= 0) return kErrInvalidArg;

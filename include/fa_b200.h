@@ -319,7 +319,7 @@ typedef struct fab_fa_config {
   int head_dim_padded; /* head_dim rounded up to whole 128-byte swizzle atoms */
   int q_tiles_per_cta; /* 128-row query tiles per CTA (BLOCK_M = 128 * this) */
   int block_n;         /* keys per KV tile */
-  int stages;          /* K and V ring depth */
+  int stages;          /* K/V ring slots: K and V tiles alternate in one ring */
   int threads;
   int smem_bytes;
   int tmem_columns;

@@ -75,13 +75,13 @@ def test_return_code_mapping():
 @pytest.mark.parametrize(
     "dtype, D, expect",
     [
-        # (head_dim_padded, q_tiles_per_cta, block_n, stages, s_buffers)
-        (_native.FAB_DTYPE_BF16, 64, (64, 2, 128, 3, 1)),
-        (_native.FAB_DTYPE_BF16, 128, (128, 2, 128, 2, 1)),
-        (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 2, 1)),
-        (_native.FAB_DTYPE_F16, 256, (256, 1, 64, 2, 2)),
-        (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 2, 1)),
-        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 2, 2)),
+        # (head_dim_padded, q_tiles_per_cta, block_n, K/V ring slots, s_buffers)
+        (_native.FAB_DTYPE_BF16, 64, (64, 2, 128, 10, 1)),
+        (_native.FAB_DTYPE_BF16, 128, (128, 2, 128, 5, 1)),
+        (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 5, 1)),
+        (_native.FAB_DTYPE_F16, 256, (256, 1, 64, 5, 2)),
+        (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 5, 1)),
+        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 5, 2)),
     ],
 )
 def test_tile_table(dtype, D, expect):

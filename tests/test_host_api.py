@@ -79,7 +79,7 @@ def test_tuner_candidates_are_the_compiled_tile_families(fake_limits):
     two, one = t._candidate_configs()
     assert two["variant"] == 0 and one["variant"] == 1
     assert two["BLOCK_M"] == 256 and two["BLOCK_N"] == 128 and two["BLOCK_DMODEL"] == 128
-    assert two["num_warps"] == 12 and two["num_stages"] == 2
+    assert two["num_warps"] == 12 and two["num_stages"] == 5
     assert one["BLOCK_M"] == 128 and one["BLOCK_N"] == 128 and one["num_warps"] == 8
     # D=256: both families name the same tile, so it is the only candidate
     t256 = FlashAttentionOptimizeSharedMemTuner((2, 16, 64, 256), (2, 16, 64, 256), (2, 16, 64, 256), 2,
