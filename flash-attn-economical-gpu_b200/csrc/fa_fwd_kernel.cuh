@@ -249,11 +249,21 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full, a * C::kAtom,
                     q_row0 + m0 + i * C::kBM, h, map_b);
     // Ring tile t: K_{t/2} for even t, V_{t/2} for odd t, in slot t % kRing.
+    // With one S buffer the MMA thread frees V_j and K_{j+1} with one commit
+    // (release group j+1; group 0 is K_0), on barrier group % kRing; with two,
+    // every slot has its own release.
     int issued = 0;
     for (int t = 0; t < 2 * nt; ++t) {
       const int s = t % kRing;
       const uint32_t ph = (t / kRing) & 1;
-      if (!mbar_wait(bar_kv_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
+      if constexpr (kSB == 1) {
+        if (t >= kRing) {
+          const int g = (t - kRing + 1) >> 1;  // release group of the slot's previous tile
+          if (!mbar_wait(bar_kv_empty + g % kRing, (g / kRing) & 1, abort_flag, kDevTimeoutEmpty)) break;
+        }
+      } else {
+        if (!mbar_wait(bar_kv_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
+      }
       mbar_arrive_expect_tx(bar_kv_full + s, C::kKVTileBytes);
       const CUtensorMap* map = (t & 1) ? &tm_v : &tm_k;
       const int row = k_row0 + n_begin + (t >> 1) * kBN;
@@ -357,8 +367,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
           if (jn < nt) mma_commit(bar_s_full + slot);
         }
         if (!ok) break;
-        mma_commit(bar_kv_empty + s);
-        if (jn < nt) mma_commit(bar_kv_empty + sn);
+        mma_commit(bar_kv_empty + (j + 1) % kRing);  // release group j+1: V_j and K_{j+1}
       } else {
         // Two S buffers per Q tile: S_i(j+1) is already in TMEM while the
         // softmax works on tile j.  The softmax of tile j+1 waits for
