@@ -641,10 +641,28 @@ int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t str
   return kErrUnsupported;
 }
 
+}  // namespace fab
+
+#include "gemm_pair_kernel.cuh"
+
+namespace fab {
+
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
   if (L.M < 0 || L.N < 0 || L.K < 0) return kErrInvalidArg;
   if (L.M == 0 || L.N == 0) return 0;
   const int in = L.in_dtype, out = L.out_dtype;
+  if (L.K > 0 && gemm_use_pair(L)) {
+    if (in == kDtypeF16) {
+      if (out == kDtypeF16) return launch_gemm_pair<__half, __half>(L, stream);
+      if (out == kDtypeBF16) return launch_gemm_pair<__half, __nv_bfloat16>(L, stream);
+      if (out == kDtypeF32) return launch_gemm_pair<__half, float>(L, stream);
+    } else {
+      if (out == kDtypeF16) return launch_gemm_pair<__nv_bfloat16, __half>(L, stream);
+      if (out == kDtypeBF16) return launch_gemm_pair<__nv_bfloat16, __nv_bfloat16>(L, stream);
+      if (out == kDtypeF32) return launch_gemm_pair<__nv_bfloat16, float>(L, stream);
+    }
+    return kErrInvalidArg;
+  }
   if (in == kDtypeF16) {
     if (out == kDtypeF16) return launch_gemm<__half, __half>(L, stream);
     if (out == kDtypeBF16) return launch_gemm<__half, __nv_bfloat16>(L, stream);

@@ -1,0 +1,97 @@
+"""The CTA-pair matmul (tcgen05 cta_group::2, 256x256 tiles per pair of SMs) against the oracle.
+
+16-bit inputs take this kernel when the problem has at least one wave of pair tiles (one per two SMs);
+every shape here does (asserted).  Tolerance: max-abs 2e-2 and rtol 1e-2 of the fp32
+oracle on inputs ~ N(0,1)/sqrt(K).  Rows are sampled for the oracle (first, last, ragged edge, a few in
+between); a column-sum identity checks every row.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import _native
+from mma import matmul
+from oracle.mma_oracle import tiled_matmul
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 2e-2
+NAME = {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(cuda_device):
+    yield
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0, "a kernel gave up on a bounded wait"
+
+
+def _pair_tiles(M, N):
+    return -(-M // 256) * -(-N // 256)
+
+
+def _inputs(M, N, K, dtype, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    a = (torch.randn(M, K, generator=g, device=device) / K ** 0.5).to(dtype)
+    b = (torch.randn(K, N, generator=g, device=device) / K ** 0.5).to(dtype)
+    return a, b
+
+
+def _check(a, b, c, round_f16):
+    M = a.shape[0]
+    rows = torch.tensor(sorted({0, 1, 127, 128, 255, 256, M // 2 + 3, M - 129, M - 1}))
+    ref = tiled_matmul(a[rows].float().cpu().numpy(), b.float().cpu().numpy(), round_f16=round_f16,
+                       out_dtype=NAME[c.dtype])
+    torch.testing.assert_close(c[rows.to(c.device)].float().cpu(), torch.from_numpy(np.asarray(ref, np.float32)),
+                               rtol=RTOL, atol=ATOL)
+    # Every row: 1^T C == (1^T A) B up to each element's output rounding.
+    lhs = c.float().sum(dim=0, dtype=torch.float64)
+    rhs = (a.double().sum(dim=0) @ b.double())
+    tol = 2e-2 * M ** 0.5 + 1e-2 * rhs.abs()
+    assert torch.all((lhs - rhs).abs() <= tol)
+
+
+SHAPES = [
+    # M, N, K: ragged in every dimension, K not a multiple of the 64-deep stage
+    (2381, 2376, 1000),
+    (2304, 4672, 520),
+    (4097, 2304, 136),
+    (2048, 3584, 18944),   # the TTFT down projection at TP=1
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "M{}N{}K{}".format(*s))
+@pytest.mark.parametrize("dtype, out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float16),
+                                              (torch.bfloat16, torch.float32), (torch.float16, torch.bfloat16)],
+                         ids=lambda d: NAME[d])
+def test_pair_matches_oracle(shape, dtype, out_dtype, cuda_device):
+    M, N, K = shape
+    assert _pair_tiles(M, N) >= torch.cuda.get_device_properties(cuda_device).multi_processor_count // 2
+    a, b = _inputs(M, N, K, dtype, cuda_device, seed=M + N + K)
+    c = matmul(a, b, out_dtype=out_dtype)
+    _check(a, b, c, round_f16=False)
+
+
+def test_pair_round_f16(cuda_device):
+    a, b = _inputs(2381, 2376, 1000, torch.bfloat16, cuda_device, seed=9)
+    _check(a, b, matmul(a, b, round_f16=True), round_f16=True)
+
+
+def test_pair_leading_dimensions(cuda_device):
+    """Row-major views with padded leading dimensions, and a strided output."""
+    a_full, b_full = _inputs(2500, 3000, 1104, torch.bfloat16, cuda_device, seed=13)
+    a = a_full[:, :1000]
+    b = b_full[:1000, 64:2624]
+    c_full = torch.full((2500, 2688), 5.0, device=cuda_device, dtype=torch.bfloat16)
+    c = c_full[:, :2560]
+    from mma import _gemm
+    _gemm(a, b, c, 2500, 2560, 1000, lda=a.stride(0), ldb=b.stride(0), ldc=c.stride(0), round_f16=False)
+    _check(a, b, c, round_f16=False)
+    assert torch.all(c_full[:, 2560:] == 5.0)
+
+
+def test_pair_deterministic(cuda_device):
+    a, b = _inputs(3000, 3072, 704, torch.bfloat16, cuda_device, seed=21)
+    assert torch.equal(matmul(a, b), matmul(a, b))
