@@ -32,31 +32,38 @@
 
 namespace fab {
 
+// kBN: 256, or 224 where that width leaves fewer idle pairs in the last wave
+// (e.g. N = 3584 = 16 x 224).  B's half per CTA is kBN / 2 columns in two
+// 64-column swizzle atoms (the second one partly used at 224).
+template <int kBN_ = 256>
 struct GemmPairCfg {
   static constexpr int kBM = 256;                     // rows per pair tile (128 per CTA)
   static constexpr int kBMc = 128;                    // rows per CTA
-  static constexpr int kBN = 256;                     // columns per tile (TMEM columns per accumulator)
-  static constexpr int kBNc = 128;                    // B columns each CTA holds
+  static constexpr int kBN = kBN_;                    // columns per tile
+  static constexpr int kBNc = kBN / 2;                // B columns each CTA holds
+  static constexpr int kAccStride = 256;              // TMEM columns between the two accumulators
   static constexpr int kBK = 64;                      // one 128-byte swizzle atom of 16-bit K
   static constexpr int kStages = 6;
   static constexpr int kKInstr = 16;
   static constexpr int kABytes = kBMc * 128;          // 128 rows x one atom
   static constexpr int kBAtomN = 64;
   static constexpr int kBAtomBytes = kBK * 128;
-  static constexpr int kBBytes = (kBNc / kBAtomN) * kBAtomBytes;
+  static constexpr int kBAtoms = (kBNc + kBAtomN - 1) / kBAtomN;
+  static constexpr int kBBytes = kBAtoms * kBAtomBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kThreads = 256;
-  static constexpr int kTmemCols = 512;               // 2 x 256 fp32 accumulators
+  static constexpr int kTmemCols = 512;               // 2 accumulators, kAccStride apart
   static constexpr int kNumBars = 2 * kStages + 4 + 1;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 64;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kBN % 32 == 0 && kBN <= kAccStride && kBNc % 16 == 0, "tile width");
 };
 
-template <typename Tin, typename Tout>
+template <typename Tin, typename Tout, int kBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_pair_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_b) {
-  using C = GemmPairCfg;
+  using C = GemmPairCfg<kBN>;
   static_assert(sizeof(Tin) == 2, "CTA-pair GEMM: 16-bit inputs");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -126,7 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const uint32_t full_s = mapa_shared(smem_u32(bar_full + s), 0);  // rank 0's full[s]
         tma_load_2d_pair(st, &tm_a, full_s, kb * C::kBK, m0);
 #pragma unroll
-        for (int a = 0; a < C::kBNc / C::kBAtomN; ++a)
+        for (int a = 0; a < C::kBAtoms; ++a)
           tma_load_2d_pair(st + C::kABytes + a * C::kBAtomBytes, &tm_b, full_s, n0 + a * C::kBAtomN, kb * C::kBK);
       }
     }
@@ -150,7 +157,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const uint32_t use = tcount >> 1;
       if (!(ok = mbar_wait(bar_acc_empty + buf, (use & 1) ^ 1, abort_flag, kDevTimeoutAcc))) break;
       tc_fence_after();
-      const uint32_t d = tmem + buf * C::kBN;
+      const uint32_t d = tmem + buf * C::kAccStride;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
@@ -184,8 +191,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       int pm, pn;
       gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
       const int row = pm * C::kBM + static_cast<int>(rank) * C::kBMc + r;
-      const uint32_t acc = tmem + lane_base + buf * C::kBN;
-      if (sizeof(Tout) == 2 && p.swiglu) {
+      const uint32_t acc = tmem + lane_base + buf * C::kAccStride;
+      if (sizeof(Tout) == 2 && kBN == 256 && p.swiglu) {
         // Tile columns: gate 0-63, up 0-63, gate 64-127, up 64-127 of the
         // 128 output columns starting at pn * 128.
         const int o0 = pn * (C::kBN / 2);
@@ -251,11 +258,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   }
 }
 
-// Pair tiles (256 x 256) in a grid of up to one pair per two SMs.
-template <typename Tin, typename Tout>
-static int launch_gemm_pair(const GemmLaunch& L, cudaStream_t stream) {
-  using C = GemmPairCfg;
-  auto kern = gemm_pair_kernel<Tin, Tout>;
+// Pair tiles (256 x kBN) in a grid of up to one pair per two SMs.
+template <typename Tin, typename Tout, int kBN>
+static int launch_gemm_pair_w(const GemmLaunch& L, cudaStream_t stream) {
+  using C = GemmPairCfg<kBN>;
+  auto kern = gemm_pair_kernel<Tin, Tout, kBN>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
   const CUtensorMapDataType dt =
@@ -283,6 +290,26 @@ static int launch_gemm_pair(const GemmLaunch& L, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 
+// Relative time of a pair-tile width: full waves of pairs times the work of
+// one tile (proportional to its width).
+static long long gemm_pair_cost(const GemmLaunch& L, int bn, int pairs) {
+  const long long tiles = static_cast<long long>((L.M + 255) / 256) * ((L.N + bn - 1) / bn);
+  return (tiles + pairs - 1) / pairs * bn;
+}
+
+template <typename Tin, typename Tout>
+static int launch_gemm_pair(const GemmLaunch& L, cudaStream_t stream) {
+  const int pairs = num_sms() / 2;
+  // 224-wide tiles only where they leave less of the last wave idle and K is
+  // short: a 224-wide tile's B halves start off the 128-byte line, which
+  // costs L2 traffic in long main loops (measured on B200: N = 3584 gains 7 %
+  // at K = 3584, loses 2-7 % at K = 18944).  The SwiGLU epilogue pairs
+  // 64-column gate/up blocks within 256-wide tiles.
+  if (!L.swiglu && pairs > 0 && L.K <= 8192 && gemm_pair_cost(L, 224, pairs) < gemm_pair_cost(L, 256, pairs))
+    return launch_gemm_pair_w<Tin, Tout, 224>(L, stream);
+  return launch_gemm_pair_w<Tin, Tout, 256>(L, stream);
+}
+
 // The pair kernel serves 16-bit inputs when the problem fills at least one
 // wave of pairs; smaller problems keep the single-CTA kernel's finer tiles.
 static bool gemm_use_pair(const GemmLaunch& L) {
@@ -291,8 +318,7 @@ static bool gemm_use_pair(const GemmLaunch& L) {
 #else
   if (L.in_dtype != kDtypeBF16 && L.in_dtype != kDtypeF16) return false;
   const int sms = num_sms();
-  const long long tiles = static_cast<long long>((L.M + GemmPairCfg::kBM - 1) / GemmPairCfg::kBM) *
-                          ((L.N + GemmPairCfg::kBN - 1) / GemmPairCfg::kBN);
+  const long long tiles = static_cast<long long>((L.M + 255) / 256) * ((L.N + 255) / 256);
   return sms >= 2 && tiles >= sms / 2;
 #endif
 }
