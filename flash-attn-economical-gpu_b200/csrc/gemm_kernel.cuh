@@ -140,6 +140,52 @@ __device__ __forceinline__ float round_to(float x) {
     return __half2float(__float2half_rn(x));
 }
 
+// One thread's row of a finished accumulator tile, from TMEM to C: `acc` is
+// the row's TMEM address of column 0, `row` its row of C, `n0` the tile's
+// first column of B, `width` the tile's columns (multiple of 32).  Plain
+// store (optionally through fp16), or with p.swiglu the SwiGLU of each
+// 64-column gate block and the up block after it: a 256-wide tile holds
+// gate 0-63, up 0-63, gate 64-127, up 64-127 of output columns n0/2 ... n0/2+127.
+template <typename Tout, int kWidth>
+__device__ __forceinline__ void gemm_store_tile_row(const GemmKernelParams& p, uint32_t acc, int row, int n0) {
+  if constexpr (sizeof(Tout) == 2 && kWidth == 256) {
+    if (p.swiglu) {
+      const int o0 = n0 / 2;
+      Tout* orow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + o0;
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {  // 32 output columns each
+        const int cg = (q >> 1) * 4 + (q & 1);
+        uint32_t rg[32], ru[32];
+        tmem_ld32(acc + cg * 32, rg);
+        tmem_ld32(acc + (cg + 2) * 32, ru);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float g = round_to<Tout>(__uint_as_float(rg[e]));
+          const float u = round_to<Tout>(__uint_as_float(ru[e]));
+          v[e] = round_to<Tout>(g / (1.0f + expf(-g))) * u;
+        }
+        const int ncols = min(32, p.N / 2 - o0 - q * 32);
+        if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(orow + q * 32, v, ncols, false);
+      }
+      return;
+    }
+  }
+  Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
+#pragma unroll 1
+  for (int cc = 0; cc < kWidth / 32; ++cc) {
+    uint32_t rr[32];
+    tmem_ld32(acc + cc * 32, rr);
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+    const int ncols = min(32, p.N - n0 - cc * 32);
+    if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
+  }
+}
+
 // 32 fp32 values as four 16-byte groups of 16-bit values.
 template <typename Tout>
 __device__ __forceinline__ void pack_chunk(const float (&v)[32], uint4 (&out)[4]) {
@@ -365,48 +411,7 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         int pm, pn;
         gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
-        const int row = pm * C::kBM + r;
-        if constexpr (sizeof(Tout) == 2) {
-          if (p.swiglu) {
-            // Tile columns: gate 0-63, up 0-63, gate 64-127, up 64-127 of the
-            // 128 output columns starting at pn * 128.
-            const int o0 = pn * (C::kBN / 2);
-            Tout* orow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + o0;
-#pragma unroll 1
-            for (int q = 0; q < 4; ++q) {  // 32 output columns each
-              const int cg = (q >> 1) * 4 + (q & 1);
-              uint32_t rg[32], ru[32];
-              tmem_ld32(tmem + lane_base + buf * C::kBN + cg * 32, rg);
-              tmem_ld32(tmem + lane_base + buf * C::kBN + (cg + 2) * 32, ru);
-              tmem_wait_ld();
-              float v[32];
-#pragma unroll
-              for (int e = 0; e < 32; ++e) {
-                const float g = round_to<Tout>(__uint_as_float(rg[e]));
-                const float u = round_to<Tout>(__uint_as_float(ru[e]));
-                v[e] = round_to<Tout>(g / (1.0f + expf(-g))) * u;
-              }
-              const int ncols = min(32, p.N / 2 - o0 - q * 32);
-              if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(orow + q * 32, v, ncols, false);
-            }
-            tc_fence_before();
-            mbar_arrive(bar_acc_empty + buf);
-            continue;
-          }
-        }
-        const int n0 = pn * C::kBN;
-        Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
-#pragma unroll 1
-        for (int cc = 0; cc < C::kBN / 32; ++cc) {
-          uint32_t rr[32];
-          tmem_ld32(tmem + lane_base + buf * C::kBN + cc * 32, rr);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
-          const int ncols = min(32, p.N - n0 - cc * 32);
-          if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
-        }
+        gemm_store_tile_row<Tout, C::kBN>(p, tmem + lane_base + buf * C::kBN, pm * C::kBM + r, pn * C::kBN);
         tc_fence_before();
         mbar_arrive(bar_acc_empty + buf);
       }

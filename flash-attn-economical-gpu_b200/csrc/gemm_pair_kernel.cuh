@@ -190,45 +190,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       tc_fence_after();
       int pm, pn;
       gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
-      const int row = pm * C::kBM + static_cast<int>(rank) * C::kBMc + r;
-      const uint32_t acc = tmem + lane_base + buf * C::kAccStride;
-      if (sizeof(Tout) == 2 && kBN == 256 && p.swiglu) {
-        // Tile columns: gate 0-63, up 0-63, gate 64-127, up 64-127 of the
-        // 128 output columns starting at pn * 128.
-        const int o0 = pn * (C::kBN / 2);
-        Tout* orow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + o0;
-#pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
-          const int cg = (q >> 1) * 4 + (q & 1);
-          uint32_t rg[32], ru[32];
-          tmem_ld32(acc + cg * 32, rg);
-          tmem_ld32(acc + (cg + 2) * 32, ru);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float g = round_to<Tout>(__uint_as_float(rg[e]));
-            const float u = round_to<Tout>(__uint_as_float(ru[e]));
-            v[e] = round_to<Tout>(g / (1.0f + expf(-g))) * u;
-          }
-          const int ncols = min(32, p.N / 2 - o0 - q * 32);
-          if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(orow + q * 32, v, ncols, false);
-        }
-      } else {
-        const int n0 = pn * C::kBN;
-        Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
-#pragma unroll 1
-        for (int cc = 0; cc < C::kBN / 32; ++cc) {
-          uint32_t rr[32];
-          tmem_ld32(acc + cc * 32, rr);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
-          const int ncols = min(32, p.N - n0 - cc * 32);
-          if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
-        }
-      }
+      gemm_store_tile_row<Tout, kBN>(p, tmem + lane_base + buf * C::kAccStride,
+                                     pm * C::kBM + static_cast<int>(rank) * C::kBMc + r, pn * C::kBN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(bar_acc_empty + buf), 0));  // rank 0's
