@@ -74,9 +74,9 @@ struct FaCfg {
   static constexpr int kDataBytes = kNQ * kQTileBytes + kRing * kKVTileBytes;
   // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
   // ring tiles 2j+1 .. 2j+4 are resident together.
-  // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
-  // ring tiles 2j+1 .. 2j+4 are resident together.
-  static_assert(kRing >= 2 * kSB && kRing >= 2, "K/V ring too short for the S buffering");
+  // The ring holds tiles in the order the MMA thread uses them, so at most
+  // V_j and K_{j+2} (two S buffers) or V_j and K_{j+1} (one) are held at once.
+  static_assert(kRing >= 2, "K/V ring too short");
   static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
   static_assert(kTmemUsed <= 512, "TMEM budget");
@@ -84,6 +84,18 @@ struct FaCfg {
   __host__ __device__ static constexpr int tmem_s(int slot) { return slot * kBN; }
   __host__ __device__ static constexpr int tmem_o(int i) { return kSlots * kBN + i * kDP; }
 };
+
+// Ring positions with two S buffers: the MMA thread uses K_0, K_1, then V_j
+// followed by K_{j+2} while that exists (P*V_j, then the S product that
+// reuses the buffer), and the producer loads them in that order.
+__host__ __device__ constexpr int ring_pos_k2(int j) { return j <= 1 ? j : 2 * j - 1; }
+__host__ __device__ constexpr int ring_pos_v2(int j, int nt) {
+  return nt == 1 ? 1 : (j <= nt - 3 ? 2 + 2 * j : nt + j);
+}
+static_assert(ring_pos_v2(0, 1) == 1 && ring_pos_k2(1) == 1 && ring_pos_v2(0, 2) == 2 && ring_pos_v2(1, 2) == 3 &&
+                  ring_pos_k2(2) == 3 && ring_pos_v2(1, 3) == 4 && ring_pos_v2(2, 3) == 5 && ring_pos_k2(3) == 5 &&
+                  ring_pos_v2(2, 4) == 6 && ring_pos_v2(3, 4) == 7,
+              "ring order K0 K1 V0 K2 V1 K3 ... V(nt-2) V(nt-1)");
 
 template <typename T>
 struct ElemOps;
@@ -265,8 +277,30 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         if (!mbar_wait(bar_kv_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
       }
       mbar_arrive_expect_tx(bar_kv_full + s, C::kKVTileBytes);
-      const CUtensorMap* map = (t & 1) ? &tm_v : &tm_k;
-      const int row = k_row0 + n_begin + (t >> 1) * kBN;
+      // Which tile is ring position t: alternating K/V with one S buffer;
+      // K_0, K_1, then V_j, K_{j+2} with two.
+      bool is_v = (t & 1) != 0;
+      int tj = t >> 1;
+      if constexpr (kSB == 2) {
+        if (t == 0 || (t == 1 && nt > 1)) {
+          is_v = false;
+          tj = t;
+        } else if (nt == 1) {
+          is_v = true;
+          tj = 0;
+        } else {
+          const int q = t - 2, pairs = nt - 2;  // (V_j, K_{j+2}) pairs, then the last two V
+          if (q < 2 * pairs) {
+            is_v = (q & 1) == 0;
+            tj = (q >> 1) + (is_v ? 0 : 2);
+          } else {
+            is_v = true;
+            tj = pairs + (q - 2 * pairs);
+          }
+        }
+      }
+      const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+      const int row = k_row0 + n_begin + tj * kBN;
       for (int a = 0; a < C::kNumAtoms; ++a)
         tma_load_4d(sKV + s * C::kKVTileBytes + a * C::kKVAtomBytes, map, bar_kv_full + s, a * C::kAtom, row, hk,
                     map_b);
@@ -292,11 +326,14 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     const uint32_t q_lo = umma_desc_lo(smem_u32(sQ), 16);
     const uint32_t k_lo = umma_desc_lo(smem_u32(sKV), 16);
     const uint32_t v_lo = umma_desc_lo(smem_u32(sKV), C::kKVAtomBytes);
-    // Ring slot and phase of K_j (tile 2j) and V_j (tile 2j+1).
-    auto kslot = [](int j) { return (2 * j) % kRing; };
-    auto kpar = [](int j) { return static_cast<uint32_t>(((2 * j) / kRing) & 1); };
-    auto vslot = [](int j) { return (2 * j + 1) % kRing; };
-    auto vpar = [](int j) { return static_cast<uint32_t>(((2 * j + 1) / kRing) & 1); };
+    // Ring slot and phase of K_j and V_j: tiles 2j and 2j+1 with one S buffer,
+    // the ring_pos_*2 order with two.
+    auto kpos = [&](int j) { return kSB == 2 ? ring_pos_k2(j) : 2 * j; };
+    auto vpos = [&](int j) { return kSB == 2 ? ring_pos_v2(j, nt) : 2 * j + 1; };
+    auto kslot = [&](int j) { return kpos(j) % kRing; };
+    auto kpar = [&](int j) { return static_cast<uint32_t>((kpos(j) / kRing) & 1); };
+    auto vslot = [&](int j) { return vpos(j) % kRing; };
+    auto vpar = [&](int j) { return static_cast<uint32_t>((vpos(j) / kRing) & 1); };
     auto issue_qk = [&](int i, int slot, int s) {
       const uint32_t d = tmem + C::tmem_s(slot);
       uint32_t qa = q_lo + i * (C::kQTileBytes >> 4);
@@ -757,7 +794,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) fa_split_combine_kernel(
 #define FAB_FA_TABLE(X)                                    \
   X(2, 64, 2, 128, 10, 1)   /* 16-bit, head dim <= 64 */    \
   X(2, 128, 2, 128, 5, 1)   /* 16-bit, head dim <= 128 */   \
-  X(2, 256, 1, 64, 5, 2)    /* 16-bit, head dim <= 256 */   \
+  X(2, 256, 1, 128, 2, 2)   /* 16-bit, head dim <= 256 */   \
   X(4, 64, 2, 128, 5, 1)    /* fp32/tf32, head dim <= 64 */ \
   X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
 
@@ -829,7 +866,7 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream) {
 #define FAB_FA_SPLIT_TABLE(X)                              \
   X(2, 64, 1, 128, 8, 2)    /* 16-bit, head dim <= 64 */    \
   X(2, 128, 1, 128, 6, 2)   /* 16-bit, head dim <= 128 */   \
-  X(2, 256, 1, 64, 5, 2)    /* 16-bit, head dim <= 256 */   \
+  X(2, 256, 1, 128, 2, 2)   /* 16-bit, head dim <= 256 */   \
   X(4, 64, 1, 128, 6, 2)    /* fp32/tf32, head dim <= 64 */ \
   X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
 

@@ -85,7 +85,7 @@ def test_tuner_candidates_are_the_compiled_tile_families(fake_limits):
     t256 = FlashAttentionOptimizeSharedMemTuner((2, 16, 64, 256), (2, 16, 64, 256), (2, 16, 64, 256), 2,
                                                 causal=True, return_lse=False)
     (cfg,) = t256._candidate_configs()
-    assert cfg["BLOCK_M"] == 128 and cfg["BLOCK_N"] == 64 and cfg["BLOCK_DMODEL"] == 256
+    assert cfg["BLOCK_M"] == 128 and cfg["BLOCK_N"] == 128 and cfg["BLOCK_DMODEL"] == 256
     t512 = FlashAttentionTuner((1, 1, 64, 512), (1, 1, 64, 512), (1, 1, 64, 512), 2, causal=False, return_lse=False)
     assert t512._candidate_configs() == []
     # the reference's shared-memory estimate formula (tuner.py:237-245)
