@@ -796,7 +796,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) fa_split_combine_kernel(
   X(2, 128, 2, 128, 5, 1)   /* 16-bit, head dim <= 128 */   \
   X(2, 256, 1, 128, 2, 2)   /* 16-bit, head dim <= 256 */   \
   X(4, 64, 2, 128, 5, 1)    /* fp32/tf32, head dim <= 64 */ \
-  X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
+  X(4, 128, 1, 128, 2, 2)   /* fp32/tf32, head dim <= 128 */
 
 static bool fa_table_lookup(int elt, int D, int* d_pad) {
   int best = 0;
@@ -868,7 +868,7 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream) {
   X(2, 128, 1, 128, 6, 2)   /* 16-bit, head dim <= 128 */   \
   X(2, 256, 1, 128, 2, 2)   /* 16-bit, head dim <= 256 */   \
   X(4, 64, 1, 128, 6, 2)    /* fp32/tf32, head dim <= 64 */ \
-  X(4, 128, 1, 64, 5, 2)    /* fp32/tf32, head dim <= 128 */
+  X(4, 128, 1, 128, 2, 2)   /* fp32/tf32, head dim <= 128 */
 
 int fa_select_split_config(int dtype, int D, FaConfigInfo* out) {
   if (D <= 0) return kErrInvalidArg;

@@ -81,7 +81,7 @@ def test_return_code_mapping():
         (_native.FAB_DTYPE_F16, 96, (128, 2, 128, 5, 1)),
         (_native.FAB_DTYPE_F16, 256, (256, 1, 128, 2, 2)),
         (_native.FAB_DTYPE_F32, 64, (64, 2, 128, 5, 1)),
-        (_native.FAB_DTYPE_F32, 128, (128, 1, 64, 5, 2)),
+        (_native.FAB_DTYPE_F32, 128, (128, 1, 128, 2, 2)),
     ],
 )
 def test_tile_table(dtype, D, expect):
