@@ -500,10 +500,26 @@ def _matmul(a: torch.Tensor, b: torch.Tensor, how: str) -> torch.Tensor:
     raise ValueError(f"unknown gemm backend {how!r}")
 
 
-def _attention_segments(q, k, v, out, plan: RankPlan, how: str) -> None:
-    """q/out [1, nq, S, D], k/v [1, nkv_local, S, D] (strided views); causal; one call per key/value head.
+def _even_group(segments: tuple[tuple[int, int, int], ...]) -> int:
+    """g when the local query heads split into runs of g heads over consecutive key/value heads, else 0."""
+    g = segments[0][1]
+    even = all(cnt == g and first == i * g and kv == i for i, (first, cnt, kv) in enumerate(segments))
+    return g if even else 0
 
-    For torch backends the caller holds the `torch_sdpa_backend` context."""
+
+def _attention_segments(q, k, v, out, plan: RankPlan, how: str) -> None:
+    """q/out [1, nq, S, D], k/v [1, nkv_local, S, D] (strided views); causal.
+
+    When the rank's query heads split evenly over its key/value heads (TP 1, 2, 4 for 28/4 heads) one grouped
+    call covers them all, so the kernel sees every head's row blocks at once; otherwise one call per
+    key/value head.  For torch backends the caller holds the `torch_sdpa_backend` context."""
+    g = _even_group(plan.segments)
+    if g:
+        if how == "native":
+            attention_forward(q, k, v, causal=True, out=out)
+        else:
+            out.copy_(F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=g > 1))
+        return
     for first, count, kv in plan.segments:
         qs = q[:, first:first + count]
         ks = k[:, kv:kv + 1]
