@@ -7,10 +7,11 @@
 // to the input dtype before the P*V product, final O = acc / l.
 //
 // B200 structure (one CTA per SM, 128 + NQ*128 threads):
-//   warp 0      TMA producer: Q tiles once, then K and V tiles alternating
-//               through one ring of kRing tile slots (K_j is ring tile 2j,
-//               V_j ring tile 2j+1), so every slot the Q tiles leave free in
-//               shared memory adds load lead time.
+//   warp 0      TMA producer: Q tiles once, then K and V tiles through one
+//               ring of kRing tile slots, in the order the MMA thread uses
+//               them (K_j, V_j alternating with one S buffer; K_0, K_1, then
+//               V_j, K_{j+2} with two), so every slot the Q tiles leave free
+//               in shared memory adds load lead time.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
 //   warps 4..   one 128-thread softmax group per 128-row Q tile; thread r of
 //               the group owns row r (TMEM lane r) for the whole kernel.
@@ -409,7 +410,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
         // Two S buffers per Q tile: S_i(j+1) is already in TMEM while the
         // softmax works on tile j.  The softmax of tile j+1 waits for
         // P_i*V(j) before it may rescale O, and the producer's next V and K
-        // loads wait for V(j)'s stage: release both right after the P*V
+        // loads wait for V(j)'s slot: release both right after the P*V
         // products; K(j+2) is issued only after V(j+1), so wait for it
         // afterwards.
         for (int i = 0; i < kNQ; ++i) {
