@@ -5,7 +5,10 @@ BLOCK_K=..., GROUP_M=..., USE_CACHE_EVICTION_HINTS=..., num_warps=...,
 num_stages=...)` keeps the Triton kernel's call form (mma.py:8-21) and
 result: C = A B over row-major contiguous storage with fp32 accumulation,
 rounded to fp16 and then stored in C's dtype (mma.py:51-52).  It runs the
-persistent sm_100a tcgen05 GEMM through the C ABI (`fab_matmul_contiguous`);
+persistent sm_100a tcgen05 GEMM through the C ABI (`fab_matmul_contiguous`),
+which picks the kernel: 16-bit problems of at least one wave of 256x256 tiles
+run on CTA pairs (tcgen05 cta_group::2, one tile per two SMs), the rest on one
+CTA per 128x256 tile;
 the Triton tiling keywords (BLOCK_*, GROUP_M, cache hints, num_warps,
 num_stages) are accepted and not needed.  `_select_2d_contiguous_config` accepts and
 rejects exactly the shapes the reference accepts and rejects (mma.py:63-81)
@@ -23,8 +26,10 @@ from tuner import get_architecture
 
 logger = logging.getLogger(__name__)
 
-# Tile of the sm_100a kernel: 128x256 outputs per CTA, one 128-byte swizzle
-# atom of K per stage, 4 stages, 8 warps (TMA, MMA, 4 epilogue + 2 spare).
+# Tile of the single-CTA sm_100a kernel, reported as the launch config:
+# 128x256 outputs per CTA, one 128-byte swizzle atom of K per stage, 4 stages,
+# 8 warps (TMA, MMA, 4 epilogue + 2 spare).  Each CTA of a pair holds the same
+# 128 rows and half of a 256-wide tile's columns per stage.
 SM100_BLOCK_M = 128
 SM100_BLOCK_N = 256
 SM100_NUM_WARPS = 8
