@@ -1,7 +1,8 @@
-// C-ABI entry points of libfa_b200.so (declared in include/fa_b200.h) plus
-// the host helpers the kernels share.  This is the library's only
-// translation unit: the kernel sources are included below, so the device
-// error word needs no relocatable device code.
+// C-ABI entry points of libfa_b200.so (declared in include/fa_b200.h), the
+// host helpers the kernels share, and the attention and decoder-op kernels
+// (included below).  The GEMM kernels are the library's second translation
+// unit (gemm.cu); each unit keeps its own copy of the device status word, so
+// neither needs relocatable device code.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -16,7 +17,6 @@
 #include "ptx.cuh"
 
 #include "fa_fwd_kernel.cuh"
-#include "gemm_kernel.cuh"
 #include "decoder_ops.cuh"
 
 namespace fab {
@@ -786,13 +786,18 @@ int fab_device_limits_query(int device, fab_device_limits* out) {
 
 int fab_get_device_error(int* code) {
   if (code == nullptr) return kErrInvalidArg;
+  // This unit's status word (attention, decoder ops), then the GEMM unit's;
+  // both are cleared, the first code recorded is reported.
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_fab_device_error, sizeof(int)) != cudaSuccess) return kErrCuda;
   if (v != 0) {
     const int zero = 0;
     if (cudaMemcpyToSymbol(g_fab_device_error, &zero, sizeof(int)) != cudaSuccess) return kErrCuda;
   }
-  *code = v;
+  int g = 0;
+  const int rc = gemm_take_device_error(&g);
+  if (rc) return rc;
+  *code = v != 0 ? v : g;
   return kOk;
 }
 

@@ -93,6 +93,17 @@ __host__ __device__ constexpr int ring_pos_k2(int j) { return j <= 1 ? j : 2 * j
 __host__ __device__ constexpr int ring_pos_v2(int j, int nt) {
   return nt == 1 ? 1 : (j <= nt - 3 ? 2 + 2 * j : nt + j);
 }
+// Ring positions of K_j and V_j for either S buffering (one: 2j and 2j+1).
+template <int kSB>
+__host__ __device__ constexpr int ring_pos_k(int j) {
+  if constexpr (kSB == 2) return ring_pos_k2(j);
+  else return 2 * j;
+}
+template <int kSB>
+__host__ __device__ constexpr int ring_pos_v(int j, int nt) {
+  if constexpr (kSB == 2) return ring_pos_v2(j, nt);
+  else return 2 * j + 1;
+}
 static_assert(ring_pos_v2(0, 1) == 1 && ring_pos_k2(1) == 1 && ring_pos_v2(0, 2) == 2 && ring_pos_v2(1, 2) == 3 &&
                   ring_pos_k2(2) == 3 && ring_pos_v2(1, 3) == 4 && ring_pos_v2(2, 3) == 5 && ring_pos_k2(3) == 5 &&
                   ring_pos_v2(2, 4) == 6 && ring_pos_v2(3, 4) == 7,
@@ -280,9 +291,11 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
       mbar_arrive_expect_tx(bar_kv_full + s, C::kKVTileBytes);
       // Which tile is ring position t: alternating K/V with one S buffer;
       // K_0, K_1, then V_j, K_{j+2} with two.
-      bool is_v = (t & 1) != 0;
-      int tj = t >> 1;
+      const CUtensorMap* map;
+      int row;
       if constexpr (kSB == 2) {
+        bool is_v;
+        int tj;
         if (t == 0 || (t == 1 && nt > 1)) {
           is_v = false;
           tj = t;
@@ -299,9 +312,12 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
             tj = pairs + (q - 2 * pairs);
           }
         }
+        map = is_v ? &tm_v : &tm_k;
+        row = k_row0 + n_begin + tj * kBN;
+      } else {
+        map = (t & 1) ? &tm_v : &tm_k;
+        row = k_row0 + n_begin + (t >> 1) * kBN;
       }
-      const CUtensorMap* map = is_v ? &tm_v : &tm_k;
-      const int row = k_row0 + n_begin + tj * kBN;
       for (int a = 0; a < C::kNumAtoms; ++a)
         tma_load_4d(sKV + s * C::kKVTileBytes + a * C::kKVAtomBytes, map, bar_kv_full + s, a * C::kAtom, row, hk,
                     map_b);
@@ -329,12 +345,10 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
     const uint32_t v_lo = umma_desc_lo(smem_u32(sKV), C::kKVAtomBytes);
     // Ring slot and phase of K_j and V_j: tiles 2j and 2j+1 with one S buffer,
     // the ring_pos_*2 order with two.
-    auto kpos = [&](int j) { return kSB == 2 ? ring_pos_k2(j) : 2 * j; };
-    auto vpos = [&](int j) { return kSB == 2 ? ring_pos_v2(j, nt) : 2 * j + 1; };
-    auto kslot = [&](int j) { return kpos(j) % kRing; };
-    auto kpar = [&](int j) { return static_cast<uint32_t>((kpos(j) / kRing) & 1); };
-    auto vslot = [&](int j) { return vpos(j) % kRing; };
-    auto vpar = [&](int j) { return static_cast<uint32_t>((vpos(j) / kRing) & 1); };
+    auto kslot = [](int j) { return ring_pos_k<kSB>(j) % kRing; };
+    auto kpar = [](int j) { return static_cast<uint32_t>((ring_pos_k<kSB>(j) / kRing) & 1); };
+    auto vslot = [=](int j) { return ring_pos_v<kSB>(j, nt) % kRing; };
+    auto vpar = [=](int j) { return static_cast<uint32_t>((ring_pos_v<kSB>(j, nt) / kRing) & 1); };
     auto issue_qk = [&](int i, int slot, int s) {
       const uint32_t d = tmem + C::tmem_s(slot);
       uint32_t qa = q_lo + i * (C::kQTileBytes >> 4);

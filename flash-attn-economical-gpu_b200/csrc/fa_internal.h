@@ -152,6 +152,8 @@ int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
 int gemm_ar_tiles(int M, int N);
 int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t stream);
 int gemm_kernel_attrs(int in_dtype, int* regs, int* smem, int* threads);
+// Reads and clears the GEMM translation unit's device status word.
+int gemm_take_device_error(int* code);
 
 // Helpers implemented in capi.cu.
 int ensure_smem_attr(const void* kernel, int bytes);

@@ -28,8 +28,9 @@ enum DeviceError : int {
   kDevTimeoutPeerDone = 10,  // the reduced tiles from every owner never all arrived
 };
 
-// Device-global status word shared by all kernels of this library (the
-// library is a single translation unit, so internal linkage is enough).
+// Device-global status word of the kernels of one translation unit (internal
+// linkage: capi.cu and gemm.cu each have one; fab_get_device_error reads
+// both).  A kernel that starts after a failed wait of its unit skips its work.
 static __device__ int g_fab_device_error = 0;
 
 // A single wait may take at most this long before the kernel gives up.
