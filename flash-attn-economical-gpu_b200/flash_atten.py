@@ -477,6 +477,87 @@ def attention_forward_varlen(
     return (o, lse) if return_lse else o
 
 
+def attention_forward_host(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = False,
+    sm_scale: float | None = None,
+    out: torch.Tensor | None = None,
+    device=None,
+    chunks: int = 16,
+) -> torch.Tensor:
+    """attention_forward for host tensors: q [B, Hq, M, D], k/v [B, Hkv, N, D] in CPU memory (pinned for overlap).
+
+    Returns O in host memory (`out`, or a new pinned tensor) once it has landed there.  The call is cut into up
+    to `chunks` pieces of whole (batch entry, key/value-head group) units and pipelined over three streams of
+    `device` (default: the current device): piece c+1 is copied in while piece c is computed and piece c-1 is
+    copied out, so both directions of the host link are busy at once and the kernel time hides behind the
+    copies.  Each piece is the same kernel call as attention_forward on its units, which are independent, so
+    the result equals attention_forward's bit for bit.  No counterpart in the reference (its kernels take
+    device tensors).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu":
+            raise ValueError(f"attention_forward_host: {name} must be a CPU tensor")
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("attention_forward_host expects q, k, v with shape [batch, heads, seq, head_dim]")
+    B, Hq, M, D = q.shape
+    Hkv = k.shape[1]
+    if Hkv <= 0 or Hq % Hkv or k.shape[0] != B or v.shape != k.shape:
+        raise ValueError("attention_forward_host: k and v must be [batch, kv_heads, seq, head_dim] with kv_heads "
+                         "dividing q's heads")
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=torch.cuda.is_available())
+    elif out.device.type != "cpu" or out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("attention_forward_host: out must be a CPU tensor shaped and typed like q")
+    if q.numel() == 0:
+        return out
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    g = Hq // Hkv
+    # Pieces: per batch entry, runs of whole key/value-head groups.
+    per_b = max(1, min(Hkv, -(-max(1, chunks) // B)))
+    pieces = []
+    for b in range(B):
+        for i in range(per_b):
+            h0, h1 = Hkv * i // per_b, Hkv * (i + 1) // per_b
+            if h1 > h0:
+                pieces.append((b, h0, h1))
+    widest = max(h1 - h0 for _, h0, h1 in pieces)
+    with torch.cuda.device(dev):
+        compute = torch.cuda.current_stream(dev)
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        # Two device slots per operand, each as wide as the widest piece.
+        slots = [tuple(torch.empty((1, widest * hs, t.shape[2], D), device=dev, dtype=t.dtype)
+                       for t, hs in ((q, g), (k, 1), (v, 1), (q, g))) for _ in range(2)]
+        # The slots come from the caching allocator on the compute stream: the first copy in waits for what is
+        # already queued there (which may still be using that memory).
+        h2d.wait_event(compute.record_event())
+        copied, computed, drained = [], [], []
+        for c, (b, h0, h1) in enumerate(pieces):
+            qd, kd, vd, od = (t[:, :(h1 - h0) * hs] for t, hs in zip(slots[c % 2], (g, 1, 1, g)))
+            with torch.cuda.stream(h2d):
+                if c >= 2:
+                    h2d.wait_event(computed[c - 2])  # this slot's inputs were read by piece c-2's kernel
+                qd.copy_(q[b:b + 1, h0 * g:h1 * g], non_blocking=True)
+                kd.copy_(k[b:b + 1, h0:h1], non_blocking=True)
+                vd.copy_(v[b:b + 1, h0:h1], non_blocking=True)
+                copied.append(h2d.record_event())
+            compute.wait_event(copied[c])
+            if c >= 2:
+                compute.wait_event(drained[c - 2])  # this slot's output was copied out by piece c-2
+            attention_forward(qd, kd, vd, causal=causal, sm_scale=sm_scale, out=od)
+            computed.append(compute.record_event())
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(computed[c])
+                out[b:b + 1, h0 * g:h1 * g].copy_(od, non_blocking=True)
+                drained.append(d2h.record_event())
+        compute.wait_event(drained[-1])
+        d2h.synchronize()
+    return out
+
+
 def splitkv_workspace_bytes(q_shape, k_shape, dtype, *, num_splits: int = 0, causal: bool = False) -> tuple[int, int]:
     """(workspace bytes, splits used) that attention_forward_splitkv needs for contiguous inputs of these shapes."""
     B, Hq, M, D = q_shape
@@ -503,6 +584,7 @@ __all__ = [
     "attention_forward",
     "attention_forward_splitkv",
     "attention_forward_varlen",
+    "attention_forward_host",
     "splitkv_workspace_bytes",
     "_flash_attn_fwd_kernel_basic",
     "_flash_attn_fwd_kernel_optimize_shared_mem",

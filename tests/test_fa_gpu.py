@@ -353,3 +353,29 @@ def test_tuner_times_both_families(cuda_device):
     o = flash_attention(spec)
     ro, _ = _oracle(qd.cpu(), kd.cpu(), vd.cpu(), True, torch.bfloat16)
     _close(o, ro)
+
+
+# ------------------------------------------------------------ host-buffer entry point
+@pytest.mark.parametrize("shape, chunks", [((2, 4, 4, 300, 300, 64), 16), ((1, 8, 2, 257, 513, 128), 3),
+                                           ((3, 6, 3, 128, 1000, 128), 1), ((2, 4, 2, 200, 200, 256), 64)],
+                         ids=["mha", "gqa", "one_piece", "d256"])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_host_entry_equals_device_call(shape, chunks, causal, cuda_device):
+    """attention_forward_host on host tensors, pipelined in pieces, returns attention_forward's bits."""
+    q, k, v, qd, kd, vd = _inputs(shape, torch.bfloat16, seed=sum(shape) + chunks, dev=cuda_device)
+    want = attention_forward(qd, kd, vd, causal=causal).cpu()
+    qp, kp, vp = q.pin_memory(), k.pin_memory(), v.pin_memory()
+    got = flash_atten.attention_forward_host(qp, kp, vp, causal=causal, chunks=chunks, device=cuda_device)
+    assert got.device.type == "cpu" and got.is_pinned()
+    assert torch.equal(got, want)
+    # caller-supplied output, pageable inputs, sm_scale passed through
+    out = torch.full_like(q, 7.0)
+    flash_atten.attention_forward_host(q, k, v, causal=causal, sm_scale=0.05, out=out, chunks=chunks,
+                                       device=cuda_device)
+    assert torch.equal(out, attention_forward(qd, kd, vd, causal=causal, sm_scale=0.05).cpu())
+
+
+def test_host_entry_fp32_and_oracle(cuda_device):
+    q, k, v, _, _, _ = _inputs((2, 2, 1, 192, 320, 64), torch.float32, seed=5, dev=cuda_device)
+    got = flash_atten.attention_forward_host(q, k, v, causal=True, chunks=4, device=cuda_device)
+    _close(got, _oracle(q, k, v, True, torch.float32)[0])

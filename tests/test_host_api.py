@@ -257,3 +257,19 @@ def test_matmul_swiglu_refuses_cpu_and_odd_widths():
         mma.matmul_swiglu(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(8, 192, dtype=torch.bfloat16))
     with pytest.raises(ValueError):
         mma.matmul_swiglu(torch.zeros(4, 8), torch.zeros(8, 256))
+
+
+def test_host_entry_validation():
+    x = torch.zeros(1, 2, 16, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="q must be a CPU tensor"):
+        flash_atten.attention_forward_host(torch.zeros(1, 2, 16, 64, dtype=torch.bfloat16, device="meta"), x, x)
+    with pytest.raises(ValueError, match="shape \\[batch, heads, seq, head_dim\\]"):
+        flash_atten.attention_forward_host(x[0], x, x)
+    with pytest.raises(ValueError, match="kv_heads dividing"):
+        flash_atten.attention_forward_host(x, torch.zeros(1, 3, 16, 64, dtype=torch.bfloat16),
+                                           torch.zeros(1, 3, 16, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="out must be a CPU tensor"):
+        flash_atten.attention_forward_host(x, x, x, out=torch.zeros(1, 2, 16, 32, dtype=torch.bfloat16))
+    # nothing to compute: returns without touching a device
+    e = torch.zeros(0, 2, 16, 64, dtype=torch.bfloat16)
+    assert flash_atten.attention_forward_host(e, e, e).shape == e.shape
