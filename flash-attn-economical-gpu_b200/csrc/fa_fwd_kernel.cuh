@@ -197,14 +197,24 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: heads are the slow index so CTAs resident together share K/V
-  // in L2; within a head the longest (causal) row blocks start first.
-  // Rows are the query positions of one (batch, query head), or with
-  // pack_gqa the (query head, position) pairs of the query heads sharing one
-  // key/value head.  blockIdx.y selects a split of split_len keys.
+  // Work item: (batch, head) items are dealt in groups of head_group, the
+  // slow index, so CTAs resident together share the group's K/V in L2;
+  // within a group the row blocks go longest (causal) first across all its
+  // items, so the grid's last CTAs are short ones and the SMs finish
+  // together.  Rows are the query positions of one (batch, query head), or
+  // with pack_gqa the (query head, position) pairs of the query heads sharing
+  // one key/value head.  blockIdx.y selects a split of split_len keys.
   const int heads = p.pack_gqa ? p.Hq / p.group : p.Hq;
-  const int bh = blockIdx.x / p.num_m_blocks;
-  const int mblk = p.num_m_blocks - 1 - (blockIdx.x % p.num_m_blocks);
+  int bh, mblk;
+  {
+    const int items = static_cast<int>(gridDim.x) / p.num_m_blocks;
+    const int per_group = p.head_group * p.num_m_blocks;
+    const int grp = static_cast<int>(blockIdx.x) / per_group;
+    const int in_grp = min(p.head_group, items - grp * p.head_group);
+    const int r = static_cast<int>(blockIdx.x) - grp * per_group;
+    bh = grp * p.head_group + r % in_grp;
+    mblk = p.num_m_blocks - 1 - r / in_grp;
+  }
   const int b = bh / heads;
   const int h = bh % heads;  // query head; key/value head when packed
   const int hk = p.pack_gqa ? h : h / p.group;
@@ -641,6 +651,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, 1)
 
 // ---------------------------------------------------------------- host side
 
+// Causal launches deal (batch, head) items in groups whose K and V together
+// take at most this much of the 126 MB L2 (see fa_fwd_kernel's work item).
+#ifndef FAB_CAUSAL_GROUP_L2_MB
+#define FAB_CAUSAL_GROUP_L2_MB 48
+#endif
+constexpr long long kCausalGroupL2Bytes = static_cast<long long>(FAB_CAUSAL_GROUP_L2_MB) << 20;
+
 template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
 static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kRing, kSB>;
@@ -715,8 +732,20 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   kp.lse_part = L.lse_part;
   kp.cu_q = L.cu_q;
   kp.cu_k = L.cu_k;
-  const long long grid = static_cast<long long>(kp.num_m_blocks) * L.B * (L.pack_gqa ? L.Hkv : L.Hq);
+  const int items = L.B * (L.pack_gqa ? L.Hkv : L.Hq);
+  const long long grid = static_cast<long long>(kp.num_m_blocks) * items;
   if (grid <= 0) return 0;
+  // Causal row blocks differ in length: deal the (batch, head) items in
+  // groups whose K and V fit in a slice of L2 and run each group's row blocks
+  // longest first.  Without a mask every block is as long, and one item per
+  // group keeps a head's blocks together.
+  kp.head_group = 1;
+  if (L.causal) {
+    // K and V bytes per item: the query heads of one key/value head share it.
+    const long long kv_bytes = 2LL * (L.N > 0 ? L.N : 1) * L.D * elt / (L.pack_gqa ? 1 : group);
+    const long long fit = kCausalGroupL2Bytes / (kv_bytes > 0 ? kv_bytes : 1);
+    kp.head_group = static_cast<int>(fit < 1 ? 1 : (fit > items ? items : fit));
+  }
   if (grid > 0x7fffffffLL || splits > 65535) return kErrInvalidArg;
   kern<<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(splits)), C::kThreads, C::kSmemBytes, stream>>>(
       kp, tq, tk, tv);

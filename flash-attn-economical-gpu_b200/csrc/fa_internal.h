@@ -32,6 +32,9 @@ struct FaKernelParams {
   float scale_log2;
   int causal;
   int num_m_blocks;
+  // blockIdx.x walks groups of head_group (batch, head) items; inside a group
+  // the row block is the slow index (longest first) and the item the fast one.
+  int head_group;
   // Key splits: CTA (x, y) attends to keys [y * split_len, (y + 1) * split_len).
   // Without splitting split_len >= N and gridDim.y == 1.
   int split_len;
