@@ -26,6 +26,9 @@ FAB_ERR_WORKSPACE = 6
 
 FAB_GEMM_EPILOGUE_STORE = 0
 FAB_GEMM_EPILOGUE_SWIGLU = 1
+FAB_GEMM_KERNEL_SINGLE = 0
+FAB_GEMM_KERNEL_PAIR = 1
+FAB_GEMM_KERNEL_SPLITK = 2
 
 FAB_DTYPE_F16 = 0
 FAB_DTYPE_BF16 = 1
@@ -130,6 +133,7 @@ PROTOTYPES = {
     "fab_attention_fwd_splitkv_static": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
     "fab_matmul_contiguous": (_i32, [_vp] * 3 + [_i32] * 6 + [_vp]),
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
+    "fab_gemm_plan": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "fab_gemm_allreduce_layout": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_size_t),
                                          ctypes.POINTER(ctypes.c_size_t)]),
     "fab_gemm_allreduce": (_i32, [ctypes.POINTER(FabGemmAllreduceParams), _vp]),
@@ -147,7 +151,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 def _load() -> ctypes.CDLL:

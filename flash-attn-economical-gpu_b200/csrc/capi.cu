@@ -254,7 +254,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 4; }
+int fab_abi_version(void) { return 5; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -495,10 +495,14 @@ int fab_attention_fwd_splitkv_static(const fab_attention_params* p, int num_spli
   return fa_forward_split(L, static_cast<cudaStream_t>(stream));
 }
 
-int fab_gemm(const fab_gemm_params* p, void* stream) {
+static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothing, bool* empty_k) {
+  *nothing = *empty_k = false;
   if (p == nullptr) return kErrInvalidArg;
   if (p->M < 0 || p->N < 0 || p->K < 0) return kErrInvalidArg;
-  if (p->M == 0 || p->N == 0) return kOk;
+  if (p->M == 0 || p->N == 0) {
+    *nothing = true;
+    return kOk;
+  }
   for (int dt : {p->in_dtype, p->out_dtype})
     if (dt != kDtypeF16 && dt != kDtypeBF16 && dt != kDtypeF32) return kErrInvalidArg;
   if (p->c == nullptr || !aligned16(p->c)) return kErrInvalidArg;
@@ -509,13 +513,12 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   const int c_cols = swiglu ? p->N / 2 : p->N;
   if ((p->ldc * oe) % 16 != 0 || p->ldc < c_cols) return kErrInvalidArg;
   if (p->K == 0) {
-    // Empty contraction: C = 0 (also under SwiGLU: silu(0) * 0 = 0).
-    cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(c_cols) * oe, size_t(p->M),
-                                      static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? kOk : kErrCuda;
+    *empty_k = true;
+    return kOk;
   }
   if (p->lda < p->K || p->ldb < p->N) return kErrInvalidArg;
-  GemmLaunch L{};
+  GemmLaunch& L = *out;
+  L = GemmLaunch{};
   L.a = p->a;
   L.b = p->b;
   L.c = p->c;
@@ -530,7 +533,34 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   L.round_f16 = p->round_f16;
   L.group_m = p->group_m;
   L.swiglu = swiglu ? 1 : 0;
+  return kOk;
+}
+
+int fab_gemm(const fab_gemm_params* p, void* stream) {
+  GemmLaunch L;
+  bool nothing, empty_k;
+  const int rc = gemm_validate(p, &L, &nothing, &empty_k);
+  if (rc || nothing) return rc;
+  if (empty_k) {
+    // Empty contraction: C = 0 (also under SwiGLU: silu(0) * 0 = 0).
+    const int oe = elt_size(p->out_dtype);
+    const int c_cols = p->epilogue == FAB_GEMM_EPILOGUE_SWIGLU ? p->N / 2 : p->N;
+    cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(c_cols) * oe, size_t(p->M),
+                                      static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? kOk : kErrCuda;
+  }
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_gemm_plan(const fab_gemm_params* p, int* kernel, int* k_split) {
+  if (kernel == nullptr || k_split == nullptr) return kErrInvalidArg;
+  *kernel = FAB_GEMM_KERNEL_SINGLE;
+  *k_split = 1;
+  GemmLaunch L;
+  bool nothing, empty_k;
+  const int rc = gemm_validate(p, &L, &nothing, &empty_k);
+  if (rc || nothing || empty_k) return rc;
+  return gemm_plan(L, kernel, k_split);
 }
 
 int fab_gemm_allreduce_layout(int M, int N, int world, int* tiles_per_owner, size_t* inbox_bytes,

@@ -649,13 +649,58 @@ int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t str
 }  // namespace fab
 
 #include "gemm_pair_kernel.cuh"
+#include "gemm_splitk_kernel.cuh"
 
 namespace fab {
+
+template <typename Tin>
+static int gemm_splitk_factor_out(const GemmLaunch& L) {
+  if (L.out_dtype == kDtypeF16) return gemm_splitk_factor<Tin, __half>(L);
+  if (L.out_dtype == kDtypeBF16) return gemm_splitk_factor<Tin, __nv_bfloat16>(L);
+  if (L.out_dtype == kDtypeF32) return gemm_splitk_factor<Tin, float>(L);
+  return 1;
+}
+
+// Which kernel gemm_forward runs for L: 0 single CTA per tile, 1 CTA pairs,
+// 2 split K over a cluster of *split CTAs per tile.
+int gemm_plan(const GemmLaunch& L, int* kernel, int* split) {
+  *kernel = 0;
+  *split = 1;
+  if (L.M <= 0 || L.N <= 0 || L.K <= 0) return 0;
+#ifndef FAB_GEMM_NO_SPLITK
+  if (L.in_dtype == kDtypeF16 || L.in_dtype == kDtypeBF16) {
+    const int s = L.in_dtype == kDtypeF16 ? gemm_splitk_factor_out<__half>(L) : gemm_splitk_factor_out<__nv_bfloat16>(L);
+    if (s > 1) {
+      *kernel = 2;
+      *split = s;
+      return 0;
+    }
+  }
+#endif
+  if (gemm_use_pair(L)) *kernel = 1;
+  return 0;
+}
+
+template <typename Tin>
+static int gemm_forward_splitk(const GemmLaunch& L, cudaStream_t stream, bool* taken) {
+  if (L.out_dtype == kDtypeF16) return launch_gemm_splitk<Tin, __half>(L, stream, taken);
+  if (L.out_dtype == kDtypeBF16) return launch_gemm_splitk<Tin, __nv_bfloat16>(L, stream, taken);
+  if (L.out_dtype == kDtypeF32) return launch_gemm_splitk<Tin, float>(L, stream, taken);
+  *taken = false;
+  return 0;
+}
 
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
   if (L.M < 0 || L.N < 0 || L.K < 0) return kErrInvalidArg;
   if (L.M == 0 || L.N == 0) return 0;
   const int in = L.in_dtype, out = L.out_dtype;
+  if (L.K > 0 && (in == kDtypeF16 || in == kDtypeBF16)) {
+    // Too few output tiles for the SMs: the CTAs of a cluster share each tile's K.
+    bool taken = false;
+    const int rc = in == kDtypeF16 ? gemm_forward_splitk<__half>(L, stream, &taken)
+                                   : gemm_forward_splitk<__nv_bfloat16>(L, stream, &taken);
+    if (taken) return rc;
+  }
   if (L.K > 0 && gemm_use_pair(L)) {
     if (in == kDtypeF16) {
       if (out == kDtypeF16) return launch_gemm_pair<__half, __half>(L, stream);

@@ -265,8 +265,9 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
-// Every thread of both CTAs: barrier over the cluster (no time limit, so only
-// where every thread of the cluster always arrives: kernel start).
+// Every thread of every CTA of the cluster: barrier over the cluster (no time
+// limit, so only at points every thread of the cluster always reaches, with
+// its warp converged).
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -277,6 +278,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
+}
+
+// 16-byte store into the shared memory of any CTA of the cluster
+// (shared::cluster address); ordered for the owner by the next cluster barrier.
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
 }
 
 // Arrive on an mbarrier of any CTA of the cluster (shared::cluster address).

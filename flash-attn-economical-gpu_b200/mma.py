@@ -84,6 +84,32 @@ def _gemm(
     _native.check(rc, what)
 
 
+_KERNEL_NAMES = {_native.FAB_GEMM_KERNEL_SINGLE: "single", _native.FAB_GEMM_KERNEL_PAIR: "pair",
+                 _native.FAB_GEMM_KERNEL_SPLITK: "splitk"}
+
+
+def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
+                out_dtype: torch.dtype | None = None, device=None) -> tuple[str, int]:
+    """(kernel, k_split) that `matmul` runs for row-major contiguous operands of these shapes.
+
+    kernel: "single" (one CTA per 128x256 tile), "pair" (CTA pairs per 256x256 tile) or "splitk" (a cluster of
+    k_split CTAs shares each 128x256 tile's K).  No counterpart in the reference; it reads only the shapes.
+    """
+    out_dtype = in_dtype if out_dtype is None else out_dtype
+    p = _native.FabGemmParams()
+    p.a = p.b = p.c = 256  # only shapes are read
+    p.lda, p.ldb, p.ldc = max(int(K), 1), max(int(N), 1), max(int(N), 1)
+    p.M, p.N, p.K = int(M), int(N), int(K)
+    p.in_dtype = _native.dtype_code(in_dtype)
+    p.out_dtype = _native.dtype_code(out_dtype)
+    kernel, split = ctypes.c_int(0), ctypes.c_int(1)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _native.check(_native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)),
+                      "kernel_plan")
+    return _KERNEL_NAMES[kernel.value], split.value
+
+
 class _MatmulKernel:
     """Stands in for the Triton JITFunction `_matmul_contiguous_kernel`."""
 
@@ -233,6 +259,7 @@ __all__ = [
     "_matmul_contiguous_kernel",
     "matmul",
     "matmul_swiglu",
+    "kernel_plan",
     "interleave_gate_up",
     "split_gate_up",
     "get_architecture",

@@ -12,6 +12,8 @@ from pathlib import Path
 
 import pytest
 
+import torch
+
 import _native
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -220,3 +222,22 @@ def test_varlen_entry_validates_before_any_launch():
     assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
     p.total_q = 0  # nothing to compute
     assert lib.fab_attention_fwd_varlen(ctypes.byref(p), None) == _native.FAB_OK
+
+
+def test_gemm_plan_validates_like_gemm():
+    p = _native.FabGemmParams()
+    p.a = p.b = p.c = 256
+    p.lda, p.ldb, p.ldc = 64, 64, 64
+    p.M, p.N, p.K = 64, 64, 64
+    p.in_dtype = p.out_dtype = _native.dtype_code(torch.bfloat16)
+    kernel, split = ctypes.c_int(-1), ctypes.c_int(-1)
+    p.M = -1
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == \
+        _native.FAB_ERR_INVALID_ARG
+    p.M = 0  # nothing to compute
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == _native.FAB_OK
+    assert (kernel.value, split.value) == (_native.FAB_GEMM_KERNEL_SINGLE, 1)
+    p.M, p.ldc = 64, 32  # ldc < N
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == \
+        _native.FAB_ERR_INVALID_ARG
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), None, ctypes.byref(split)) == _native.FAB_ERR_INVALID_ARG
