@@ -368,10 +368,10 @@ int fab_attention_fwd_variant(const fab_attention_params* p, int variant, void* 
   bool empty = false;
   const int rc = attention_validate(L, &empty);
   if (rc || empty) return rc;
-  // The split-KV tile family run as a single pass: one key range, no merge.
+  // One query tile per CTA, one pass over all keys.
   L.num_splits = 1;
   L.split_len = L.N > 0 ? L.N : 1;
-  return fa_forward_split(L, static_cast<cudaStream_t>(stream));
+  return fa_forward_one_tile(L, static_cast<cudaStream_t>(stream));
 }
 
 int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_config* out) {
@@ -379,7 +379,7 @@ int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_c
   if (variant == FAB_FA_VARIANT_TWO_TILES) return fab_flash_attn_config(dtype, head_dim, out);
   if (variant != FAB_FA_VARIANT_ONE_TILE) return kErrInvalidArg;
   FaConfigInfo c;
-  const int rc = fa_select_split_config(dtype, head_dim, &c);
+  const int rc = fa_select_one_tile_config(dtype, head_dim, &c);
   if (rc) return rc;
   out->head_dim_padded = c.d_pad;
   out->q_tiles_per_cta = c.nq;

@@ -58,13 +58,19 @@ struct FaCfg {
   static constexpr int kKVTileBytes = kKVAtomBytes * kNumAtoms;
   static constexpr int kKInstr = 32 / kElt;          // K extent of one MMA instruction
   static constexpr int kThreads = 128 + kNQ * 128;
-  // Register split for the 384-thread shape: the launch gives every thread
-  // kLaunchRegs; the TMA/MMA warpgroup gives registers back so the two
-  // softmax warpgroups can hold a whole 128-column S row without spilling.
-  static constexpr bool kSplitRegs = kNQ == 2;
-  static constexpr int kLaunchRegs = 168;            // 65536 / 384, rounded down to 8
-  static constexpr int kProducerRegs = 72;
-  static constexpr int kSoftmaxRegs = 216;
+  // One Q tile with one S buffer: small enough (<= ~112 KB of shared memory,
+  // 256 TMEM columns, 128 registers a thread) that two CTAs share an SM, and
+  // the tensor core alternates between their tiles.
+  static constexpr bool kDual = kNQ == 1 && kSB == 1;
+  static constexpr int kCtasPerSm = kDual ? 2 : 1;
+  // Register split: the launch gives every thread kLaunchRegs; the TMA/MMA
+  // warpgroup gives registers back so the softmax warpgroups can hold a
+  // whole 128-column S row.  384 threads: 65536 / 384 rounded down to 8;
+  // two 256-thread CTAs: 32768 / 256.
+  static constexpr bool kSplitRegs = kNQ == 2 || kDual;
+  static constexpr int kLaunchRegs = kDual ? 128 : 168;
+  static constexpr int kProducerRegs = kDual ? 56 : 72;
+  static constexpr int kSoftmaxRegs = kDual ? 200 : 216;
   static_assert(!kSplitRegs || 128 * kProducerRegs + kNQ * 128 * kSoftmaxRegs <= kThreads * kLaunchRegs,
                 "register split exceeds the block's launch allocation");
   static constexpr int kSlots = kNQ * kSB;           // S/P buffers in TMEM
@@ -82,6 +88,7 @@ struct FaCfg {
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
   static_assert(kTmemUsed <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(!kDual || (2 * (kSmemBytes + 1024) <= 233472 && kTmemAlloc <= 256), "two CTAs per SM");
   __host__ __device__ static constexpr int tmem_s(int slot) { return slot * kBN; }
   __host__ __device__ static constexpr int tmem_o(int i) { return kSlots * kBN + i * kDP; }
 };
@@ -172,7 +179,7 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 }
 
 template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
-__global__ void __launch_bounds__(128 + kNQ * 128, 1)
+__global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 1)
     fa_fwd_kernel(const __grid_constant__ FaKernelParams p, const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kRing, kSB>;
@@ -914,6 +921,63 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream) {
   X(4, 64, 1, 128, 6, 2)    /* fp32/tf32, head dim <= 64 */ \
   X(4, 128, 1, 128, 2, 2)   /* fp32/tf32, head dim <= 128 */
 
+// The one-query-tile family run as a single pass (FAB_FA_VARIANT_ONE_TILE,
+// picked for shapes with few query tiles): two CTAs per SM with one S buffer
+// each where that fits and the launch has at least 1.5 CTAs per SM, so that
+// most SMs hold two tiles that take turns on the tensor core; otherwise (or
+// with too few CTAs, when a lone one-buffer CTA would leave its tensor core
+// idle during every softmax) the split-KV tiles, whose two S buffers overlap
+// S(j+1) with softmax(j) inside one CTA.
+#define FAB_FA_ONE_TILE_TABLE(X)                                         \
+  X(2, 64, 1, 128, 4, 1)    /* 16-bit, head dim <= 64: 2 CTAs/SM */      \
+  X(2, 128, 1, 128, 2, 1)   /* 16-bit, head dim <= 128: 2 CTAs/SM */     \
+  X(2, 256, 1, 128, 2, 2)   /* 16-bit, head dim <= 256 */                \
+  X(4, 64, 1, 128, 2, 1)    /* fp32/tf32, head dim <= 64: 2 CTAs/SM */   \
+  X(4, 128, 1, 128, 2, 2)   /* fp32/tf32, head dim <= 128 */
+
+int fa_select_one_tile_config(int dtype, int D, FaConfigInfo* out) {
+  if (D <= 0) return kErrInvalidArg;
+  if (dtype != kDtypeF16 && dtype != kDtypeBF16 && dtype != kDtypeF32) return kErrInvalidArg;
+  const int elt = dtype == kDtypeF32 ? 4 : 2;
+  int best = 0;
+#define FAB_FA_OPICK(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && D <= DP && (best == 0 || DP < best)) best = DP;
+  FAB_FA_ONE_TILE_TABLE(FAB_FA_OPICK)
+#undef FAB_FA_OPICK
+  if (best == 0) return kErrUnsupported;
+#define FAB_FA_OFILL(E, DP, NQ, BN, ST, SB)                                                      \
+  if (elt == E && best == DP) {                                                                 \
+    using Cf = FaCfg<E, DP, NQ, BN, ST, SB>;                                                    \
+    *out = FaConfigInfo{DP, NQ, BN, ST, Cf::kThreads, Cf::kSmemBytes, Cf::kTmemAlloc, SB};      \
+    return 0;                                                                                   \
+  }
+  FAB_FA_ONE_TILE_TABLE(FAB_FA_OFILL)
+#undef FAB_FA_OFILL
+  return kErrUnsupported;
+}
+
+int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
+
+int fa_forward_one_tile(const FaLaunch& L, cudaStream_t stream) {
+  FaConfigInfo c;
+  int rc = fa_select_one_tile_config(L.dtype, L.D, &c);
+  if (rc) return rc;
+  if (c.s_bufs == 1) {
+    const long long rows = L.pack_gqa ? static_cast<long long>(L.Hq / L.Hkv) * L.M : L.M;
+    const long long ctas = (rows + 127) / 128 * L.B * (L.pack_gqa ? L.Hkv : L.Hq) * std::max(L.num_splits, 1);
+    const int sms = num_sms();
+    if (sms <= 0) return kErrCuda;
+    if (2 * ctas < 3LL * sms) return fa_forward_split(L, stream);
+  }
+  const int elt = L.dtype == kDtypeF32 ? 4 : 2;
+  rc = kErrUnsupported;
+#define FAB_FA_OLAUNCH(E, DP, NQ, BN, ST, SB) \
+  if (elt == E && c.d_pad == DP) rc = launch_entry<E, DP, NQ, BN, ST, SB>(L, stream);
+  FAB_FA_ONE_TILE_TABLE(FAB_FA_OLAUNCH)
+#undef FAB_FA_OLAUNCH
+  return rc;
+}
+
 int fa_select_split_config(int dtype, int D, FaConfigInfo* out) {
   if (D <= 0) return kErrInvalidArg;
   if (dtype != kDtypeF16 && dtype != kDtypeBF16 && dtype != kDtypeF32) return kErrInvalidArg;
@@ -1004,14 +1068,14 @@ int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
 
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile) {
   FaConfigInfo c;
-  int rc = one_tile ? fa_select_split_config(dtype, D, &c) : fa_select_config(dtype, D, &c);
+  int rc = one_tile ? fa_select_one_tile_config(dtype, D, &c) : fa_select_config(dtype, D, &c);
   if (rc) return rc;
   const int elt = dtype == kDtypeF32 ? 4 : 2;
   const void* k = nullptr;
 #define FAB_FA_ATTR(E, DP, NQ, BN, ST, SB) \
   if (elt == E && c.d_pad == DP) k = kernel_entry<E, DP, NQ, BN, ST, SB>(dtype);
   if (one_tile) {
-    FAB_FA_SPLIT_TABLE(FAB_FA_ATTR)
+    FAB_FA_ONE_TILE_TABLE(FAB_FA_ATTR)
   } else {
     FAB_FA_TABLE(FAB_FA_ATTR)
   }

@@ -145,6 +145,8 @@ struct GemmLaunch {
 int fa_select_config(int dtype, int D, FaConfigInfo* out);
 int fa_forward(const FaLaunch& L, cudaStream_t stream);
 int fa_select_split_config(int dtype, int D, FaConfigInfo* out);
+int fa_select_one_tile_config(int dtype, int D, FaConfigInfo* out);
+int fa_forward_one_tile(const FaLaunch& L, cudaStream_t stream);
 // num_splits <= 0 picks a split count from the SM count (needs a device).
 int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
 // Launches the split kernel and the combine kernel; L carries the plan.

@@ -348,8 +348,11 @@ int fab_flash_attn_config(int dtype, int head_dim, fab_fa_config* out);
  * Tile families for fab_attention_fwd_variant / fab_flash_attn_config_variant.
  * TWO_TILES is the table fab_attention_fwd uses (two 128-row query tiles per
  * CTA where TMEM allows, one S buffer each); ONE_TILE is one 128-row query
- * tile with two S buffers (more CTAs for the same rows: better for short or
- * few sequences).  Which is faster depends on the shape; the Python tuner
+ * tile per CTA (more CTAs for the same rows: better for short or few
+ * sequences) -- with one S buffer and two CTAs per SM where shared memory
+ * allows (16-bit head dim <= 128, fp32 <= 64; the config reports s_buffers 1)
+ * and the launch has at least 1.5 CTAs per SM, else two S buffers and one
+ * CTA per SM.  Which is faster depends on the shape; the Python tuner
  * picks by measured time (the reference picks the largest tile that fits,
  * tuner.py:503-517).
  */
