@@ -55,10 +55,15 @@ WORKLOADS = {
     "fa_s4096_noncausal": (4, 32, 32, 4096, 128, False),
     "fa_s2048_noncausal": (4, 32, 32, 2048, 128, False),
     "fa_s1024_noncausal": (4, 32, 32, 1024, 128, False),
+    "fa_s4096_causal": (4, 32, 32, 4096, 128, True),
+    "fa_s2048_causal": (4, 32, 32, 2048, 128, True),
+    "fa_s1024_causal": (4, 32, 32, 1024, 128, True),
+    "fa_d256_s4096_causal": (2, 16, 16, 4096, 256, True),
+    "fa_d256_s2048_causal": (2, 16, 16, 2048, 256, True),
     "fa_d256_s8192_causal": (2, 16, 16, 8192, 256, True),
     "fa_gqa_s8192_causal": (2, 16, 4, 8192, 128, True),
 }
-GEMM_WORKLOADS = {"gemm_8192": 8192, "gemm_16384": 16384, "gemm_4096": 4096}
+GEMM_WORKLOADS = {"gemm_8192": 8192, "gemm_16384": 16384, "gemm_4096": 4096, "gemm_2048": 2048, "gemm_1024": 1024}
 # Split-KV decode steps (not a BASELINE config; K/V cache resident on the device):
 # name: (B, Hq, Hkv, query rows, keys, D)
 DECODE_WORKLOADS = {
@@ -191,6 +196,15 @@ def setup_dist(args):
     return world, rank, local
 
 
+def host_lead(ms=3.0):
+    """Queue a device-side sleep ahead of the timed launches.
+
+    The host then enqueues the timed steps while the GPU is still busy, so each event pair brackets device time
+    only, not the host's launch latency (tens of microseconds per call through Python and ctypes, as long as a
+    whole 1024^3 matmul).  The sleep itself ends before the first timed event."""
+    torch.cuda._sleep(int(ms * 1e-3 * 1.965e9))
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -309,6 +323,7 @@ def run_attention(args, world, rank, local):
     with ClockSampler(local) as clocks:
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
+        host_lead()
         t_begin.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
@@ -636,23 +651,32 @@ def run_gemm(args, world, rank, local):
     flops = 2.0 * n ** 3
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if 3 * n * n * 2 < L2_BYTES * 2 else None
-    for _ in range(args.warmup):
-        matmul(a, b)
-    torch.cuda.synchronize(dev)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    total_ms = 0.0
-    with ClockSampler(local) as clocks:
-        for i in range(args.steps):
+    c = torch.empty(n, n, device=dev, dtype=dtype)
+
+    def timed_steps(fn, steps):
+        """Device ms of `steps` calls, each after an L2 flush (small sizes), events around the call alone."""
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        host_lead()
+        for i in range(steps):
             if flush is not None:
                 flush.zero_()
             starts[i].record(stream)
-            matmul(a, b)
+            fn()
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
-    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+    def ours():
+        matmul(a, b)
+
+    for _ in range(args.warmup):
+        ours()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        total_ms = timed_steps(ours, args.steps)
     barrier(world)
     total_ms = max_over_ranks(total_ms, world)
     if _native.device_error():
@@ -661,17 +685,14 @@ def run_gemm(args, world, rank, local):
     achieved = flops / (total_ms / args.steps / 1e3) / 1e12
     comparators = {}
     if rank == 0 and not args.no_compare:
+        def cublas():
+            torch.matmul(a, b, out=c)
+
         for _ in range(3):
-            torch.matmul(a, b)
+            cublas()
         torch.cuda.synchronize(dev)
-        c0 = torch.cuda.Event(enable_timing=True)
-        c1 = torch.cuda.Event(enable_timing=True)
-        c0.record(stream)
-        for _ in range(10):
-            torch.matmul(a, b)
-        c1.record(stream)
-        torch.cuda.synchronize(dev)
-        comparators["torch_matmul_cublas_tflops"] = round(flops * 10 / (c0.elapsed_time(c1) / 1e3) / 1e12, 1)
+        ms = timed_steps(cublas, 10)
+        comparators["torch_matmul_cublas_tflops"] = round(flops * 10 / (ms / 1e3) / 1e12, 1)
     return {
         "metric": METRIC,
         "value": round(value, 1),

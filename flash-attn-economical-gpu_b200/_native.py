@@ -133,7 +133,8 @@ PROTOTYPES = {
     "fab_attention_fwd_splitkv_static": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
     "fab_matmul_contiguous": (_i32, [_vp] * 3 + [_i32] * 6 + [_vp]),
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
-    "fab_gemm_plan": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "fab_gemm_plan": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                             ctypes.POINTER(_i32)]),
     "fab_gemm_allreduce_layout": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_size_t),
                                          ctypes.POINTER(ctypes.c_size_t)]),
     "fab_gemm_allreduce": (_i32, [ctypes.POINTER(FabGemmAllreduceParams), _vp]),
@@ -151,7 +152,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 def _load() -> ctypes.CDLL:

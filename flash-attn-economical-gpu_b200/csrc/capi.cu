@@ -254,7 +254,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 5; }
+int fab_abi_version(void) { return 6; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -552,15 +552,16 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
 }
 
-int fab_gemm_plan(const fab_gemm_params* p, int* kernel, int* k_split) {
-  if (kernel == nullptr || k_split == nullptr) return kErrInvalidArg;
+int fab_gemm_plan(const fab_gemm_params* p, int* kernel, int* k_split, int* tile_n) {
+  if (kernel == nullptr || k_split == nullptr || tile_n == nullptr) return kErrInvalidArg;
   *kernel = FAB_GEMM_KERNEL_SINGLE;
   *k_split = 1;
+  *tile_n = 256;
   GemmLaunch L;
   bool nothing, empty_k;
   const int rc = gemm_validate(p, &L, &nothing, &empty_k);
   if (rc || nothing || empty_k) return rc;
-  return gemm_plan(L, kernel, k_split);
+  return gemm_plan(L, kernel, k_split, tile_n);
 }
 
 int fab_gemm_allreduce_layout(int M, int N, int world, int* tiles_per_owner, size_t* inbox_bytes,

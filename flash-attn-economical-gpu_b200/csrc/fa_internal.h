@@ -153,7 +153,7 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
 int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile = false);
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
-int gemm_plan(const GemmLaunch& L, int* kernel, int* split);
+int gemm_plan(const GemmLaunch& L, int* kernel, int* split, int* tile_n);
 // Output tiles of the fused GEMM + all-reduce: tile t belongs to rank t % world.
 int gemm_ar_tiles(int M, int N);
 int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t stream);

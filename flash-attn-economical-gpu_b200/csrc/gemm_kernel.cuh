@@ -42,12 +42,14 @@
 
 namespace fab {
 
-template <int kElt>
+// kBN_: output tile width, 256 by default; 128 or 64 (with more stages) for
+// problems whose 256-wide tiles would leave many SMs idle.
+template <int kElt, int kBN_ = 256, int kStages_ = 4>
 struct GemmCfg {
   static constexpr int kBM = 128;
-  static constexpr int kBN = 256;
+  static constexpr int kBN = kBN_;
   static constexpr int kBK = 128 / kElt;             // one 128-byte swizzle atom of K
-  static constexpr int kStages = 4;
+  static constexpr int kStages = kStages_;
   static constexpr int kKInstr = 32 / kElt;
   static constexpr int kABytes = kBM * 128;          // 128 rows x one atom
   static constexpr int kBAtomN = 128 / kElt;         // N elements per B atom
@@ -55,7 +57,8 @@ struct GemmCfg {
   static constexpr int kBBytes = (kBN / kBAtomN) * kBAtomBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kThreads = 256;
-  static constexpr int kTmemCols = 512;              // 2 x 256 fp32 accumulators
+  static constexpr int kTmemCols = 2 * kBN;          // two fp32 accumulators
+  static_assert(kBN == 64 || kBN == 128 || kBN == 256, "tile width");
   static constexpr int kNumBars = 2 * kStages + 4 + 1;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 64;  // + 16 status words
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -270,11 +273,12 @@ __device__ __forceinline__ int claim_ready_tile(int* next, const GemmArParams& a
   }
 }
 
-template <typename Tin, typename Tout, bool kAR>
+template <typename Tin, typename Tout, bool kAR, int kBN = 256, int kStages = 4>
 __global__ void __launch_bounds__(256, 1)
     gemm_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
                 const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ GemmArParams ar) {
-  using C = GemmCfg<sizeof(Tin)>;
+  using C = GemmCfg<sizeof(Tin), kBN, kStages>;
+  static_assert(!kAR || kBN == 256, "the fused all-reduce epilogue moves 256-column rows");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -586,10 +590,10 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-template <typename Tin, typename Tout, bool kAR = false>
+template <typename Tin, typename Tout, bool kAR = false, int kBN = 256, int kStages = 4>
 static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArParams* ar = nullptr) {
-  using C = GemmCfg<sizeof(Tin)>;
-  auto kern = gemm_kernel<Tin, Tout, kAR>;
+  using C = GemmCfg<sizeof(Tin), kBN, kStages>;
+  auto kern = gemm_kernel<Tin, Tout, kAR, kBN, kStages>;
   constexpr int kSmem = C::kSmemBytes + (kAR ? 128 + 32 * 32 * 16 : 0);  // reducer staging
   static_assert(kSmem <= 232448, "shared memory budget");
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmem);
@@ -661,11 +665,29 @@ static int gemm_splitk_factor_out(const GemmLaunch& L) {
   return 1;
 }
 
-// Which kernel gemm_forward runs for L: 0 single CTA per tile, 1 CTA pairs,
-// 2 split K over a cluster of *split CTAs per tile.
-int gemm_plan(const GemmLaunch& L, int* kernel, int* split) {
+// Output tile width of the single-CTA kernel: 256, unless that leaves more
+// than a quarter of the SMs without a tile; then the widest of 128 and 64
+// that gives at least 3/4 of the SMs a tile (64 if neither does).  Narrow
+// tiles spread a small problem's loads over more SMs and keep more stages in
+// flight per CTA (6 and 8), which is what a short kernel with a cold L2
+// waits on.  16-bit inputs without the SwiGLU epilogue only.
+static int gemm_single_width(const GemmLaunch& L) {
+  if (L.swiglu || (L.in_dtype != kDtypeF16 && L.in_dtype != kDtypeBF16)) return 256;
+  const int sms = num_sms();
+  if (sms <= 0) return 256;
+  const long long rows = (L.M + 127) / 128;
+  auto tiles = [&](int w) { return rows * ((L.N + w - 1) / w); };
+  if (4 * tiles(256) >= 3LL * sms) return 256;
+  if (4 * tiles(128) >= 3LL * sms) return 128;
+  return 64;
+}
+
+// Which kernel gemm_forward runs for L: 0 single CTA per tile (*tile_n wide),
+// 1 CTA pairs, 2 split K over a cluster of *split CTAs per tile.
+int gemm_plan(const GemmLaunch& L, int* kernel, int* split, int* tile_n) {
   *kernel = 0;
   *split = 1;
+  *tile_n = 256;
   if (L.M <= 0 || L.N <= 0 || L.K <= 0) return 0;
 #ifndef FAB_GEMM_NO_SPLITK
   if (L.in_dtype == kDtypeF16 || L.in_dtype == kDtypeBF16) {
@@ -677,8 +699,21 @@ int gemm_plan(const GemmLaunch& L, int* kernel, int* split) {
     }
   }
 #endif
-  if (gemm_use_pair(L)) *kernel = 1;
+  if (gemm_use_pair(L))
+    *kernel = 1;
+  else
+    *tile_n = gemm_single_width(L);
   return 0;
+}
+
+template <typename Tin, typename Tout>
+static int launch_gemm_single(const GemmLaunch& L, cudaStream_t stream) {
+  if constexpr (sizeof(Tin) == 2) {
+    const int w = gemm_single_width(L);
+    if (w == 64) return launch_gemm<Tin, Tout, false, 64, 8>(L, stream);
+    if (w == 128) return launch_gemm<Tin, Tout, false, 128, 6>(L, stream);
+  }
+  return launch_gemm<Tin, Tout>(L, stream);
 }
 
 template <typename Tin>
@@ -714,13 +749,13 @@ int gemm_forward(const GemmLaunch& L, cudaStream_t stream) {
     return kErrInvalidArg;
   }
   if (in == kDtypeF16) {
-    if (out == kDtypeF16) return launch_gemm<__half, __half>(L, stream);
-    if (out == kDtypeBF16) return launch_gemm<__half, __nv_bfloat16>(L, stream);
-    if (out == kDtypeF32) return launch_gemm<__half, float>(L, stream);
+    if (out == kDtypeF16) return launch_gemm_single<__half, __half>(L, stream);
+    if (out == kDtypeBF16) return launch_gemm_single<__half, __nv_bfloat16>(L, stream);
+    if (out == kDtypeF32) return launch_gemm_single<__half, float>(L, stream);
   } else if (in == kDtypeBF16) {
-    if (out == kDtypeF16) return launch_gemm<__nv_bfloat16, __half>(L, stream);
-    if (out == kDtypeBF16) return launch_gemm<__nv_bfloat16, __nv_bfloat16>(L, stream);
-    if (out == kDtypeF32) return launch_gemm<__nv_bfloat16, float>(L, stream);
+    if (out == kDtypeF16) return launch_gemm_single<__nv_bfloat16, __half>(L, stream);
+    if (out == kDtypeBF16) return launch_gemm_single<__nv_bfloat16, __nv_bfloat16>(L, stream);
+    if (out == kDtypeF32) return launch_gemm_single<__nv_bfloat16, float>(L, stream);
   } else if (in == kDtypeF32) {
     if (out == kDtypeF16) return launch_gemm<float, __half>(L, stream);
     if (out == kDtypeBF16) return launch_gemm<float, __nv_bfloat16>(L, stream);

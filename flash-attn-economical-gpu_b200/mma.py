@@ -89,11 +89,12 @@ _KERNEL_NAMES = {_native.FAB_GEMM_KERNEL_SINGLE: "single", _native.FAB_GEMM_KERN
 
 
 def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
-                out_dtype: torch.dtype | None = None, device=None) -> tuple[str, int]:
-    """(kernel, k_split) that `matmul` runs for row-major contiguous operands of these shapes.
+                out_dtype: torch.dtype | None = None, device=None) -> tuple[str, int, int]:
+    """(kernel, k_split, tile_n) that `matmul` runs for row-major contiguous operands of these shapes.
 
-    kernel: "single" (one CTA per 128x256 tile), "pair" (CTA pairs per 256x256 tile) or "splitk" (a cluster of
-    k_split CTAs shares each 128x256 tile's K).  No counterpart in the reference; it reads only the shapes.
+    kernel: "single" (one CTA per 128 x tile_n tile; tile_n 256, or 128 / 64 for small 16-bit problems), "pair"
+    (CTA pairs per 256x256 tile) or "splitk" (a cluster of k_split CTAs shares each 128x256 tile's K).  No
+    counterpart in the reference; it reads only the shapes.
     """
     out_dtype = in_dtype if out_dtype is None else out_dtype
     p = _native.FabGemmParams()
@@ -102,12 +103,12 @@ def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
     p.M, p.N, p.K = int(M), int(N), int(K)
     p.in_dtype = _native.dtype_code(in_dtype)
     p.out_dtype = _native.dtype_code(out_dtype)
-    kernel, split = ctypes.c_int(0), ctypes.c_int(1)
+    kernel, split, tile_n = ctypes.c_int(0), ctypes.c_int(1), ctypes.c_int(256)
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
-        _native.check(_native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)),
-                      "kernel_plan")
-    return _KERNEL_NAMES[kernel.value], split.value
+        _native.check(_native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split),
+                                                ctypes.byref(tile_n)), "kernel_plan")
+    return _KERNEL_NAMES[kernel.value], split.value, tile_n.value
 
 
 class _MatmulKernel:

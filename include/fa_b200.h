@@ -235,18 +235,20 @@ int fab_gemm(const fab_gemm_params* params, void* stream);
 /*
  * Which kernel fab_gemm runs for these parameters (no counterpart in the
  * reference; like the launch facts of `_select_2d_contiguous_config`,
- * mma.py:22-81, it only reads the shapes): one CTA per 128x256 output tile,
- * CTA pairs per 256x256 tile (16-bit inputs, at least one wave of pairs), or
- * split K, where the *k_split CTAs of a cluster share each 128x256 tile's K
- * and add their partial sums in distributed shared memory (16-bit inputs, too
- * few tiles for half the SMs).  Validates like fab_gemm; pointers are not
- * dereferenced.  Nothing to compute (M, N or K zero) reports SINGLE, 1.
+ * mma.py:22-81, it only reads the shapes): one CTA per 128 x *tile_n output
+ * tile (*tile_n 256, or 128 / 64 for 16-bit problems whose 256-wide tiles
+ * would leave over a quarter of the SMs idle), CTA pairs per 256x256 tile
+ * (16-bit inputs, at least one wave of pairs), or split K, where the
+ * *k_split CTAs of a cluster share each 128x256 tile's K and add their
+ * partial sums in distributed shared memory (16-bit inputs, few tiles, deep
+ * K).  Validates like fab_gemm; pointers are not dereferenced.  Nothing to
+ * compute (M, N or K zero) reports SINGLE, 1, 256.
  */
 #define FAB_GEMM_KERNEL_SINGLE 0
 #define FAB_GEMM_KERNEL_PAIR 1
 #define FAB_GEMM_KERNEL_SPLITK 2
 
-int fab_gemm_plan(const fab_gemm_params* params, int* kernel, int* k_split);
+int fab_gemm_plan(const fab_gemm_params* params, int* kernel, int* k_split, int* tile_n);
 
 /*
  * GEMM + all-reduce over the ranks of a tensor-parallel group in one kernel,

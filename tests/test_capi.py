@@ -230,14 +230,15 @@ def test_gemm_plan_validates_like_gemm():
     p.lda, p.ldb, p.ldc = 64, 64, 64
     p.M, p.N, p.K = 64, 64, 64
     p.in_dtype = p.out_dtype = _native.dtype_code(torch.bfloat16)
-    kernel, split = ctypes.c_int(-1), ctypes.c_int(-1)
+    kernel, split, tile_n = ctypes.c_int(-1), ctypes.c_int(-1), ctypes.c_int(-1)
     p.M = -1
-    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == \
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split), ctypes.byref(tile_n)) == \
         _native.FAB_ERR_INVALID_ARG
     p.M = 0  # nothing to compute
-    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == _native.FAB_OK
-    assert (kernel.value, split.value) == (_native.FAB_GEMM_KERNEL_SINGLE, 1)
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split), ctypes.byref(tile_n)) == _native.FAB_OK
+    assert (kernel.value, split.value, tile_n.value) == (_native.FAB_GEMM_KERNEL_SINGLE, 1, 256)
     p.M, p.ldc = 64, 32  # ldc < N
-    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split)) == \
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split), ctypes.byref(tile_n)) == \
         _native.FAB_ERR_INVALID_ARG
-    assert _native.lib.fab_gemm_plan(ctypes.byref(p), None, ctypes.byref(split)) == _native.FAB_ERR_INVALID_ARG
+    assert _native.lib.fab_gemm_plan(ctypes.byref(p), None, ctypes.byref(split), ctypes.byref(tile_n)) == \
+        _native.FAB_ERR_INVALID_ARG

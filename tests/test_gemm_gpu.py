@@ -143,3 +143,51 @@ def test_config4_full_size(n, dtype, cuda_device):
     assert err < 2e-3 * n ** 0.5 * 8, err
     del a, b, c
     torch.cuda.empty_cache()
+
+
+# ------------------------------------------------------ narrow tiles for small problems
+NARROW = [
+    # M, N, K, tile width the plan takes: 256-wide tiles would leave over a quarter of the 148 SMs idle
+    (1024, 1024, 1024, 64),   # 32 tiles of 256, 128 of 64
+    (1536, 1536, 512, 128),   # 72 tiles of 256, 144 of 128
+    (300, 1000, 520, 64),     # ragged M, N and K
+    (129, 200, 72, 64),       # one partial K block past the first, ragged everywhere
+    (1, 64, 256, 64),         # one row, one tile
+]
+
+
+@pytest.mark.parametrize("shape", NARROW, ids=lambda s: "M{}N{}K{}".format(*s[:3]))
+@pytest.mark.parametrize("dtype, out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float16),
+                                              (torch.bfloat16, torch.float32), (torch.float16, torch.bfloat16)],
+                         ids=lambda d: NAME[d])
+def test_narrow_tiles_match_oracle(shape, dtype, out_dtype, cuda_device):
+    M, N, K, width = shape
+    assert mma.kernel_plan(M, N, K, dtype, out_dtype) == ("single", 1, width)
+    g = torch.Generator(device=cuda_device).manual_seed(M * 7 + N + K)
+    a = (torch.randn(M, K, generator=g, device=cuda_device) / K ** 0.5).to(dtype)
+    b = (torch.randn(K, N, generator=g, device=cuda_device) / K ** 0.5).to(dtype)
+    c = matmul(a, b, out_dtype=out_dtype)
+    ref = tiled_matmul(a.float().cpu().numpy(), b.float().cpu().numpy(), round_f16=False, out_dtype=NAME[out_dtype])
+    _close(c, ref)
+
+
+def test_narrow_tiles_round_f16_strided_and_deterministic(cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    a_full = (torch.randn(700, 1104, generator=g, device=cuda_device) / 1000 ** 0.5).to(torch.bfloat16)
+    b_full = (torch.randn(1104, 1200, generator=g, device=cuda_device) / 1000 ** 0.5).to(torch.bfloat16)
+    a, b = a_full[:, :1000], b_full[:1000, 64:1064]
+    assert mma.kernel_plan(700, 1000, 1000)[2] == 64
+    c_full = torch.full((700, 1088), 5.0, device=cuda_device, dtype=torch.bfloat16)
+    c = c_full[:, :1000]
+    mma._gemm(a, b, c, 700, 1000, 1000, lda=a.stride(0), ldb=b.stride(0), ldc=c.stride(0), round_f16=True)
+    ref = tiled_matmul(a.float().cpu().numpy(), b.float().cpu().numpy(), round_f16=True, out_dtype="bf16")
+    _close(c, ref)
+    assert torch.all(c_full[:, 1000:] == 5.0)
+    c2 = torch.empty_like(c_full)
+    mma._gemm(a, b, c2, 700, 1000, 1000, lda=a.stride(0), ldb=b.stride(0), ldc=c2.stride(0), round_f16=True)
+    assert torch.equal(c2[:, :1000], c)
+
+
+def test_wide_tiles_where_they_fill_the_gpu(cuda_device):
+    assert mma.kernel_plan(2048, 2048, 2048) == ("single", 1, 256)
+    assert mma.kernel_plan(1024, 1024, 1024, torch.float32) == ("single", 1, 256)  # tf32 keeps 256

@@ -59,7 +59,7 @@ SHAPES = [
                          ids=lambda d: NAME[d])
 def test_splitk_matches_oracle(shape, dtype, out_dtype, cuda_device):
     M, N, K, splits = shape
-    kernel, split = kernel_plan(M, N, K, dtype, out_dtype)
+    kernel, split, _ = kernel_plan(M, N, K, dtype, out_dtype)
     assert kernel == "splitk" and split in splits
     a, b = _inputs(M, N, K, dtype, cuda_device, seed=M + N + K)
     _check(a, b, matmul(a, b, out_dtype=out_dtype))
