@@ -181,7 +181,8 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
 __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 1)
     fa_fwd_kernel(const __grid_constant__ FaKernelParams p, const __grid_constant__ CUtensorMap tm_q,
-                  const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+                  const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                  const __grid_constant__ CUtensorMap tm_o) {
   using C = FaCfg<sizeof(T), kDP, kNQ, kBN, kRing, kSB>;
   constexpr float kNegInf = -INFINITY;
 
@@ -605,7 +606,61 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
     float* lse_out = p.o_part != nullptr ? p.lse_part + part_row
                      : p.lse != nullptr  ? p.lse + l_boff + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm
                                          : nullptr;
-    if (ok && nt > 0) {
+    bool via_tma = false;
+    if constexpr (sizeof(T) == 2) {
+      if (nt > 0 && p.o_tma) {
+        via_tma = true;
+        // Dense 16-bit O: the tile is staged in this Q tile's shared memory,
+        // idle once O is final (every S product has completed by then), in
+        // the 128-byte swizzled layout of a tm_o box, and written by one TMA
+        // tensor store per 64-column atom: whole lines, clipped at the
+        // tensor's bounds, instead of 16-byte pieces of 128 rows.  All four
+        // warps reach the named barrier on every path.
+        const uint32_t last_phase = kSB == 2 ? ((nt - 1) & 1) : 0u;
+        const bool got = ok && mbar_wait_warp(bar_o_done + i, last_phase, abort_flag, kDevTimeoutO);
+        tc_fence_after();
+        uint8_t* stage = sQ + i * C::kQTileBytes;
+        if (got) {
+          const float inv_l = 1.0f / l_run;
+#pragma unroll 1
+          for (int cc = 0; cc < kDP / 32; ++cc) {
+            uint32_t rr[32];
+            tmem_ld32(t_o + cc * 32, rr);
+            tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[e] = ElemOps<T>::pack2(__uint_as_float(rr[2 * e]) * inv_l, __uint_as_float(rr[2 * e + 1]) * inv_l);
+            uint8_t* rowp = stage + ((cc * 32) / C::kAtom) * C::kQAtomBytes + r * 128;
+            const int chunk0 = ((cc * 32) % C::kAtom) * static_cast<int>(sizeof(T)) / 16;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(rowp + (((chunk0 + q) ^ (r & 7)) * 16)) =
+                  make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        // Compile-time ids, so the kernel reserves only the barriers it names.
+        if (i == 0)
+          named_barrier_sync(1, 128);
+        else
+          named_barrier_sync(2, 128);
+        if (r == 0 && got) {
+#pragma unroll
+          for (int a = 0; a < C::kNumAtoms; ++a)
+            tma_store_4d(&tm_o, stage + a * C::kQAtomBytes, a * C::kAtom, m0 + i * C::kBM, h, b);
+          bulk_commit_group();
+          bulk_wait_read_all();
+        }
+        if (got && lse_out != nullptr && row_ok) {
+          const float m_base = (m_run == kNegInf) ? 0.f : m_run;
+          *lse_out = (m_base + log2f(l_run)) * 0.6931471805599453f;
+        }
+      }
+    }
+    if (via_tma) {
+      // written above
+    } else if (ok && nt > 0) {
       // One S buffer: O's only commit comes after the last product (phase 0);
       // two: one commit per KV tile.
       const uint32_t last_phase = kSB == 2 ? ((nt - 1) & 1) : 0u;
@@ -739,6 +794,17 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   kp.lse_part = L.lse_part;
   kp.cu_q = L.cu_q;
   kp.cu_k = L.cu_k;
+  // O through TMA tensor stores where the map allows it (dense, one query
+  // head per row block, 16-bit, 16-byte-aligned base and strides).
+  CUtensorMap to = tq;  // not read when o_tma is 0
+  kp.o_tma = 0;
+  if (elt == 2 && !varlen && !L.pack_gqa && L.o_part == nullptr && L.M > 0) {
+    if (make_bhsd_map(&to, L.o, dt, elt, L.D, L.M, L.Hq, L.B, L.o_ss, L.o_sh, L.o_sb, C::kAtom, C::kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) == 0)
+      kp.o_tma = 1;
+    else
+      to = tq;
+  }
   const int items = L.B * (L.pack_gqa ? L.Hkv : L.Hq);
   const long long grid = static_cast<long long>(kp.num_m_blocks) * items;
   if (grid <= 0) return 0;
@@ -755,7 +821,7 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   }
   if (grid > 0x7fffffffLL || splits > 65535) return kErrInvalidArg;
   kern<<<dim3(static_cast<unsigned>(grid), static_cast<unsigned>(splits)), C::kThreads, C::kSmemBytes, stream>>>(
-      kp, tq, tk, tv);
+      kp, tq, tk, tv, to);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 

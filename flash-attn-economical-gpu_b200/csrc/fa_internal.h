@@ -51,6 +51,9 @@ struct FaKernelParams {
   // cu_k); M and N are then the longest lengths.  NULL for dense batches.
   const int* cu_q;
   const int* cu_k;
+  // 1: O (dense, 16-bit, 16-byte-aligned strides) is written by TMA tensor
+  // stores from shared memory through the tm_o map; 0: direct stores.
+  int o_tma;
 };
 
 // A fully validated attention launch (element strides, unit stride on D).

@@ -115,6 +115,24 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) 
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// ----------------------------------------------------- TMA tensor stores ---
+// Store one box of shared memory (laid out as the map's box, swizzle
+// included) to global memory at the given coordinates; the box is clipped at
+// the tensor's bounds.  Generic-proxy writes to `src` must be fenced with
+// fence_proxy_async_smem() first; the store is complete for shared memory
+// (may be overwritten / the CTA may exit) after bulk_wait_read_all().
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ------------------------------------------------- cross-GPU signalling ---
 // Counters in (possibly peer) global memory, ordered at system scope so that
 // NVLink peer stores issued before a release are visible after the matching
