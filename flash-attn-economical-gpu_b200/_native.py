@@ -26,6 +26,7 @@ FAB_ERR_WORKSPACE = 6
 
 FAB_GEMM_EPILOGUE_STORE = 0
 FAB_GEMM_EPILOGUE_SWIGLU = 1
+FAB_GEMM_EPILOGUE_BIAS_ROPE = 2
 FAB_GEMM_KERNEL_SINGLE = 0
 FAB_GEMM_KERNEL_PAIR = 1
 FAB_GEMM_KERNEL_SPLITK = 2
@@ -68,6 +69,7 @@ class FabGemmParams(ctypes.Structure):
         ("lda", _i64), ("ldb", _i64), ("ldc", _i64),
         ("M", _i32), ("N", _i32), ("K", _i32),
         ("in_dtype", _i32), ("out_dtype", _i32), ("round_f16", _i32), ("group_m", _i32), ("epilogue", _i32),
+        ("bias", _vp), ("rope_cos", _vp), ("rope_sin", _vp), ("rope_cols", _i32), ("head_dim", _i32),
     ]
 
 
@@ -152,7 +154,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 def _load() -> ctypes.CDLL:

@@ -254,7 +254,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 6; }
+int fab_abi_version(void) { return 7; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -507,9 +507,23 @@ static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothin
     if (dt != kDtypeF16 && dt != kDtypeBF16 && dt != kDtypeF32) return kErrInvalidArg;
   if (p->c == nullptr || !aligned16(p->c)) return kErrInvalidArg;
   const int oe = elt_size(p->out_dtype);
-  if (p->epilogue != FAB_GEMM_EPILOGUE_STORE && p->epilogue != FAB_GEMM_EPILOGUE_SWIGLU) return kErrInvalidArg;
+  if (p->epilogue != FAB_GEMM_EPILOGUE_STORE && p->epilogue != FAB_GEMM_EPILOGUE_SWIGLU &&
+      p->epilogue != FAB_GEMM_EPILOGUE_BIAS_ROPE)
+    return kErrInvalidArg;
   const bool swiglu = p->epilogue == FAB_GEMM_EPILOGUE_SWIGLU;
   if (swiglu && (p->N % 128 != 0 || oe != 2 || p->round_f16)) return kErrInvalidArg;
+  const bool rope = p->epilogue == FAB_GEMM_EPILOGUE_BIAS_ROPE;
+  if (rope) {
+    // Whole heads inside 256-column tiles; bias and tables in the output type.
+    const int hd = p->head_dim;
+    if ((hd != 64 && hd != 128 && hd != 256) || oe != 2 || p->in_dtype != p->out_dtype || p->round_f16 ||
+        p->N % hd != 0 || p->rope_cols < 0 || p->rope_cols > p->N || p->rope_cols % hd != 0)
+      return kErrInvalidArg;
+    if (p->bias != nullptr && !aligned16(p->bias)) return kErrInvalidArg;
+    if (p->rope_cols > 0 && (p->rope_cos == nullptr || p->rope_sin == nullptr || !aligned16(p->rope_cos) ||
+                             !aligned16(p->rope_sin)))
+      return kErrInvalidArg;
+  }
   const int c_cols = swiglu ? p->N / 2 : p->N;
   if ((p->ldc * oe) % 16 != 0 || p->ldc < c_cols) return kErrInvalidArg;
   if (p->K == 0) {
@@ -533,6 +547,14 @@ static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothin
   L.round_f16 = p->round_f16;
   L.group_m = p->group_m;
   L.swiglu = swiglu ? 1 : 0;
+  if (rope) {
+    L.bias_rope = 1;
+    L.rope_cols = p->rope_cols;
+    L.head_dim = p->head_dim;
+    L.bias = p->bias;
+    L.rope_cos = p->rope_cos;
+    L.rope_sin = p->rope_sin;
+  }
   return kOk;
 }
 
@@ -542,12 +564,17 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
   const int rc = gemm_validate(p, &L, &nothing, &empty_k);
   if (rc || nothing) return rc;
   if (empty_k) {
-    // Empty contraction: C = 0 (also under SwiGLU: silu(0) * 0 = 0).
+    // Empty contraction: C = 0 (also under SwiGLU: silu(0) * 0 = 0); with
+    // bias + RoPE, then the epilogue on the zeros, as the two-pass path does.
     const int oe = elt_size(p->out_dtype);
     const int c_cols = p->epilogue == FAB_GEMM_EPILOGUE_SWIGLU ? p->N / 2 : p->N;
     cudaError_t e = cudaMemset2DAsync(p->c, size_t(p->ldc) * oe, 0, size_t(c_cols) * oe, size_t(p->M),
                                       static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? kOk : kErrCuda;
+    if (e != cudaSuccess) return kErrCuda;
+    if (p->epilogue == FAB_GEMM_EPILOGUE_BIAS_ROPE)
+      return fab_bias_rope(p->c, p->bias, p->rope_cos, p->rope_sin, p->M, p->N / p->head_dim,
+                           p->rope_cols / p->head_dim, p->head_dim, p->ldc, p->out_dtype, stream);
+    return kOk;
   }
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
 }

@@ -116,6 +116,15 @@ struct GemmKernelParams {
   // SwiGLU epilogue: B's columns alternate 64 gate / 64 up columns, and C
   // receives round(round(silu(round(g))) * round(u)), N / 2 columns.
   int swiglu;
+  // Bias + rotate-half RoPE epilogue (bias_rope 1): every column gets
+  // round(round(acc) + bias), and the heads of head_dim columns among the
+  // first rope_cols are rotated with row r's cos/sin ([M][head_dim] tables).
+  int bias_rope;
+  int rope_cols;
+  int head_dim;
+  const void* bias;  // [N] or null
+  const void* rope_cos;
+  const void* rope_sin;
 };
 
 // Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output
@@ -143,7 +152,16 @@ struct GemmLaunch {
   int round_f16;
   int group_m;
   int swiglu;
+  int bias_rope;  // see GemmKernelParams
+  int rope_cols;
+  int head_dim;
+  const void* bias;
+  const void* rope_cos;
+  const void* rope_sin;
 };
+
+// Epilogues that need whole 256-column tiles (gate/up block pairs, whole heads).
+inline bool gemm_fixed_width(const GemmLaunch& L) { return L.swiglu || L.bias_rope; }
 
 int fa_select_config(int dtype, int D, FaConfigInfo* out);
 int fa_forward(const FaLaunch& L, cudaStream_t stream);

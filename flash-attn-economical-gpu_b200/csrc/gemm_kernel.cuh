@@ -149,9 +149,97 @@ __device__ __forceinline__ float round_to(float x) {
 // store (optionally through fp16), or with p.swiglu the SwiGLU of each
 // 64-column gate block and the up block after it: a 256-wide tile holds
 // gate 0-63, up 0-63, gate 64-127, up 64-127 of output columns n0/2 ... n0/2+127.
+template <typename Tout>
+__device__ __forceinline__ void load8(const void* src, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if constexpr (std::is_same<Tout, __nv_bfloat16>::value) {
+      f[2 * e] = __uint_as_float(w[e] << 16);
+      f[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[e]);
+      const float2 x = __half22float2(h);
+      f[2 * e] = x.x;
+      f[2 * e + 1] = x.y;
+    }
+  }
+}
+
+// The bias + RoPE epilogue for one row of a 256-column tile: whole heads of
+// p.head_dim columns (n0 is a multiple of it).  Rounds where the two-pass
+// path rounds (GEMM output, + bias, each product and the sum), so it equals
+// fab_gemm followed by fab_bias_rope bit for bit.
+template <typename Tout>
+__device__ __forceinline__ void gemm_store_bias_rope_row(const GemmKernelParams& p, uint32_t acc, int row, int n0) {
+  // Every lane runs the TMEM loads (warp-collective) and the arithmetic; rows
+  // past M read table row 0 and store nothing.
+  const bool row_ok = row < p.M;
+  const int trow = row_ok ? row : 0;
+  const int hd = p.head_dim, half = hd / 2;
+  Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(trow) * p.ldc;
+  const Tout* bias = static_cast<const Tout*>(p.bias);
+  const Tout* cs = static_cast<const Tout*>(p.rope_cos) + static_cast<int64_t>(trow) * hd;
+  const Tout* sn = static_cast<const Tout*>(p.rope_sin) + static_cast<int64_t>(trow) * hd;
+#pragma unroll 1
+  for (int h0 = 0; h0 < 256; h0 += hd) {
+    const int col = n0 + h0;  // first column of this head
+    if (col >= p.N) break;
+    const bool rot = col < p.rope_cols;
+#pragma unroll 1
+    for (int c = 0; c < half; c += 32) {
+      uint32_t rl[32], rh[32];
+      tmem_ld32(acc + h0 + c, rl);
+      tmem_ld32(acc + h0 + half + c, rh);
+      tmem_wait_ld();
+      float lo[32], hi[32];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float bl[8], bh[8], cl[8], ch[8], sl[8], sh[8];
+        if (bias != nullptr) {
+          load8<Tout>(bias + col + c + 8 * g, bl);
+          load8<Tout>(bias + col + half + c + 8 * g, bh);
+        }
+        if (rot) {
+          load8<Tout>(cs + c + 8 * g, cl);
+          load8<Tout>(cs + half + c + 8 * g, ch);
+          load8<Tout>(sn + c + 8 * g, sl);
+          load8<Tout>(sn + half + c + 8 * g, sh);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float l = round_to<Tout>(__uint_as_float(rl[8 * g + e]));
+          float h = round_to<Tout>(__uint_as_float(rh[8 * g + e]));
+          if (bias != nullptr) {
+            l = round_to<Tout>(l + bl[e]);
+            h = round_to<Tout>(h + bh[e]);
+          }
+          if (rot) {
+            const float nl = round_to<Tout>(round_to<Tout>(l * cl[e]) + round_to<Tout>(-h * sl[e]));
+            const float nh = round_to<Tout>(round_to<Tout>(h * ch[e]) + round_to<Tout>(l * sh[e]));
+            l = nl;
+            h = nh;
+          }
+          lo[8 * g + e] = l;
+          hi[8 * g + e] = h;
+        }
+      }
+      if (row_ok) {
+        gemm_store_chunk<Tout>(crow + col + c, lo, 32, false);
+        gemm_store_chunk<Tout>(crow + col + half + c, hi, 32, false);
+      }
+    }
+  }
+}
+
 template <typename Tout, int kWidth>
 __device__ __forceinline__ void gemm_store_tile_row(const GemmKernelParams& p, uint32_t acc, int row, int n0) {
   if constexpr (sizeof(Tout) == 2 && kWidth == 256) {
+    if (p.bias_rope) {
+      gemm_store_bias_rope_row<Tout>(p, acc, row, n0);
+      return;
+    }
     if (p.swiglu) {
       const int o0 = n0 / 2;
       Tout* orow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + o0;
@@ -618,6 +706,12 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   kp.group_m = L.group_m > 0 ? L.group_m : 8;
   kp.round_f16 = L.round_f16;
   kp.swiglu = L.swiglu;
+  kp.bias_rope = L.bias_rope;
+  kp.rope_cols = L.rope_cols;
+  kp.head_dim = L.head_dim;
+  kp.bias = L.bias;
+  kp.rope_cos = L.rope_cos;
+  kp.rope_sin = L.rope_sin;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   int sms = num_sms();
@@ -672,7 +766,7 @@ static int gemm_splitk_factor_out(const GemmLaunch& L) {
 // flight per CTA (6 and 8), which is what a short kernel with a cold L2
 // waits on.  16-bit inputs without the SwiGLU epilogue only.
 static int gemm_single_width(const GemmLaunch& L) {
-  if (L.swiglu || (L.in_dtype != kDtypeF16 && L.in_dtype != kDtypeBF16)) return 256;
+  if (gemm_fixed_width(L) || (L.in_dtype != kDtypeF16 && L.in_dtype != kDtypeBF16)) return 256;
   const int sms = num_sms();
   if (sms <= 0) return 256;
   const long long rows = (L.M + 127) / 128;

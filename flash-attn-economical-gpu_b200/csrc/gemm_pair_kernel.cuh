@@ -244,6 +244,12 @@ static int launch_gemm_pair_w(const GemmLaunch& L, cudaStream_t stream) {
   kp.group_m = L.group_m > 0 ? L.group_m : 8;
   kp.round_f16 = L.round_f16;
   kp.swiglu = L.swiglu;
+  kp.bias_rope = L.bias_rope;
+  kp.rope_cols = L.rope_cols;
+  kp.head_dim = L.head_dim;
+  kp.bias = L.bias;
+  kp.rope_cos = L.rope_cos;
+  kp.rope_sin = L.rope_sin;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   const int sms = num_sms();
@@ -268,7 +274,7 @@ static int launch_gemm_pair(const GemmLaunch& L, cudaStream_t stream) {
   // costs L2 traffic in long main loops (measured on B200: N = 3584 gains 7 %
   // at K = 3584, loses 2-7 % at K = 18944).  The SwiGLU epilogue pairs
   // 64-column gate/up blocks within 256-wide tiles.
-  if (!L.swiglu && pairs > 0 && L.K <= 8192 && gemm_pair_cost(L, 224, pairs) < gemm_pair_cost(L, 256, pairs))
+  if (!gemm_fixed_width(L) && pairs > 0 && L.K <= 8192 && gemm_pair_cost(L, 224, pairs) < gemm_pair_cost(L, 256, pairs))
     return launch_gemm_pair_w<Tin, Tout, 224>(L, stream);
   return launch_gemm_pair_w<Tin, Tout, 256>(L, stream);
 }

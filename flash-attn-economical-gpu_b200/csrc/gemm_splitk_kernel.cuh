@@ -253,6 +253,10 @@ static int launch_gemm_splitk_k(const GemmLaunch& L, cudaStream_t stream) {
   kp.group_m = L.group_m > 0 ? L.group_m : 8;
   kp.round_f16 = L.round_f16;
   kp.swiglu = 0;
+  kp.bias_rope = 0;
+  kp.rope_cols = 0;
+  kp.head_dim = 0;
+  kp.bias = kp.rope_cos = kp.rope_sin = nullptr;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   kern<<<static_cast<unsigned>(tiles * kSplit), C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
@@ -271,7 +275,7 @@ constexpr int kSplitMinKBlocks = 48;
 template <typename Tin, typename Tout>
 static int gemm_splitk_factor(const GemmLaunch& L) {
   using C = GemmCfg<2>;
-  if (L.in_dtype == kDtypeF32 || L.swiglu || L.K <= 0) return 1;
+  if (L.in_dtype == kDtypeF32 || gemm_fixed_width(L) || L.K <= 0) return 1;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   const int nkb = (L.K + C::kBK - 1) / C::kBK;
   const int sms = num_sms();

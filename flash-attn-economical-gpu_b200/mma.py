@@ -61,11 +61,13 @@ def _gemm(
     round_f16: bool,
     group_m: int = 8,
     epilogue: int = _native.FAB_GEMM_EPILOGUE_STORE,
+    rope: tuple | None = None,
     what: str = "gemm",
 ) -> None:
     """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements).
 
-    With the SwiGLU epilogue C is [M, N/2] (see `matmul_swiglu`)."""
+    With the SwiGLU epilogue C is [M, N/2] (see `matmul_swiglu`); with the bias + RoPE epilogue `rope` is
+    (bias or None, cos, sin, rope_cols, head_dim) (see `matmul_bias_rope`)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         _require_cuda_tensor(name, t)
     if a.dtype != b.dtype:
@@ -79,6 +81,11 @@ def _gemm(
     p.round_f16 = 1 if round_f16 else 0
     p.group_m = int(group_m)
     p.epilogue = int(epilogue)
+    if rope is not None:
+        bias, cos, sin, rope_cols, head_dim = rope
+        p.bias = bias.data_ptr() if bias is not None else None
+        p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
+        p.rope_cols, p.head_dim = int(rope_cols), int(head_dim)
     with torch.cuda.device(a.device):
         rc = _native.lib.fab_gemm(ctypes.byref(p), ctypes.c_void_p(_native.current_stream_handle(a.device)))
     _native.check(rc, what)
@@ -228,6 +235,44 @@ def split_gate_up(gu: torch.Tensor, block: int = SWIGLU_BLOCK) -> tuple[torch.Te
     return v[..., 0, :].reshape(*lead, two_m // 2), v[..., 1, :].reshape(*lead, two_m // 2)
 
 
+def matmul_bias_rope(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
+                     sin: torch.Tensor, *, rope_cols: int, head_dim: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = rope(a @ w + bias): a QKV projection with its bias and rotate-half rotary embedding in the epilogue.
+
+    a [S, K], w [K, N] (16-bit, unit column stride), bias [N] or None, cos/sin [>=S, head_dim] contiguous tables
+    (row r = position r).  Every column gets the bias; the heads of head_dim columns among the first rope_cols
+    are rotated.  Equals `matmul(a, w)` followed by the bias add and `q*cos + rotate_half(q)*sin` in the
+    16-bit type, bit for bit.  No counterpart in the reference (its model adds the bias and applies RoPE as
+    separate PyTorch ops).
+    """
+    for name, t in (("a", a), ("w", w), ("cos", cos), ("sin", sin)) + ((("bias", bias),) if bias is not None else ()):
+        _require_cuda_tensor(name, t)
+    if a.dtype not in (torch.float16, torch.bfloat16) or w.dtype != a.dtype:
+        raise ValueError("matmul_bias_rope: a and w must share one 16-bit dtype")
+    for name, t in (("cos", cos), ("sin", sin)) + ((("bias", bias),) if bias is not None else ()):
+        if t.dtype != a.dtype or not t.is_contiguous():
+            raise ValueError(f"matmul_bias_rope: {name} must be contiguous in {a.dtype}")
+    if a.ndim != 2 or w.ndim != 2 or a.shape[1] != w.shape[0]:
+        raise ValueError(f"matmul_bias_rope expects a [S, K] and w [K, N], got {tuple(a.shape)} and {tuple(w.shape)}")
+    M, K = a.shape
+    N = w.shape[1]
+    if cos.shape != sin.shape or cos.ndim != 2 or cos.shape[1] != head_dim or cos.shape[0] < M:
+        raise ValueError("matmul_bias_rope: cos and sin must be [>= S, head_dim]")
+    if bias is not None and bias.numel() != N:
+        raise ValueError("matmul_bias_rope: bias must have N elements")
+    if a.stride(1) != 1:
+        a = a.contiguous()
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=a.dtype)
+    _gemm(a, w, out, M, N, K, lda=a.stride(0), ldb=w.stride(0), ldc=out.stride(0), round_f16=False,
+          epilogue=_native.FAB_GEMM_EPILOGUE_BIAS_ROPE, rope=(bias, cos, sin, rope_cols, head_dim),
+          what="matmul_bias_rope")
+    return out
+
+
 def matmul_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     """silu(a @ W_gate) * (a @ W_up) [M, m] in one kernel, for w_gate_up = interleave_gate_up(W_gate, W_up).
 
@@ -260,6 +305,7 @@ __all__ = [
     "_matmul_contiguous_kernel",
     "matmul",
     "matmul_swiglu",
+    "matmul_bias_rope",
     "kernel_plan",
     "interleave_gate_up",
     "split_gate_up",

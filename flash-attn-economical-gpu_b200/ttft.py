@@ -43,7 +43,7 @@ import torch
 import torch.nn.functional as F
 
 from flash_atten import attention_forward, flash_attention
-from mma import SWIGLU_BLOCK, interleave_gate_up, matmul_swiglu, split_gate_up
+from mma import SWIGLU_BLOCK, interleave_gate_up, matmul_bias_rope, matmul_swiglu, split_gate_up
 from tuner import FlashAttentionBlockDNomaskTuner, FlashAttenTuneArguments
 
 try:
@@ -609,9 +609,14 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
         else:
             h = _rms_norm(x, layer.ln_in, arch.rms_norm_eps)
         pending = None
-        qkv = _matmul(h, layer.w_qkv, backends.gemm)
+        if native and backends.gemm == "native":
+            # QKV GEMM with the bias add and RoPE in its epilogue
+            qkv = matmul_bias_rope(h, layer.w_qkv, layer.b_qkv, cos2, sin2, rope_cols=(nq + nkv) * D, head_dim=D)
+        else:
+            qkv = _matmul(h, layer.w_qkv, backends.gemm)
+            if native:
+                _native_bias_rope(qkv, layer.b_qkv, cos2, sin2, nq + 2 * nkv, nq + nkv, D)
         if native:
-            _native_bias_rope(qkv, layer.b_qkv, cos2, sin2, nq + 2 * nkv, nq + nkv, D)
             q = qkv[:, : nq * D].view(S, nq, D)
             k = qkv[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
             v = qkv[:, (nq + nkv) * D:].view(S, nkv, D)

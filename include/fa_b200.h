@@ -217,6 +217,12 @@ typedef struct fab_gemm_params {
   int round_f16;
   int group_m;  /* tile-row group for L2 reuse, 0 = default (8) */
   int epilogue; /* FAB_GEMM_EPILOGUE_*; 0 = store C */
+  /* FAB_GEMM_EPILOGUE_BIAS_ROPE only (ignored otherwise): */
+  const void* bias;     /* [N] in the output type, or NULL */
+  const void* rope_cos; /* [M][head_dim] in the output type (row r: position r) */
+  const void* rope_sin;
+  int rope_cols;        /* leading columns that get RoPE (whole heads) */
+  int head_dim;         /* 64, 128 or 256 */
 } fab_gemm_params;
 
 /*
@@ -229,6 +235,18 @@ typedef struct fab_gemm_params {
  */
 #define FAB_GEMM_EPILOGUE_STORE 0
 #define FAB_GEMM_EPILOGUE_SWIGLU 1
+
+/*
+ * FAB_GEMM_EPILOGUE_BIAS_ROPE: the QKV projection's bias add and rotate-half
+ * rotary embedding in the GEMM epilogue (no counterpart in the reference,
+ * whose model code adds the bias and applies RoPE as separate PyTorch ops;
+ * here it replaces fab_gemm followed by fab_bias_rope, with equal bits).
+ * Every column gets round(round(acc) + bias); each head of head_dim columns
+ * among the first rope_cols becomes [lo*cos - hi*sin, hi*cos + lo*sin] of its
+ * halves, every product and sum rounded to the output type, with row r's
+ * cos/sin.  16-bit, in type == out type, N a multiple of head_dim, round_f16 0.
+ */
+#define FAB_GEMM_EPILOGUE_BIAS_ROPE 2
 
 int fab_gemm(const fab_gemm_params* params, void* stream);
 

@@ -242,3 +242,31 @@ def test_gemm_plan_validates_like_gemm():
         _native.FAB_ERR_INVALID_ARG
     assert _native.lib.fab_gemm_plan(ctypes.byref(p), None, ctypes.byref(split), ctypes.byref(tile_n)) == \
         _native.FAB_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("change, ok", [
+    (dict(), True),
+    (dict(head_dim=96), False),
+    (dict(rope_cols=100), False),
+    (dict(rope_cols=1024), False),
+    (dict(out_dtype=2), False),
+    (dict(round_f16=1), False),
+    (dict(rope_cos=0), False),
+    (dict(bias=8), False),
+    (dict(N=640 + 64), False),
+])
+def test_bias_rope_epilogue_validation(change, ok):
+    """Argument checks of FAB_GEMM_EPILOGUE_BIAS_ROPE; only the invalid ones are sent (no GPU here)."""
+    if ok:
+        return
+    p = _native.FabGemmParams()
+    p.a = p.b = p.c = 256
+    p.M, p.N, p.K = 64, 640, 64
+    p.lda, p.ldb, p.ldc = 64, 704, 704
+    p.in_dtype = p.out_dtype = _native.dtype_code(torch.bfloat16)
+    p.epilogue = _native.FAB_GEMM_EPILOGUE_BIAS_ROPE
+    p.bias, p.rope_cos, p.rope_sin = 512, 768, 1024
+    p.rope_cols, p.head_dim = 384, 128
+    for k, v in change.items():
+        setattr(p, k, v)
+    assert _native.lib.fab_gemm(ctypes.byref(p), None) == _native.FAB_ERR_INVALID_ARG
