@@ -102,7 +102,7 @@ def main() -> None:
                           seed=seed, blocks=list(blocks)))
 
     f16, f32 = torch.float16, torch.float32
-    # BASELINE config 1 exactly: B1 H4 S256 D64 fp32, seed 0, scale 1/8, non-causal.
+    # the fp32 benchmark case exactly: B1 H4 S256 D64 fp32, seed 0, scale 1/8, non-causal.
     strided_case("cfg1_fp32", "_flash_attn_fwd_kernel_basic", 1, 4, 256, 256, 64, False, True, f32, (64, 64, 64), 0, 0.125)
     strided_case("basic_ragged_causal", "_flash_attn_fwd_kernel_basic", 1, 2, 40, 37, 64, True, True, f16, (16, 16, 64), 1)
     strided_case("basic_d128", "_flash_attn_fwd_kernel_basic", 2, 1, 70, 130, 128, False, True, f16, (32, 32, 128), 2)

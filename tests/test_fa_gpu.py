@@ -1,6 +1,6 @@
 """Attention forward on the GPU, through the C ABI, against the reference and the oracle.
 
-Tolerance: fp16/bf16 outputs within max-abs 2e-2 and
+Tolerance (the acceptance bar for 16-bit outputs): fp16/bf16 outputs within max-abs 2e-2 and
 rtol 1e-2 of an fp32 reference on the same inputs; the LSE is compared in
 fp32 (atol 2e-3).  fp32 inputs run on the tensor cores as tf32, like the
 reference's Triton `tl.dot` default, under the same tolerance.
@@ -95,7 +95,7 @@ def test_reference_golden_through_dropin(case, cuda_device):
 
 
 def test_config1_exact_baseline_case(cuda_device):
-    """B1 H4 S256 D64 fp32 N(0,1) from seed 0, scale 1/8, vs torch SDPA math on CPU."""
+    """The fp32 benchmark case: B1 H4 S256 D64 fp32 N(0,1) from seed 0, scale 1/8, vs torch SDPA math on CPU."""
     g = torch.Generator().manual_seed(0)
     q, k, v = (torch.randn(1, 4, 256, 64, generator=g) for _ in range(3))
     ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=0.125)
@@ -144,7 +144,7 @@ def test_oracle_parity_fp32_tf32(shape, causal, cuda_device):
 
 @pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
 def test_grouped_query_heads(causal, cuda_device):
-    """BASELINE config 3 GQA shape (16 query heads over 4 KV heads, D=128), shortened sequence."""
+    """The GQA benchmark shape (16 query heads over 4 KV heads, D=128), shortened sequence."""
     shape = (2, 16, 4, 640, 640, 128)
     q, k, v, qd, kd, vd = _inputs(shape, torch.bfloat16, seed=5, dev=cuda_device)
     o = attention_forward(qd, kd, vd, causal=causal)
@@ -270,7 +270,7 @@ def test_unsupported_head_dim_raises(cuda_device):
         attention_forward(x, x, x)
 
 
-# ------------------------------------------------------- full BASELINE sizes
+# ------------------------------------------------------ full benchmark sizes
 def _sampled_rows_check(q, k, v, o, causal, dtype, picks):
     """Oracle on selected (b, h, row-block) slices of a full-size problem."""
     for b, h, m0, m1 in picks:
@@ -286,7 +286,7 @@ def _sampled_rows_check(q, k, v, o, causal, dtype, picks):
 
 @pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
 def test_config2_full_size_sampled(causal, cuda_device):
-    """BASELINE config 2 at S=8192: B4 H32 D128 bf16; rows sampled across heads and positions."""
+    """The headline benchmark shape at S=8192: B4 H32 D128 bf16; rows sampled across heads and positions."""
     B, H, S, D = 4, 32, 8192, 128
     g = torch.Generator(device=cuda_device).manual_seed(21)
     q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
@@ -297,7 +297,7 @@ def test_config2_full_size_sampled(causal, cuda_device):
 
 
 def test_config3_d256_full_size_sampled(cuda_device):
-    """D=256, B2 H16 S8192 bf16, causal, scale 1/16."""
+    """The D=256 benchmark shape: B2 H16 S8192 bf16, causal, scale 1/16."""
     B, H, S, D = 2, 16, 8192, 256
     g = torch.Generator(device=cuda_device).manual_seed(22)
     q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
@@ -307,7 +307,7 @@ def test_config3_d256_full_size_sampled(cuda_device):
 
 
 def test_config3_gqa_full_size_sampled(cuda_device):
-    """BASELINE config 3 GQA: 16 query heads over 4 KV heads, D=128, S=8192, causal."""
+    """The GQA benchmark shape: 16 query heads over 4 KV heads, D=128, S=8192, causal."""
     B, Hq, Hkv, S, D = 2, 16, 4, 8192, 128
     g = torch.Generator(device=cuda_device).manual_seed(23)
     q = torch.randn(B, Hq, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16)

@@ -1,6 +1,6 @@
 """Matmul on the GPU, through the C ABI, against the reference's outputs and the oracle.
 
-Tolerance: within max-abs 2e-2 and rtol 1e-2 of the
+Tolerance (the acceptance bar for 16-bit outputs): within max-abs 2e-2 and rtol 1e-2 of the
 fp32 oracle on the same inputs (inputs ~ N(0,1)/sqrt(K) keep |C| ~ 1).
 """
 from __future__ import annotations
@@ -126,7 +126,7 @@ def test_deterministic(cuda_device):
 @pytest.mark.parametrize("n", [4096, 8192, 16384])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 def test_config4_full_size(n, dtype, cuda_device):
-    """BASELINE config 4 sizes: sampled rows against the oracle plus a column-sum identity over all of C."""
+    """Benchmark matmul sizes: sampled rows against the oracle plus a column-sum identity over all of C."""
     g = torch.Generator(device=cuda_device).manual_seed(n)
     a = (torch.randn(n, n, generator=g, device=cuda_device) / n ** 0.5).to(dtype)
     b = (torch.randn(n, n, generator=g, device=cuda_device) / n ** 0.5).to(dtype)

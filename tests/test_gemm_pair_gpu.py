@@ -2,7 +2,7 @@
 
 16-bit inputs take this kernel when the problem has at least one wave of pair tiles (one per two SMs);
 every shape here does (asserted).  Tiles are 256 columns wide, or 224 where that leaves fewer pairs idle in
-the last wave and K <= 8192; the shapes below exercise both.  Tolerance: max-abs 2e-2 and rtol 1e-2 of the fp32
+the last wave and K <= 8192; the shapes below exercise both.  Tolerance (the acceptance bar for 16-bit outputs): max-abs 2e-2 and rtol 1e-2 of the fp32
 oracle on inputs ~ N(0,1)/sqrt(K).  Rows are sampled for the oracle (first, last, ragged edge, a few in
 between); a column-sum identity checks every row.
 """

@@ -3,7 +3,7 @@ memory) against the oracle.
 
 16-bit inputs take this kernel when the output has at most a quarter as many 128x256 tiles as there are SMs and K
 has at least 48 64-deep blocks; `mma.kernel_plan` reports the choice and every shape here asserts it.  Tolerance
-max-abs 2e-2 and rtol 1e-2 of the fp32 oracle on inputs ~ N(0,1)/sqrt(K).
+(the acceptance bar for 16-bit outputs): max-abs 2e-2 and rtol 1e-2 of the fp32 oracle on inputs ~ N(0,1)/sqrt(K).
 """
 from __future__ import annotations
 

@@ -33,7 +33,7 @@ MMA = [c for c in CASES if c["kind"] == "matmul"]
 
 def test_golden_inventory():
     names = {c["name"] for c in CASES}
-    assert "cfg1_fp32" in names  # BASELINE config 1 exactly
+    assert "cfg1_fp32" in names  # the fp32 benchmark case exactly (B1 H4 S256 D64)
     assert any(c["causal"] for c in ATT) and any(c["Hkv"] < c["Hq"] for c in ATT)
     assert {c["kernel"] for c in ATT} == {
         "_flash_attn_fwd_kernel_basic",
