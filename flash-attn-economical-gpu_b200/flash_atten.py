@@ -477,6 +477,21 @@ def attention_forward_varlen(
     return (o, lse) if return_lse else o
 
 
+def _host_pieces(batch: int, kv_heads: int, chunks: int) -> list[tuple[int, int, int]]:
+    """How attention_forward_host cuts a call: (batch entry, first kv head, end kv head) per piece.
+
+    Every batch entry is split into the same number of runs of whole key/value-head groups (as many as make about
+    `chunks` pieces in all, at most one per head), in order; together the pieces cover each unit exactly once."""
+    per_b = max(1, min(kv_heads, -(-max(1, chunks) // batch)))
+    pieces = []
+    for b in range(batch):
+        for i in range(per_b):
+            h0, h1 = kv_heads * i // per_b, kv_heads * (i + 1) // per_b
+            if h1 > h0:
+                pieces.append((b, h0, h1))
+    return pieces
+
+
 def attention_forward_host(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -516,14 +531,7 @@ def attention_forward_host(
         return out
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     g = Hq // Hkv
-    # Pieces: per batch entry, runs of whole key/value-head groups.
-    per_b = max(1, min(Hkv, -(-max(1, chunks) // B)))
-    pieces = []
-    for b in range(B):
-        for i in range(per_b):
-            h0, h1 = Hkv * i // per_b, Hkv * (i + 1) // per_b
-            if h1 > h0:
-                pieces.append((b, h0, h1))
+    pieces = _host_pieces(B, Hkv, chunks)
     widest = max(h1 - h0 for _, h0, h1 in pieces)
     with torch.cuda.device(dev):
         compute = torch.cuda.current_stream(dev)

@@ -273,3 +273,11 @@ def test_host_entry_validation():
     # nothing to compute: returns without touching a device
     e = torch.zeros(0, 2, 16, 64, dtype=torch.bfloat16)
     assert flash_atten.attention_forward_host(e, e, e).shape == e.shape
+
+
+@pytest.mark.parametrize("batch, kv_heads, chunks", [(4, 32, 16), (1, 4, 16), (3, 5, 7), (2, 1, 64), (5, 8, 1)])
+def test_host_entry_pieces_cover_every_unit_once(batch, kv_heads, chunks):
+    pieces = flash_atten._host_pieces(batch, kv_heads, chunks)
+    seen = [(b, h) for b, h0, h1 in pieces for h in range(h0, h1)]
+    assert sorted(seen) == [(b, h) for b in range(batch) for h in range(kv_heads)]
+    assert len(pieces) <= batch * -(-chunks // batch) and all(h1 > h0 for _, h0, h1 in pieces)
