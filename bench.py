@@ -72,6 +72,24 @@ DECODE_WORKLOADS = {
 }
 
 
+def attention_config(workload, world):
+    """The `config` object of an attention workload, the same on both arms."""
+    B, Hq, Hkv, S, D, causal = WORKLOADS[workload]
+    q_mb = 3 * B * Hq * S * D * 2 / 1e6
+    return {
+        "workload": f"attention forward B{B} Hq{Hq} Hkv{Hkv} S{S} D{D} bf16 {'causal' if causal else 'non-causal'}"
+                    " per GPU (BASELINE config 2/3)",
+        "global_batch": B * world,
+        "seq_len": S,
+        "heads_q": Hq,
+        "heads_kv": Hkv,
+        "head_dim": D,
+        "causal": causal,
+        "parallelism": f"dp{world} (each rank owns {B} sequences x {Hq} heads; no collective)",
+        "l2_policy": f"inputs {q_mb:.0f} MB per step > 126 MB L2; no flush",
+    }
+
+
 def attention_flops(B, H, S, D, causal):
     score = S * (S + 1) / 2 if causal else S * S
     return 4.0 * B * H * D * score
@@ -410,18 +428,7 @@ def run_attention(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) q/k/v per rank (no dataset in the reference for this path)",
-        "config": {
-            "workload": f"attention forward B{B} Hq{Hq} Hkv{Hkv} S{S} D{D} bf16 {'causal' if causal else 'non-causal'}"
-                        " per GPU (BASELINE config 2/3)",
-            "global_batch": B * world,
-            "seq_len": S,
-            "heads_q": Hq,
-            "heads_kv": Hkv,
-            "head_dim": D,
-            "causal": causal,
-            "parallelism": f"dp{world} (each rank owns {B} sequences x {Hq} heads; no collective)",
-            "l2_policy": f"inputs {3 * q.numel() * 2 / 1e6:.0f} MB per step > 126 MB L2; no flush",
-        },
+        "config": attention_config(args.workload, world),
         "e2e": {
             "value": round(e2e_value, 1),
             "unit": "TFLOP/s",
@@ -758,9 +765,7 @@ def run_reference(args, world, rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded N(0,1)",
-        "config": {"workload": f"attention forward B{B} Hq{Hq} S{S} D{D} {'causal' if causal else 'non-causal'}"
-                               " (bounded CPU sample per step)",
-                   "parallelism": "rank 0 host cores"},
+        "config": attention_config(args.workload if args.workload in WORKLOADS else "fa_s8192_noncausal", world),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
