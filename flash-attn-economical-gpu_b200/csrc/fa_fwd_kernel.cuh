@@ -77,7 +77,7 @@ struct FaCfg {
   static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                     : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kNumBars = 1 + 2 * kRing + 2 * kSlots + kNQ + 1;
+  static constexpr int kNumBars = kNQ + 2 * kRing + 2 * kSlots + kNQ + 1;
   static constexpr int kDataBytes = kNQ * kQTileBytes + kRing * kKVTileBytes;
   // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
   // ring tiles 2j+1 .. 2j+4 are resident together.
@@ -192,8 +192,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + kNQ * C::kQTileBytes;  // [kRing] K or V tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kRing * C::kKVTileBytes);
-  uint64_t* bar_q_full = bars;
-  uint64_t* bar_kv_full = bars + 1;               // [kRing]
+  uint64_t* bar_q_full = bars;                    // [kNQ], one per Q tile
+  uint64_t* bar_kv_full = bars + kNQ;             // [kRing]
   uint64_t* bar_kv_empty = bar_kv_full + kRing;   // [kRing]
   uint64_t* bar_s_full = bar_kv_empty + kRing;    // [kSlots]
   uint64_t* bar_p_full = bar_s_full + C::kSlots; // [kSlots]
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
   const int nt = n_end > n_begin ? (n_end - n_begin + kBN - 1) / kBN : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_q_full, 1);
+    for (int i = 0; i < kNQ; ++i) mbar_init(bar_q_full + i, 1);
     for (int s = 0; s < kRing; ++s) {
       mbar_init(bar_kv_full + s, 1);
       mbar_init(bar_kv_empty + s, 1);
@@ -285,11 +285,17 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
-    mbar_arrive_expect_tx(bar_q_full, kNQ * C::kQTileBytes);
-    for (int i = 0; i < kNQ; ++i)
+    auto load_q = [&](int i) {
+      mbar_arrive_expect_tx(bar_q_full + i, C::kQTileBytes);
       for (int a = 0; a < C::kNumAtoms; ++a)
-        tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full, a * C::kAtom,
+        tma_load_4d(sQ + i * C::kQTileBytes + a * C::kQAtomBytes, &tm_q, bar_q_full + i, a * C::kAtom,
                     q_row0 + m0 + i * C::kBM, h, map_b);
+    };
+    // Q tile 0, then K_0 (all the first S product needs), then the other Q
+    // tiles; with no keys only Q tile 0 is loaded (the MMA thread waits for
+    // nothing else).
+    load_q(0);
+    int q_loaded = 1;
     // Ring tile t: K_{t/2} for even t, V_{t/2} for odd t, in slot t % kRing.
     // With one S buffer the MMA thread frees V_j and K_{j+1} with one commit
     // (release group j+1; group 0 is K_0), on barrier group % kRing; with two,
@@ -340,11 +346,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
         tma_load_4d(sKV + s * C::kKVTileBytes + a * C::kKVAtomBytes, map, bar_kv_full + s, a * C::kAtom, row, hk,
                     map_b);
       issued = t + 1;
+      if (t == 0)
+        for (; q_loaded < kNQ; ++q_loaded) load_q(q_loaded);
     }
     // Never leave this CTA with bulk copies still landing in its smem: wait
     // (bounded) for the last load issued into every slot.
     volatile int no_abort = 0;
-    mbar_wait(bar_q_full, 0, &no_abort, kDevTimeoutTeardown);
+    for (int i = 0; i < q_loaded; ++i) mbar_wait(bar_q_full + i, 0, &no_abort, kDevTimeoutTeardown);
     for (int x = max(0, issued - kRing); x < issued; ++x)
       mbar_wait(bar_kv_full + (x % kRing), (x / kRing) & 1, &no_abort, kDevTimeoutTeardown);
   } else if (!skip && warp == 1 && lane == 0) {
@@ -403,18 +411,24 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
       }
     };
 
-    bool ok = mbar_wait(bar_q_full, 0, abort_flag, kDevTimeoutQ);
+    bool ok = mbar_wait(bar_q_full, 0, abort_flag, kDevTimeoutQ);  // Q tile 0
     bool any_issued = false;
-    // Prologue: S for the first kSB KV tiles of every Q tile.
+    // Prologue: S for the first kSB KV tiles of every Q tile.  Q tiles after
+    // the first land behind K_0, so tile 0's product starts without them.
     for (int j = 0; ok && j < min(kSB, nt); ++j) {
       if (!(ok = mbar_wait(bar_kv_full + kslot(j), kpar(j), abort_flag, kDevTimeoutKV))) break;
       tc_fence_after();
       for (int i = 0; i < kNQ; ++i) {
+        if (j == 0 && i > 0) {
+          if (!(ok = mbar_wait(bar_q_full + i, 0, abort_flag, kDevTimeoutQ))) break;
+          tc_fence_after();
+        }
         issue_qk(i, i * kSB + j, kslot(j));
+        any_issued = true;
         mma_commit(bar_s_full + i * kSB + j);
       }
+      if (!ok) break;
       mma_commit(bar_kv_empty + kslot(j));
-      any_issued = true;
     }
     for (int j = 0; ok && j < nt; ++j) {
       const int s = vslot(j);
