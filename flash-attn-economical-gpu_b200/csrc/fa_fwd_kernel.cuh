@@ -6,12 +6,14 @@
 // block_d_nomask_contiguous): online softmax over KV tiles in fp32, P rounded
 // to the input dtype before the P*V product, final O = acc / l.
 //
-// B200 structure (one CTA per SM, 128 + NQ*128 threads):
-//   warp 0      TMA producer: Q tiles once, then K and V tiles through one
-//               ring of kRing tile slots, in the order the MMA thread uses
-//               them (K_j, V_j alternating with one S buffer; K_0, K_1, then
-//               V_j, K_{j+2} with two), so every slot the Q tiles leave free
-//               in shared memory adds load lead time.
+// B200 structure (one CTA per SM, 128 + NQ*128 threads; the one-tile,
+// one-S-buffer family runs two CTAs per SM):
+//   warp 0      TMA producer: Q tile 0, K_0, the other Q tiles (each Q tile
+//               on its own barrier), then K and V tiles through one ring of
+//               kRing tile slots, in the order the MMA thread uses them (K_j,
+//               V_j alternating with one S buffer; K_0, K_1, then V_j,
+//               K_{j+2} with two), so every slot the Q tiles leave free in
+//               shared memory adds load lead time.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
 //   warps 4..   one 128-thread softmax group per 128-row Q tile; thread r of
 //               the group owns row r (TMEM lane r) for the whole kernel.
@@ -30,6 +32,8 @@
 // execute in issue order, so the write cannot overtake the read.  The running
 // max is only moved when it grows by more than 2^8, so O is rescaled rarely;
 // the final O / l is unaffected.
+// Epilogue: dense 16-bit O is staged in its Q tile's shared memory (idle by
+// then) and written by TMA tensor stores; other layouts are stored directly.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
