@@ -219,8 +219,11 @@ def host_lead(ms=3.0):
 
     The host then enqueues the timed steps while the GPU is still busy, so each event pair brackets device time
     only, not the host's launch latency (tens of microseconds per call through Python and ctypes, as long as a
-    whole 1024^3 matmul).  The sleep itself ends before the first timed event."""
-    torch.cuda._sleep(int(ms * 1e-3 * 1.965e9))
+    whole 1024^3 matmul).  The sleep itself ends before the first timed event.  Without torch's sleep kernel the
+    lead is skipped (the events then also include host launch latency)."""
+    sleep = getattr(torch.cuda, "_sleep", None)
+    if sleep is not None:
+        sleep(int(ms * 1e-3 * 1.965e9))
 
 
 def barrier(world):
