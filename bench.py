@@ -62,8 +62,44 @@ WORKLOADS = {
     "fa_d256_s2048_causal": (2, 16, 16, 2048, 256, True),
     "fa_d256_s8192_causal": (2, 16, 16, 8192, 256, True),
     "fa_gqa_s8192_causal": (2, 16, 4, 8192, 128, True),
+    # the reference's long-sequence pipeline cases (test_flash_atten.py:82-88), non-causal
+    "fa_b1h28_s16384_noncausal": (1, 28, 28, 16384, 128, False),
+    "fa_b1h28_s32768_noncausal": (1, 28, 28, 32768, 128, False),
+    "fa_b1h28_s65536_noncausal": (1, 28, 28, 65536, 128, False),
+    "fa_b1h16_d256_s16384_noncausal": (1, 16, 16, 16384, 256, False),
+    "fa_b1h16_d256_s32768_noncausal": (1, 16, 16, 32768, 256, False),
+    "fa_b1h16_d256_s65536_noncausal": (1, 16, 16, 65536, 256, False),
 }
+# Square matmuls of BASELINE config 4; any other shape as gemm_<M>x<K>x<N> (e.g. gemm_2048x3584x3584).
 GEMM_WORKLOADS = {"gemm_8192": 8192, "gemm_16384": 16384, "gemm_4096": 4096, "gemm_2048": 2048, "gemm_1024": 1024}
+
+
+def gemm_shape(workload: str):
+    """(M, K, N) of a matmul workload name, or None when it names none."""
+    if workload in GEMM_WORKLOADS:
+        n = GEMM_WORKLOADS[workload]
+        return n, n, n
+    if workload.startswith("gemm_"):
+        parts = workload[5:].split("x")
+        if len(parts) == 3 and all(x.isdigit() and int(x) > 0 for x in parts):
+            return tuple(int(x) for x in parts)
+    return None
+
+
+def input_sets(input_bytes: int) -> int:
+    """How many distinct input sets a timed run rotates through: enough that the inputs of one step were
+    last read at least 2 x L2 bytes of other inputs ago (the reference draws fresh inputs every
+    iteration, test_flash_atten.py:516-531); one set when a step's inputs alone are that large."""
+    return max(1, math.ceil(2 * L2_BYTES / max(input_bytes, 1)))
+
+
+def l2_policy(input_bytes: int) -> str:
+    sets = input_sets(input_bytes)
+    mb = input_bytes / 1e6
+    if sets == 1:
+        return f"inputs {mb:.0f} MB per step >= 2 x 126 MB L2; no flush"
+    return (f"inputs {mb:.0f} MB per step < 2 x 126 MB L2: {sets} seeded input sets in rotation "
+            f"({sets * mb:.0f} MB), so no step reads inputs left in L2 by the previous one")
 # Split-KV decode steps (not a BASELINE config; K/V cache resident on the device):
 # name: (B, Hq, Hkv, query rows, keys, D)
 DECODE_WORKLOADS = {
@@ -75,7 +111,7 @@ DECODE_WORKLOADS = {
 def attention_config(workload, world):
     """The `config` object of an attention workload, the same on both arms."""
     B, Hq, Hkv, S, D, causal = WORKLOADS[workload]
-    q_mb = 3 * B * Hq * S * D * 2 / 1e6
+    in_bytes = (B * Hq + 2 * B * Hkv) * S * D * 2
     return {
         "workload": f"attention forward B{B} Hq{Hq} Hkv{Hkv} S{S} D{D} bf16 {'causal' if causal else 'non-causal'}"
                     " per GPU (BASELINE config 2/3)",
@@ -86,7 +122,7 @@ def attention_config(workload, world):
         "head_dim": D,
         "causal": causal,
         "parallelism": f"dp{world} (each rank owns {B} sequences x {Hq} heads; no collective)",
-        "l2_policy": f"inputs {q_mb:.0f} MB per step > 126 MB L2; no flush",
+        "l2_policy": l2_policy(in_bytes),
     }
 
 
@@ -324,15 +360,20 @@ def run_attention(args, world, rank, local):
     dtype = torch.bfloat16
     # Each rank owns batch rows [rank*B, (rank+1)*B) of a global batch of B*world sequences.
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    q = torch.randn(B, Hq, S, D, generator=g, device=dev, dtype=dtype)
-    k = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
-    v = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
+    in_bytes = (B * Hq + 2 * B * Hkv) * S * D * 2
+    sets = []
+    for _ in range(input_sets(in_bytes)):
+        q = torch.randn(B, Hq, S, D, generator=g, device=dev, dtype=dtype)
+        k = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
+        v = torch.randn(B, Hkv, S, D, generator=g, device=dev, dtype=dtype)
+        sets.append((q, k, v))
+    q, k, v = sets[0]
     o = torch.empty_like(q)
     flops = attention_flops(B, Hq, S, D, causal)
     stream = torch.cuda.current_stream(dev)
 
-    for _ in range(args.warmup):
-        attention_forward(q, k, v, causal=causal, out=o)
+    for i in range(args.warmup):
+        attention_forward(*sets[i % len(sets)], causal=causal, out=o)
     torch.cuda.synchronize(dev)
     if _native.device_error():
         raise RuntimeError("device error during warm-up")
@@ -348,7 +389,7 @@ def run_attention(args, world, rank, local):
         t_begin.record(stream)
         for i in range(args.steps):
             starts[i].record(stream)
-            attention_forward(q, k, v, causal=causal, out=o)
+            attention_forward(*sets[(args.warmup + i) % len(sets)], causal=causal, out=o)
             ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize(dev)
@@ -397,17 +438,18 @@ def run_attention(args, world, rank, local):
         for name, be in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
             try:
                 rep = Hq // Hkv
-                kk = k if rep == 1 else k.repeat_interleave(rep, dim=1)
-                vv = v if rep == 1 else v.repeat_interleave(rep, dim=1)
+                csets = [(qq, kk if rep == 1 else kk.repeat_interleave(rep, dim=1),
+                          vv if rep == 1 else vv.repeat_interleave(rep, dim=1)) for qq, kk, vv in sets]
                 with sdpa_kernel([be]):
-                    for _ in range(3):
-                        F.scaled_dot_product_attention(q, kk, vv, is_causal=causal)
+                    for i in range(3):
+                        F.scaled_dot_product_attention(*csets[i % len(csets)], is_causal=causal)
                     torch.cuda.synchronize(dev)
                     c0 = torch.cuda.Event(enable_timing=True)
                     c1 = torch.cuda.Event(enable_timing=True)
+                    host_lead()
                     c0.record(stream)
-                    for _ in range(10):
-                        F.scaled_dot_product_attention(q, kk, vv, is_causal=causal)
+                    for i in range(10):
+                        F.scaled_dot_product_attention(*csets[(3 + i) % len(csets)], is_causal=causal)
                     c1.record(stream)
                     torch.cuda.synchronize(dev)
                 comparators[name + "_tflops"] = round(flops * 10 / (c0.elapsed_time(c1) / 1e3) / 1e12, 1)
@@ -649,19 +691,21 @@ def run_ttft(args, world, rank, local):
 # ------------------------------------------------------------------ gemm arm
 def run_gemm(args, world, rank, local):
     import _native
+    import mma
     from mma import matmul
 
-    n = GEMM_WORKLOADS[args.workload]
+    M, K, N = gemm_shape(args.workload)
     dev = torch.device("cuda", local)
     dtype = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(2000 + rank)
-    # Rank r owns output column block r of a (n) x (n * world) product; A is replicated.
-    a = (torch.randn(n, n, generator=g, device=dev) / n ** 0.5).to(dtype)
-    b = (torch.randn(n, n, generator=g, device=dev) / n ** 0.5).to(dtype)
-    flops = 2.0 * n ** 3
+    # Rank r owns output column block r of an M x (N * world) product; A is replicated.
+    a = (torch.randn(M, K, generator=g, device=dev) / K ** 0.5).to(dtype)
+    b = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).to(dtype)
+    flops = 2.0 * M * N * K
     stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if 3 * n * n * 2 < L2_BYTES * 2 else None
-    c = torch.empty(n, n, device=dev, dtype=dtype)
+    operand_bytes = (M * K + K * N + M * N) * 2
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if operand_bytes < L2_BYTES * 2 else None
+    c = torch.empty(M, N, device=dev, dtype=dtype)
 
     def timed_steps(fn, steps):
         """Device ms of `steps` calls, each after an L2 flush (small sizes), events around the call alone."""
@@ -716,11 +760,13 @@ def run_gemm(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1)/sqrt(K)",
-        "config": {"workload": f"matmul {n}x{n}x{n} bf16 per GPU (BASELINE config 4)",
+        "config": {"workload": f"matmul {M}x{K}x{N} (M x K x N) bf16 per GPU"
+                               + (" (BASELINE config 4)" if M == K == N else ""),
                    "parallelism": f"dp{world} (output-column shards, A replicated; no collective)",
                    "l2_policy": "L2 flushed between steps" if flush is not None else "operands > L2"},
         "roofline": peaks_entry(achieved, args.workload),
         "gpu_launches": args.steps,
+        "kernel_plan": list(mma.kernel_plan(M, N, K, dtype, device=dev)),
         "clocks": clocks.summary(),
         "comparators": comparators,
     }
@@ -783,7 +829,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="fa_s8192_noncausal",
-                    choices=sorted(WORKLOADS) + sorted(GEMM_WORKLOADS) + sorted(DECODE_WORKLOADS))
+                    help="one of " + ", ".join(sorted(WORKLOADS) + sorted(GEMM_WORKLOADS) + sorted(DECODE_WORKLOADS))
+                         + ", or gemm_<M>x<K>x<N>")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch comparators")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of the CPU baseline sample")
@@ -793,6 +840,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.workload not in WORKLOADS and args.workload not in DECODE_WORKLOADS and gemm_shape(args.workload) is None:
+        ap.error(f"unknown workload {args.workload}")
     if args.impl == "reference":
         # CPU-only arm: no process group; ranks other than 0 exit without work.
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -802,7 +851,7 @@ def main():
         return
     world, rank, local = setup_dist(args)
     try:
-        if args.workload in GEMM_WORKLOADS:
+        if gemm_shape(args.workload) is not None:
             result = run_gemm(args, world, rank, local)
         elif args.workload in DECODE_WORKLOADS:
             result = run_decode(args, world, rank, local)

@@ -107,6 +107,10 @@ class FabFaConfig(ctypes.Structure):
     ]
 
 
+class FabFaPlan(ctypes.Structure):
+    _fields_ = [("config", FabFaConfig), ("ctas", ctypes.c_longlong), ("ctas_per_sm", _i32)]
+
+
 class FabKernelAttrs(ctypes.Structure):
     _fields_ = [("registers_per_thread", _i32), ("shared_bytes", _i32), ("threads", _i32)]
 
@@ -129,6 +133,9 @@ PROTOTYPES = {
     "fab_attention_fwd_varlen": (_i32, [ctypes.POINTER(FabAttentionVarlenParams), _vp]),
     "fab_attention_fwd_variant": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp]),
     "fab_flash_attn_config_variant": (_i32, [_i32, _i32, _i32, ctypes.POINTER(FabFaConfig)]),
+    "fab_attention_fwd_plan": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(FabFaPlan)]),
+    "fab_debug_set_wait_limit_ns": (_i32, [ctypes.c_ulonglong]),
+    "fab_debug_starve_kv_load": (_i32, [_i32]),
     "fab_attention_fwd_splitkv_workspace": (
         _i32, [ctypes.POINTER(FabAttentionParams), _i32, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(_i32)]),
     "fab_attention_fwd_splitkv": (_i32, [ctypes.POINTER(FabAttentionParams), _i32, _vp, ctypes.c_size_t, _vp]),
@@ -154,7 +161,7 @@ PROTOTYPES = {
     "fab_abi_version": (_i32, []),
 }
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 def _load() -> ctypes.CDLL:
@@ -239,6 +246,16 @@ def fa_config_variant(dtype: int, head_dim: int, variant: int) -> FabFaConfig | 
         return None
     check(rc, "fab_flash_attn_config_variant")
     return cfg
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Time limit of one bounded wait in the attention kernels of the current device (0: the 2 s default)."""
+    check(lib.fab_debug_set_wait_limit_ns(int(ns)), "fab_debug_set_wait_limit_ns")
+
+
+def starve_kv_load(ring_tile: int) -> None:
+    """Test hook: every attention CTA skips K/V ring load `ring_tile` (-1: none), so its wait runs out."""
+    check(lib.fab_debug_starve_kv_load(int(ring_tile)), "fab_debug_starve_kv_load")
 
 
 def kernel_attrs(which: int, dtype: int, head_dim: int = 0) -> FabKernelAttrs:

@@ -237,14 +237,22 @@ static __device__ __align__(256) unsigned char g_splitkv_static_scratch[kStaticS
 
 constexpr int kMaxScratchDevices = 64;
 
+// Device address of the scratch array on `device` (the current device).  Only
+// a successful lookup is cached, so a call after a failed one tries again; a
+// failed lookup's error is read off the runtime here, so it is not reported
+// later by an unrelated launch check.
 static void* static_scratch_address(int device) {
-  static std::once_flag once[kMaxScratchDevices];
+  static std::mutex mu;
   static void* addr[kMaxScratchDevices] = {};
   if (device < 0 || device >= kMaxScratchDevices) return nullptr;
-  std::call_once(once[device], [device] {
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_splitkv_static_scratch) == cudaSuccess) addr[device] = p;
-  });
+    if (cudaGetSymbolAddress(&p, g_splitkv_static_scratch) == cudaSuccess)
+      addr[device] = p;
+    else
+      cudaGetLastError();
+  }
   return addr[device];
 }
 
@@ -254,7 +262,7 @@ using namespace fab;
 
 extern "C" {
 
-int fab_abi_version(void) { return 7; }
+int fab_abi_version(void) { return 8; }
 
 const char* fab_error_string(int rc) {
   switch (rc) {
@@ -372,6 +380,36 @@ int fab_attention_fwd_variant(const fab_attention_params* p, int variant, void* 
   L.num_splits = 1;
   L.split_len = L.N > 0 ? L.N : 1;
   return fa_forward_one_tile(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_attention_fwd_plan(const fab_attention_params* p, int variant, fab_fa_plan* out) {
+  if (p == nullptr || out == nullptr) return kErrInvalidArg;
+  if (variant != FAB_FA_VARIANT_TWO_TILES && variant != FAB_FA_VARIANT_ONE_TILE) return kErrInvalidArg;
+  FaLaunch L = launch_from_params(p);
+  bool empty = false;
+  int rc = attention_validate(L, &empty);
+  if (rc) return rc;
+  *out = fab_fa_plan{};
+  if (empty) return kOk;  // nothing would launch
+  L.num_splits = 1;
+  FaPlanInfo plan;
+  rc = fa_plan(L, variant, &plan);
+  if (rc) return rc;
+  const FaConfigInfo& c = plan.cfg;
+  out->config = fab_fa_config{c.d_pad, c.nq, c.bn, c.stages, c.threads, c.smem_bytes, c.tmem_cols, c.s_bufs};
+  out->ctas = plan.ctas;
+  out->ctas_per_sm = plan.ctas_per_sm;
+  return kOk;
+}
+
+int fab_debug_set_wait_limit_ns(unsigned long long ns) {
+  const uint64_t v = ns == 0 ? kWaitLimitNs : static_cast<uint64_t>(ns);
+  return cudaMemcpyToSymbol(g_fab_wait_limit_ns, &v, sizeof(v)) == cudaSuccess ? kOk : kErrCuda;
+}
+
+int fab_debug_starve_kv_load(int ring_tile) {
+  const int v = ring_tile < 0 ? -1 : ring_tile;
+  return cudaMemcpyToSymbol(g_fab_starve_kv_load, &v, sizeof(v)) == cudaSuccess ? kOk : kErrCuda;
 }
 
 int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_config* out) {

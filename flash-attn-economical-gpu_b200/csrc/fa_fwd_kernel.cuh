@@ -51,6 +51,11 @@
 
 namespace fab {
 
+// Test hook (fab_debug_starve_kv_load): the producer of every CTA skips the
+// K/V ring load with this index, so the wait for it runs out and the kernel
+// takes its give-up path.  -1, the default, skips nothing.
+static __device__ int g_fab_starve_kv_load = -1;
+
 template <int kElt, int kDP, int kNQ, int kBN, int kRing, int kSB>
 struct FaCfg {
   static constexpr int kBM = 128;                    // rows per Q tile (TMEM lanes)
@@ -300,6 +305,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
     // nothing else).
     load_q(0);
     int q_loaded = 1;
+    const int starve = g_fab_starve_kv_load;
     // Ring tile t: K_{t/2} for even t, V_{t/2} for odd t, in slot t % kRing.
     // With one S buffer the MMA thread frees V_j and K_{j+1} with one commit
     // (release group j+1; group 0 is K_0), on barrier group % kRing; with two,
@@ -315,6 +321,12 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
         }
       } else {
         if (!mbar_wait(bar_kv_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty)) break;
+      }
+      if (t == starve) {
+        issued = t + 1;
+        if (t == 0)
+          for (; q_loaded < kNQ; ++q_loaded) load_q(q_loaded);
+        continue;
       }
       mbar_arrive_expect_tx(bar_kv_full + s, C::kKVTileBytes);
       // Which tile is ring position t: alternating K/V with one S buffer;
@@ -1042,17 +1054,43 @@ int fa_select_one_tile_config(int dtype, int D, FaConfigInfo* out) {
 
 int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
 
-int fa_forward_one_tile(const FaLaunch& L, cudaStream_t stream) {
-  FaConfigInfo c;
-  int rc = fa_select_one_tile_config(L.dtype, L.D, &c);
-  if (rc) return rc;
-  if (c.s_bufs == 1) {
-    const long long rows = L.pack_gqa ? static_cast<long long>(L.Hq / L.Hkv) * L.M : L.M;
-    const long long ctas = (rows + 127) / 128 * L.B * (L.pack_gqa ? L.Hkv : L.Hq) * std::max(L.num_splits, 1);
-    const int sms = num_sms();
-    if (sms <= 0) return kErrCuda;
-    if (2 * ctas < 3LL * sms) return fa_forward_split(L, stream);
+// CTAs in the grid of a non-varlen launch whose tile holds nq query tiles.
+static long long fa_grid_ctas(const FaLaunch& L, int nq) {
+  const long long rows = L.pack_gqa ? static_cast<long long>(L.Hq / L.Hkv) * L.M : L.M;
+  const long long per_cta = 128LL * nq;
+  return (rows + per_cta - 1) / per_cta * L.B * (L.pack_gqa ? L.Hkv : L.Hq) * std::max(L.num_splits, 1);
+}
+
+int fa_plan(const FaLaunch& L, int variant, FaPlanInfo* out) {
+  int rc;
+  out->split_table = false;
+  if (variant == 0) {
+    rc = fa_select_config(L.dtype, L.D, &out->cfg);
+  } else {
+    rc = fa_select_one_tile_config(L.dtype, L.D, &out->cfg);
+    if (rc == 0 && out->cfg.s_bufs == 1) {
+      // Two CTAs per SM only pay when most SMs get two: below 1.5 CTAs per
+      // SM the split tiles (two S buffers in one CTA) run the pass instead.
+      const int sms = num_sms();
+      if (sms <= 0) return kErrCuda;
+      if (2 * fa_grid_ctas(L, out->cfg.nq) < 3LL * sms) {
+        rc = fa_select_split_config(L.dtype, L.D, &out->cfg);
+        out->split_table = true;
+      }
+    }
   }
+  if (rc) return rc;
+  out->ctas = fa_grid_ctas(L, out->cfg.nq);
+  out->ctas_per_sm = (out->cfg.nq == 1 && out->cfg.s_bufs == 1) ? 2 : 1;
+  return kOk;
+}
+
+int fa_forward_one_tile(const FaLaunch& L, cudaStream_t stream) {
+  FaPlanInfo plan;
+  int rc = fa_plan(L, 1, &plan);
+  if (rc) return rc;
+  if (plan.split_table) return fa_forward_split(L, stream);
+  const FaConfigInfo& c = plan.cfg;
   const int elt = L.dtype == kDtypeF32 ? 4 : 2;
   rc = kErrUnsupported;
 #define FAB_FA_OLAUNCH(E, DP, NQ, BN, ST, SB) \

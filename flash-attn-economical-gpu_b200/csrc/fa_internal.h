@@ -168,6 +168,16 @@ int fa_forward(const FaLaunch& L, cudaStream_t stream);
 int fa_select_split_config(int dtype, int D, FaConfigInfo* out);
 int fa_select_one_tile_config(int dtype, int D, FaConfigInfo* out);
 int fa_forward_one_tile(const FaLaunch& L, cudaStream_t stream);
+// The tile a forward launch of `variant` (0 two tiles, 1 one tile) runs, its
+// grid size and how many of its CTAs share an SM; fa_forward_one_tile takes
+// its kernel from this.
+struct FaPlanInfo {
+  FaConfigInfo cfg;
+  long long ctas;
+  int ctas_per_sm;
+  bool split_table;  // the one-tile call runs the split-KV tile as one pass
+};
+int fa_plan(const FaLaunch& L, int variant, FaPlanInfo* out);
 // num_splits <= 0 picks a split count from the SM count (needs a device).
 int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan);
 // Launches the split kernel and the combine kernel; L carries the plan.

@@ -36,6 +36,10 @@ static __device__ int g_fab_device_error = 0;
 // A single wait may take at most this long before the kernel gives up.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// The limit the waits of this unit apply: kWaitLimitNs unless a test has set
+// a shorter one through fab_debug_set_wait_limit_ns (attention unit only).
+static __device__ uint64_t g_fab_wait_limit_ns = kWaitLimitNs;
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -92,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > g_fab_wait_limit_ns) {
         record_device_error(code);
         *abort = 1;
         return false;

@@ -9,6 +9,12 @@ Triton's driver.  The reference's Triton IR / PTX transfer analysis
 it is unreachable at run time in the reference (nothing stores a PTX path in
 the launch context).  Register and shared-memory usage come from
 `cudaFuncGetAttributes` through the C ABI instead.
+
+Attribution: the blocks marked "interface kept from the reference" reproduce
+the interface of josephzhong/flash-attn-economical-gpu (exceptions.py: the out-of-resources error class, its hint sentences and message format), which is
+licensed under the Apache License, Version 2.0; they are kept as they are so
+that callers of the reference, and code that parses its messages, work
+unchanged.  Everything else in this module is this project's own.
 """
 from __future__ import annotations
 
@@ -96,6 +102,7 @@ def _resource_failure_text(prefix: str, exc: "OutOfResourcesWithDetail") -> str:
     return f"{prefix}: {exc} [{_resource_usage_summary('failed', getattr(exc, 'launch_context', {}) or {})}]"
 
 
+# Interface kept from the reference (exceptions.py:695-757, Apache-2.0).
 class OutOfResourcesWithDetail(OutOfResources):
     """Out-of-resources error carrying the kernel name and launch context."""
 

@@ -364,6 +364,39 @@ def attention_forward(
     return (o, lse) if return_lse else o
 
 
+def attention_plan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = False,
+                   variant: int | None = None) -> dict:
+    """The kernel `attention_forward` (variant None: the measured tile family it picks) or the given tile
+    family would launch for these tensors, without launching it: tile, grid size and CTAs per SM."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda_tensor(name, t)
+    dt = _native.dtype_code(q.dtype)
+    B, Hq, M, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    if variant is None:
+        variant = 0
+        if q.numel() and N:
+            variant = tune_table.measured_variant(dt, D, causal, B * Hq, M, N)
+    qc, kc, vc = _conform(q), _conform(k), _conform(v)
+    o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    p = _native.FabAttentionParams()
+    p.q, p.k, p.v, p.o = qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr()
+    p.q_stride_b, p.q_stride_h, p.q_stride_s = qc.stride()[:3]
+    p.k_stride_b, p.k_stride_h, p.k_stride_s = kc.stride()[:3]
+    p.v_stride_b, p.v_stride_h, p.v_stride_s = vc.stride()[:3]
+    p.o_stride_b, p.o_stride_h, p.o_stride_s = o.stride()[:3]
+    p.batch, p.heads_q, p.heads_kv, p.seqlen_q, p.seqlen_k, p.head_dim = B, Hq, Hkv, M, N, D
+    p.dtype, p.sm_scale, p.causal = dt, D ** -0.5, 1 if causal else 0
+    plan = _native.FabFaPlan()
+    with torch.cuda.device(q.device):
+        _native.check(_native.lib.fab_attention_fwd_plan(ctypes.byref(p), int(variant), ctypes.byref(plan)),
+                      "attention_plan")
+    c = plan.config
+    return {"variant": int(variant), "q_tiles_per_cta": c.q_tiles_per_cta, "block_n": c.block_n,
+            "stages": c.stages, "s_buffers": c.s_buffers, "threads": c.threads, "smem_bytes": c.smem_bytes,
+            "ctas": int(plan.ctas), "ctas_per_sm": plan.ctas_per_sm}
+
+
 def attention_forward_splitkv(
     q: torch.Tensor,
     k: torch.Tensor,

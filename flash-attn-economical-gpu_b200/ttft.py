@@ -25,6 +25,12 @@ Two parts.
 
 TTFT is measured as in ttft.py:449-480: one forward over the prompt producing
 the last position's logits and its argmax, synchronised, repeated.
+
+Attribution: the blocks marked "interface kept from the reference" reproduce
+the interface of josephzhong/flash-attn-economical-gpu (ttft.py: ModelShape, estimate_fp16_vram_gib, the SDPA-replacement argument checks and messages, _repeat_kv_for_gqa, the backend names and force_noncausal_attention), which is
+licensed under the Apache License, Version 2.0; they are kept as they are so
+that callers of the reference, and code that parses its messages, work
+unchanged.  Everything else in this module is this project's own.
 """
 from __future__ import annotations
 
@@ -60,6 +66,9 @@ DEVICE = "cuda"
 
 
 # ------------------------------------------------------------------ shapes
+# Interface kept from the reference (ttft.py, Apache-2.0) in ModelShape,
+# estimate_fp16_vram_gib, the SDPA-replacement checks and messages,
+# _repeat_kv_for_gqa, the backend names and force_noncausal_attention.
 @dataclass(frozen=True)
 class ModelShape:
     model_id: str
@@ -147,6 +156,8 @@ def _block_d_tune_args(head_dim: int) -> FlashAttenTuneArguments:
     raise ValueError(f"block-D nomask benchmark only has known launch settings for head_dim 128 or 256, got {head_dim}")
 
 
+# Interface kept from the reference (ttft.py:170-211, Apache-2.0): argument
+# checks and their messages.
 def _run_block_d_nomask_vanilla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None) -> torch.Tensor:
     """The reference's sliced-kernel SDPA path with its argument checks (ttft.py:169-196)."""
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
@@ -173,6 +184,7 @@ def _raise_unsupported_triton(reason: str):
     raise RuntimeError(f"triton_block_d_nomask unsupported SDPA call: {reason}")
 
 
+# Interface kept from the reference (ttft.py:203-219, Apache-2.0).
 def _repeat_kv_for_gqa(k_or_v: torch.Tensor, query_heads: int) -> torch.Tensor:
     kv_heads = k_or_v.shape[1]
     if kv_heads == query_heads:
@@ -210,6 +222,7 @@ def _run_efficient_gqa_expanded_sdpa(q, k, v, sdpa_fn, *, attn_mask, dropout_p, 
         return sdpa_fn(q, k, v, is_causal=is_causal, dropout_p=0.0, scale=scale)
 
 
+# Interface kept from the reference (Apache-2.0).
 @contextlib.contextmanager
 def force_noncausal_attention(model) -> Iterator[None]:
     patched = []

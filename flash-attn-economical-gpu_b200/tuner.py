@@ -20,6 +20,12 @@ choice is by measured time -- on the caller's tensors with
 (`tune_table.measured_variant`).  User tune arguments are validated exactly
 as the reference validates them and take part in the cache key; the tile
 reported in `FlashAttentionLaunchSpec.tune_args` is the one the kernel runs.
+
+Attribution: the blocks marked "interface kept from the reference" reproduce
+the interface of josephzhong/flash-attn-economical-gpu (tuner.py: the launch-spec dataclasses, the tuners' constructor checks and ValueError texts, the kernel argument tuples and the o/lse allocation), which is
+licensed under the Apache License, Version 2.0; they are kept as they are so
+that callers of the reference, and code that parses its messages, work
+unchanged.  Everything else in this module is this project's own.
 """
 from __future__ import annotations
 
@@ -39,6 +45,8 @@ def get_architecture():
     return major, minor
 
 
+# Interface kept from the reference (tuner.py:18-108, Apache-2.0): the launch-spec
+# dataclasses below, with their validation messages.
 @dataclass(frozen=True)
 class LaunchSpec:
     grid: tuple[int, ...]
@@ -124,6 +132,8 @@ class FlashAttentionTuner(Tuner):
     KERNEL_NAME = "_flash_attn_fwd_kernel_basic"
     _config_cache: dict[tuple[object, ...], tuple[dict[str, int | bool], dict[str, object]]] = {}
 
+    # Interface kept from the reference (tuner.py:115-175, Apache-2.0): the
+    # constructor checks and their ValueError texts.
     def __init__(
         self,
         q_shape: tuple[int, int, int, int],
@@ -285,6 +295,8 @@ class FlashAttentionTuner(Tuner):
         launch_context: dict[str, object] | None = None,
     ) -> FlashAttentionLaunchSpec:
         grid = (math.ceil(self.M / int(config["BLOCK_M"])), self.B * self.H)
+        # Interface kept from the reference (tuner.py:265-295, Apache-2.0): the
+        # 29-argument kernel tuple.
         kernel_args = (
             q,
             k,
@@ -430,6 +442,8 @@ class FlashAttentionTuner(Tuner):
         self._config_cache[key] = (dict(config), dict(spec.launch_context))
         return spec
 
+    # Interface kept from the reference (tuner.py:562-590, Apache-2.0): o and
+    # fp32 lse allocated as the reference allocates them.
     def build_flash_attention_launch_spec(
         self,
         q: torch.Tensor,
@@ -504,6 +518,7 @@ class FlashAttentionBlockDNomaskTuner(FlashAttentionTuner):
         launch_context: dict[str, object] | None = None,
     ) -> FlashAttentionLaunchSpec:
         grid = (math.ceil(self.M / int(config["BLOCK_M"])), self.B * self.H)
+        # Interface kept from the reference (tuner.py:640-650, Apache-2.0).
         kernel_args = (q, k, v, o, self.H, self.M, self.N, self.D, sm_scale)
         kernel_kwargs = {
             "BLOCK_M": int(config["BLOCK_M"]),

@@ -383,6 +383,23 @@ int fab_attention_fwd_variant(const fab_attention_params* params, int variant, v
 int fab_flash_attn_config_variant(int dtype, int head_dim, int variant, fab_fa_config* out);
 
 /*
+ * The kernel a fab_attention_fwd_variant call with these arguments would
+ * launch, without launching it: its tile, the CTAs of its grid and how many
+ * of them share one SM (2 for the one-tile, one-S-buffer kernel; a ONE_TILE
+ * call with fewer than 1.5 CTAs per SM runs the two-S-buffer tile instead and
+ * reports 1).  Replaces the launch facts the reference's tuner reads back
+ * from its chosen config (grid and num_warps, tuner.py:533-561).  A call with
+ * no query rows reports all zeros.
+ */
+typedef struct fab_fa_plan {
+  fab_fa_config config;
+  long long ctas;
+  int ctas_per_sm;
+} fab_fa_plan;
+
+int fab_attention_fwd_plan(const fab_attention_params* params, int variant, fab_fa_plan* out);
+
+/*
  * Compiled-kernel facts that replace Triton's `kernel.warmup(...)` metadata
  * (tuner.py:355-368: metadata.shared, metadata.num_warps, n_regs).
  * which: 0 = attention kernel for (dtype, head_dim), 1 = matmul kernel for dtype.
@@ -418,6 +435,21 @@ int fab_device_limits_query(int device, fab_device_limits* out);
  * the wait.  Synchronises with the device (call it between launches).
  */
 int fab_get_device_error(int* code);
+
+/*
+ * Test hooks for the bounded waits of the attention kernels (no counterpart
+ * in the reference, which has no device-side waits).  They change device
+ * state of the current device and synchronise with it; call them only
+ * between launches.
+ * fab_debug_set_wait_limit_ns: the time one wait may take before the kernel
+ *   records its code in the device error word and unwinds (0 restores the
+ *   default of 2 s).
+ * fab_debug_starve_kv_load: the producer of every attention CTA skips the
+ *   K/V ring load with this index (ring order: K_0, V_0, K_1, V_1, ... with
+ *   one S buffer), so the wait for it runs out; -1 restores normal loading.
+ */
+int fab_debug_set_wait_limit_ns(unsigned long long ns);
+int fab_debug_starve_kv_load(int ring_tile);
 
 /* Human-readable text for a FAB_* return code. */
 const char* fab_error_string(int rc);

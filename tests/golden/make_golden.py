@@ -4,14 +4,14 @@ Runs the reference's own Triton kernels (flash_atten.py, mma.py of
 josephzhong/flash-attn-economical-gpu) in Triton's CPU interpreter
 (TRITON_INTERPRET=1) on small seeded inputs and stores inputs and outputs in
 golden.npz plus a case list in golden.json.  It needs the reference checkout
-(path in FAB_REFERENCE_DIR, default /root/reference) and Triton, so it runs
-only where those exist; the committed .npz/.json files are what the tests read.
+(its directory is the one required argument) and Triton, so it runs only
+where those exist; the committed .npz/.json files are what the tests read.
 
 Triton's interpreter computes bf16 incorrectly (it round-trips through numpy,
 which has no bf16), so the cases are fp16 and fp32, the dtypes the reference's
 own tests and its fp32 correctness case use.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py <reference checkout directory>
 """
 from __future__ import annotations
 
@@ -23,11 +23,12 @@ from pathlib import Path
 os.environ["TRITON_INTERPRET"] = "1"
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FAB_REFERENCE_DIR", "/root/reference"))
 
 
 def main() -> None:
-    sys.path.insert(0, str(REF))
+    if len(sys.argv) != 2 or not (Path(sys.argv[1]) / "flash_atten.py").is_file():
+        sys.exit("usage: make_golden.py <reference checkout directory holding flash_atten.py and mma.py>")
+    sys.path.insert(0, str(Path(sys.argv[1]).resolve()))
     import numpy as np
     import torch
 

@@ -142,6 +142,25 @@ def test_null_and_bad_arguments_are_rejected_before_any_launch():
     assert lib.fab_attention_fwd(ctypes.byref(a), None) == _native.FAB_ERR_INVALID_ARG
 
 
+def test_attention_plan_reports_the_launch_without_a_device():
+    lib = _native.lib
+    plan = _native.FabFaPlan()
+    assert lib.fab_attention_fwd_plan(None, 0, ctypes.byref(plan)) == _native.FAB_ERR_INVALID_ARG
+    a = _native.FabAttentionParams()
+    a.batch, a.heads_q, a.heads_kv, a.seqlen_q, a.seqlen_k, a.head_dim, a.dtype = 4, 32, 32, 8192, 8192, 128, 1
+    a.sm_scale = 128 ** -0.5
+    a.q = a.k = a.v = a.o = 4096
+    a.q_stride_s = a.k_stride_s = a.v_stride_s = a.o_stride_s = 128
+    assert lib.fab_attention_fwd_plan(ctypes.byref(a), 5, ctypes.byref(plan)) == _native.FAB_ERR_INVALID_ARG
+    assert lib.fab_attention_fwd_plan(ctypes.byref(a), 0, None) == _native.FAB_ERR_INVALID_ARG
+    # The two-tile table needs no device query: 256 query rows per CTA, one CTA per SM.
+    assert lib.fab_attention_fwd_plan(ctypes.byref(a), 0, ctypes.byref(plan)) == _native.FAB_OK
+    assert (plan.config.q_tiles_per_cta, plan.config.block_n, plan.ctas, plan.ctas_per_sm) == (2, 128, 4 * 32 * 32, 1)
+    a.seqlen_q = 0
+    assert lib.fab_attention_fwd_plan(ctypes.byref(a), 0, ctypes.byref(plan)) == _native.FAB_OK
+    assert plan.ctas == 0
+
+
 def test_strided_entry_requires_unit_head_dim_stride():
     lib = _native.lib
     args = [4096, 4096, 4096, 4096, None]

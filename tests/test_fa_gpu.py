@@ -284,26 +284,108 @@ def _sampled_rows_check(q, k, v, o, causal, dtype, picks):
         _close(o[b, h, m0:m1], ro[0, 0])
 
 
+def _spread_picks(B, H, S):
+    """First, middle, last and one unaligned row block, on different (batch, head) pairs."""
+    mid = S // 2
+    return [(0, 0, 0, 128), (B // 2, H // 2, mid, mid + 128), (B - 1, H - 1, S - 128, S),
+            (B - 1, H // 3, S // 3 + 5, S // 3 + 105)]
+
+
 @pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
-def test_config2_full_size_sampled(causal, cuda_device):
-    """The headline benchmark shape at S=8192: B4 H32 D128 bf16; rows sampled across heads and positions."""
-    B, H, S, D = 4, 32, 8192, 128
-    g = torch.Generator(device=cuda_device).manual_seed(21)
+@pytest.mark.parametrize("S", [1024, 2048, 4096, 8192])
+def test_config2_full_size_sampled(S, causal, cuda_device):
+    """BASELINE config 2 at every sequence length: B4 H32 D128 bf16 through attention_forward, whose
+    measured tile-family choice switches kernels across these lengths; rows sampled across heads."""
+    B, H, D = 4, 32, 128
+    g = torch.Generator(device=cuda_device).manual_seed(21 + S)
     q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
     o = attention_forward(q, k, v, causal=causal)
     assert not torch.isnan(o).any()
-    picks = [(0, 0, 0, 128), (1, 17, 4096, 4224), (3, 31, 8064, 8192), (2, 5, 1000, 1100)]
+    picks = _spread_picks(B, H, S) + ([(1, 17, 4096, 4224), (2, 5, 1000, 1100)] if S == 8192 else [])
     _sampled_rows_check(q, k, v, o, causal, torch.bfloat16, picks)
 
 
-def test_config3_d256_full_size_sampled(cuda_device):
-    """The D=256 benchmark shape: B2 H16 S8192 bf16, causal, scale 1/16."""
-    B, H, S, D = 2, 16, 8192, 256
-    g = torch.Generator(device=cuda_device).manual_seed(22)
+@pytest.mark.parametrize("S", [2048, 4096, 8192])
+def test_config3_d256_full_size_sampled(S, cuda_device):
+    """BASELINE config 3, D=256: B2 H16 bf16, causal, scale 1/16, at every sequence length."""
+    B, H, D = 2, 16, 256
+    g = torch.Generator(device=cuda_device).manual_seed(22 + S)
     q, k, v = (torch.randn(B, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
     o = attention_forward(q, k, v, causal=True, sm_scale=1 / 16)
     assert not torch.isnan(o).any()
-    _sampled_rows_check(q, k, v, o, True, torch.bfloat16, [(0, 0, 0, 128), (1, 15, 8000, 8192), (0, 7, 3000, 3128)])
+    _sampled_rows_check(q, k, v, o, True, torch.bfloat16, _spread_picks(B, H, S))
+
+
+@pytest.mark.parametrize("S", [16384, 32768, 65536])
+@pytest.mark.parametrize("H, D", [(28, 128), (16, 256)], ids=["H28D128", "H16D256"])
+def test_reference_large_cases_sampled(H, D, S, cuda_device):
+    """The reference's long-sequence pipeline cases (test_flash_atten.py:82-88: B1, H28 D128 and H16 D256,
+    non-causal, asserted at rtol 1e-2 / atol 2e-2, :489-495) at S 16K-64K: 32-bit offsets and long
+    online-softmax accumulation.  First and last row blocks included."""
+    g = torch.Generator(device=cuda_device).manual_seed(S + D)
+    q, k, v = (torch.randn(1, H, S, D, generator=g, device=cuda_device, dtype=torch.bfloat16) for _ in range(3))
+    o = attention_forward(q, k, v)
+    assert not torch.isnan(o).any()
+    picks = [(0, 0, 0, 128), (0, H // 2, S // 2 - 64, S // 2 + 64), (0, H - 1, S - 128, S)]
+    _sampled_rows_check(q, k, v, o, False, torch.bfloat16, picks)
+
+
+# ------------------------------------------- the two-CTAs-per-SM one-tile kernel
+DUAL_CASES = [
+    # (B, Hq, Hkv, S, D, dtype, causal)
+    (4, 32, 32, 1024, 128, torch.bfloat16, False),
+    (4, 32, 32, 1024, 128, torch.bfloat16, True),
+    (4, 32, 32, 2048, 128, torch.bfloat16, False),
+    (4, 32, 32, 2048, 128, torch.bfloat16, True),
+    (4, 32, 32, 1024, 128, torch.float16, True),
+    (4, 32, 32, 2048, 128, torch.float16, False),
+    (4, 32, 32, 1024, 64, torch.float16, False),
+    (4, 32, 32, 1024, 64, torch.float16, True),
+    (4, 32, 32, 2048, 64, torch.bfloat16, True),
+    (4, 32, 32, 1024, 64, torch.float32, False),
+    (4, 32, 32, 1024, 64, torch.float32, True),
+    (1, 28, 4, 2048, 128, torch.bfloat16, True),  # the TTFT prefill: Qwen2.5-7B heads at 2048 tokens
+]
+
+
+@pytest.mark.parametrize("case", DUAL_CASES,
+                         ids=lambda c: "B{}H{}/{}S{}D{}-{}-{}".format(*c[:5], P_DTYPE[c[5]],
+                                                                      "causal" if c[6] else "full"))
+def test_two_ctas_per_sm_kernel_matches_oracle(case, cuda_device):
+    """The one-tile, one-S-buffer kernel that two CTAs share an SM with (the measured choice for causal
+    S <= 2048 and for the TTFT prefill).  It runs only with at least 1.5 CTAs per SM, so the grid here is
+    asserted to be that large; rows are checked against the oracle at the normal tolerance, LSE too."""
+    B, Hq, Hkv, S, D, dtype, causal = case
+    q, k, v, qd, kd, vd = _inputs((B, Hq, Hkv, S, S, D), dtype, seed=zlib.crc32(repr(case).encode()), dev=cuda_device)
+    plan = flash_atten.attention_plan(qd, kd, vd, causal=causal, variant=1)
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    assert plan["ctas_per_sm"] == 2 and plan["s_buffers"] == 1 and plan["q_tiles_per_cta"] == 1
+    assert 2 * plan["ctas"] >= 3 * sms, plan
+    o = torch.empty_like(qd)
+    lse = torch.empty(B, Hq, S, device=cuda_device, dtype=torch.float32)
+    flash_atten._launch_attention(qd, kd, vd, o, lse, causal=causal, sm_scale=D ** -0.5, what="test", variant=1)
+    torch.cuda.synchronize()
+    assert not torch.isnan(o).any()
+    tf32 = dtype == torch.float32
+    for b, h, m0, m1 in _spread_picks(B, Hq, S):
+        hk = h // (Hq // Hkv)
+        n_end = min(S, m1) if causal else S
+        ro, rl = tiled_attention_forward(q[b:b + 1, h:h + 1, m0:m1].float().numpy(),
+                                         k[b:b + 1, hk:hk + 1, :n_end].float().numpy(),
+                                         v[b:b + 1, hk:hk + 1, :n_end].float().numpy(), causal=causal,
+                                         p_dtype=P_DTYPE[dtype], block_m=128, block_n=512, q_row_offset=m0)
+        _close(o[b, h, m0:m1], ro[0, 0])
+        _close(lse[b, h, m0:m1], rl[0, 0], rtol=1e-3 if tf32 else 1e-4, atol=1e-2 if tf32 else LSE_ATOL)
+
+
+def test_measured_choice_takes_two_ctas_per_sm_for_short_causal(cuda_device):
+    """attention_forward's measured family choice for BASELINE config 2 causal S1024/S2048 and the TTFT
+    prefill is the two-CTAs-per-SM kernel, so the parity cases above cover what those calls run."""
+    for B, Hq, Hkv, S in ((4, 32, 32, 1024), (4, 32, 32, 2048), (1, 28, 4, 2048)):
+        q = torch.empty(B, Hq, S, 128, device=cuda_device, dtype=torch.bfloat16)
+        kv = torch.empty(B, Hkv, S, 128, device=cuda_device, dtype=torch.bfloat16)
+        plan = flash_atten.attention_plan(q, kv, kv, causal=True)
+        assert plan["variant"] == 1 and plan["ctas_per_sm"] == 2, (B, Hq, Hkv, S, plan)
 
 
 def test_config3_gqa_full_size_sampled(cuda_device):
