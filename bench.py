@@ -633,6 +633,7 @@ def run_ttft(args, world, rank, local):
            "causal": True, "unit": "ms", "timing": "wall clock per prefill, synchronised, max over ranks"}
     builds = {
         "ours": ttft.Backends(attention="native", gemm="native"),
+        "ours_norm_folded": ttft.Backends(attention="native", gemm="native", norm_fold=True),
         "ours_attention_cublas_gemm": ttft.Backends(attention="native", gemm="cublas"),
         "torch_cudnn_sdpa_cublas": ttft.Backends(attention="cudnn", gemm="cublas", elementwise="torch"),
     }

@@ -70,6 +70,7 @@ class FabGemmParams(ctypes.Structure):
         ("M", _i32), ("N", _i32), ("K", _i32),
         ("in_dtype", _i32), ("out_dtype", _i32), ("round_f16", _i32), ("group_m", _i32), ("epilogue", _i32),
         ("bias", _vp), ("rope_cos", _vp), ("rope_sin", _vp), ("rope_cols", _i32), ("head_dim", _i32),
+        ("row_scale", _vp),
     ]
 
 
@@ -151,6 +152,7 @@ PROTOTYPES = {
     "fab_ipc_import": (_i32, [_vp, ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
     "fab_ipc_close": (_i32, [_vp]),
     "fab_rmsnorm": (_i32, [_vp] * 5 + [_i32, _i32] + [_i64] * 4 + [_f32, _i32, _vp]),
+    "fab_rmsnorm_rstd": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i64, _f32, _i32, _vp]),
     "fab_bias_rope": (_i32, [_vp] * 4 + [_i32] * 4 + [_i64, _i32, _vp]),
     "fab_silu_mul": (_i32, [_vp, _vp, _i32, _i32, _i64, _i64, _i32, _i32, _vp]),
     "fab_flash_attn_config": (_i32, [_i32, _i32, ctypes.POINTER(FabFaConfig)]),

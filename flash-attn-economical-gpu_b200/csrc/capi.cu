@@ -564,6 +564,7 @@ static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothin
   }
   const int c_cols = swiglu ? p->N / 2 : p->N;
   if ((p->ldc * oe) % 16 != 0 || p->ldc < c_cols) return kErrInvalidArg;
+  if (p->row_scale != nullptr && (reinterpret_cast<uintptr_t>(p->row_scale) & 3u) != 0) return kErrInvalidArg;
   if (p->K == 0) {
     *empty_k = true;
     return kOk;
@@ -585,6 +586,7 @@ static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothin
   L.round_f16 = p->round_f16;
   L.group_m = p->group_m;
   L.swiglu = swiglu ? 1 : 0;
+  L.row_scale = p->row_scale;
   if (rope) {
     L.bias_rope = 1;
     L.rope_cols = p->rope_cols;
@@ -746,12 +748,34 @@ int fab_rmsnorm(const void* x, const void* residual, const void* w, void* h, voi
     using T = __nv_bfloat16;
     rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual),
                                             static_cast<const T*>(w), static_cast<T*>(h), static_cast<T*>(x_out), cols,
-                                            ld_x, ld_res, ld_h, ld_xo, eps);
+                                            ld_x, ld_res, ld_h, ld_xo, eps, nullptr);
   } else {
     using T = __half;
     rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual),
                                             static_cast<const T*>(w), static_cast<T*>(h), static_cast<T*>(x_out), cols,
-                                            ld_x, ld_res, ld_h, ld_xo, eps);
+                                            ld_x, ld_res, ld_h, ld_xo, eps, nullptr);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int fab_rmsnorm_rstd(const void* x, const void* residual, void* x_out, float* rstd, int rows, int cols, int64_t ld_x,
+                     int64_t ld_res, int64_t ld_xo, float eps, int dtype, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 != 0 || cols > 8192) return kErrInvalidArg;
+  if (x == nullptr || rstd == nullptr || (residual != nullptr && x_out == nullptr)) return kErrInvalidArg;
+  if (!al16(x) || !al16(residual) || !al16(x_out) || (reinterpret_cast<uintptr_t>(rstd) & 3u) != 0)
+    return kErrInvalidArg;
+  if (!ld16(ld_x) || (residual != nullptr && (!ld16(ld_res) || !ld16(ld_xo)))) return kErrInvalidArg;
+  if (dtype != kDtypeBF16 && dtype != kDtypeF16) return kErrUnsupported;
+  if (rows == 0) return kOk;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (dtype == kDtypeBF16) {
+    using T = __nv_bfloat16;
+    rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual), nullptr,
+                                            nullptr, static_cast<T*>(x_out), cols, ld_x, ld_res, 0, ld_xo, eps, rstd);
+  } else {
+    using T = __half;
+    rmsnorm_kernel<T><<<rows, 256, 0, st>>>(static_cast<const T*>(x), static_cast<const T*>(residual), nullptr,
+                                            nullptr, static_cast<T*>(x_out), cols, ld_x, ld_res, 0, ld_xo, eps, rstd);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }

@@ -48,12 +48,14 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 }
 
 // One CTA per row; `cols` a multiple of 8.  With `res` != nullptr the row is
-// x + res, written to x_out (may alias x) before the norm.
+// x + res, written to x_out (may alias x) before the norm.  With h ==
+// nullptr only the row's rsqrt(mean(x^2) + eps) is written, to rstd[row]
+// (the scale a GEMM with the norm folded into it applies).
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ res,
                                                       const T* __restrict__ w, T* __restrict__ h, T* x_out, int cols,
                                                       int64_t ld_x, int64_t ld_res, int64_t ld_h, int64_t ld_xo,
-                                                      float eps) {
+                                                      float eps, float* __restrict__ rstd) {
   constexpr int kMaxVec = 4;  // 8 columns per vector, 256 threads: up to 8192 columns
   const int64_t row = blockIdx.x;
   const int nvec = cols / 8;
@@ -85,6 +87,10 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float inv = rsqrtf(tot / static_cast<float>(cols) + eps);
+  if (h == nullptr) {
+    if (threadIdx.x == 0) rstd[row] = inv;
+    return;
+  }
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* hr = reinterpret_cast<uint4*>(h + row * ld_h);
 #pragma unroll

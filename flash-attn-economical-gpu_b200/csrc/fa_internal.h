@@ -125,6 +125,10 @@ struct GemmKernelParams {
   const void* bias;  // [N] or null
   const void* rope_cos;
   const void* rope_sin;
+  // [M] fp32 or null: row r's accumulator is multiplied by row_scale[r]
+  // before any epilogue rounding (an RMSNorm's 1/rms folded into the GEMM
+  // that consumes the normalised rows; its weight is folded into B).
+  const float* row_scale;
 };
 
 // Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output
@@ -158,6 +162,7 @@ struct GemmLaunch {
   const void* bias;
   const void* rope_cos;
   const void* rope_sin;
+  const float* row_scale;  // see GemmKernelParams
 };
 
 // Epilogues that need whole 256-column tiles (gate/up block pairs, whole heads).

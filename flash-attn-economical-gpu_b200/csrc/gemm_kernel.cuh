@@ -177,6 +177,7 @@ __device__ __forceinline__ void gemm_store_bias_rope_row(const GemmKernelParams&
   // past M read table row 0 and store nothing.
   const bool row_ok = row < p.M;
   const int trow = row_ok ? row : 0;
+  const float rs = p.row_scale != nullptr ? p.row_scale[trow] : 1.0f;  // x * 1.0f == x: no-op without a scale
   const int hd = p.head_dim, half = hd / 2;
   Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(trow) * p.ldc;
   const Tout* bias = static_cast<const Tout*>(p.bias);
@@ -209,8 +210,8 @@ __device__ __forceinline__ void gemm_store_bias_rope_row(const GemmKernelParams&
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float l = round_to<Tout>(__uint_as_float(rl[8 * g + e]));
-          float h = round_to<Tout>(__uint_as_float(rh[8 * g + e]));
+          float l = round_to<Tout>(__uint_as_float(rl[8 * g + e]) * rs);
+          float h = round_to<Tout>(__uint_as_float(rh[8 * g + e]) * rs);
           if (bias != nullptr) {
             l = round_to<Tout>(l + bl[e]);
             h = round_to<Tout>(h + bh[e]);
@@ -235,6 +236,7 @@ __device__ __forceinline__ void gemm_store_bias_rope_row(const GemmKernelParams&
 
 template <typename Tout, int kWidth>
 __device__ __forceinline__ void gemm_store_tile_row(const GemmKernelParams& p, uint32_t acc, int row, int n0) {
+  const float rs = (p.row_scale != nullptr && row < p.M) ? p.row_scale[row] : 1.0f;
   if constexpr (sizeof(Tout) == 2 && kWidth == 256) {
     if (p.bias_rope) {
       gemm_store_bias_rope_row<Tout>(p, acc, row, n0);
@@ -253,8 +255,8 @@ __device__ __forceinline__ void gemm_store_tile_row(const GemmKernelParams& p, u
         float v[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float g = round_to<Tout>(__uint_as_float(rg[e]));
-          const float u = round_to<Tout>(__uint_as_float(ru[e]));
+          const float g = round_to<Tout>(__uint_as_float(rg[e]) * rs);
+          const float u = round_to<Tout>(__uint_as_float(ru[e]) * rs);
           v[e] = round_to<Tout>(g / (1.0f + expf(-g))) * u;
         }
         const int ncols = min(32, p.N / 2 - o0 - q * 32);
@@ -271,7 +273,7 @@ __device__ __forceinline__ void gemm_store_tile_row(const GemmKernelParams& p, u
     tmem_wait_ld();
     float v[32];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]) * rs;
     const int ncols = min(32, p.N - n0 - cc * 32);
     if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
   }
@@ -712,6 +714,7 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   kp.bias = L.bias;
   kp.rope_cos = L.rope_cos;
   kp.rope_sin = L.rope_sin;
+  kp.row_scale = L.row_scale;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   int sms = num_sms();

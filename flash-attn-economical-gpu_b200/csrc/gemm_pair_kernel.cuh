@@ -250,6 +250,7 @@ static int launch_gemm_pair_w(const GemmLaunch& L, cudaStream_t stream) {
   kp.bias = L.bias;
   kp.rope_cos = L.rope_cos;
   kp.rope_sin = L.rope_sin;
+  kp.row_scale = L.row_scale;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   const int sms = num_sms();

@@ -257,6 +257,7 @@ static int launch_gemm_splitk_k(const GemmLaunch& L, cudaStream_t stream) {
   kp.rope_cols = 0;
   kp.head_dim = 0;
   kp.bias = kp.rope_cos = kp.rope_sin = nullptr;
+  kp.row_scale = nullptr;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   kern<<<static_cast<unsigned>(tiles * kSplit), C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
@@ -275,7 +276,8 @@ constexpr int kSplitMinKBlocks = 48;
 template <typename Tin, typename Tout>
 static int gemm_splitk_factor(const GemmLaunch& L) {
   using C = GemmCfg<2>;
-  if (L.in_dtype == kDtypeF32 || gemm_fixed_width(L) || L.K <= 0) return 1;
+  // The split kernel has no row-scaled epilogue: such GEMMs are not split.
+  if (L.in_dtype == kDtypeF32 || gemm_fixed_width(L) || L.row_scale != nullptr || L.K <= 0) return 1;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   const int nkb = (L.K + C::kBK - 1) / C::kBK;
   const int sms = num_sms();

@@ -62,12 +62,14 @@ def _gemm(
     group_m: int = 8,
     epilogue: int = _native.FAB_GEMM_EPILOGUE_STORE,
     rope: tuple | None = None,
+    row_scale: torch.Tensor | None = None,
     what: str = "gemm",
 ) -> None:
     """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements).
 
     With the SwiGLU epilogue C is [M, N/2] (see `matmul_swiglu`); with the bias + RoPE epilogue `rope` is
-    (bias or None, cos, sin, rope_cols, head_dim) (see `matmul_bias_rope`)."""
+    (bias or None, cos, sin, rope_cols, head_dim) (see `matmul_bias_rope`).  `row_scale` (fp32 [M] or None)
+    multiplies row r's accumulator by row_scale[r] before the epilogue (an RMSNorm folded into the GEMM)."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         _require_cuda_tensor(name, t)
     if a.dtype != b.dtype:
@@ -86,6 +88,11 @@ def _gemm(
         p.bias = bias.data_ptr() if bias is not None else None
         p.rope_cos, p.rope_sin = cos.data_ptr(), sin.data_ptr()
         p.rope_cols, p.head_dim = int(rope_cols), int(head_dim)
+    if row_scale is not None:
+        _require_cuda_tensor("row_scale", row_scale)
+        if row_scale.dtype != torch.float32 or row_scale.numel() < M or not row_scale.is_contiguous():
+            raise ValueError(f"{what}: row_scale must be a contiguous float32 tensor of at least {M} elements")
+        p.row_scale = row_scale.data_ptr()
     with torch.cuda.device(a.device):
         rc = _native.lib.fab_gemm(ctypes.byref(p), ctypes.c_void_p(_native.current_stream_handle(a.device)))
     _native.check(rc, what)
@@ -237,14 +244,15 @@ def split_gate_up(gu: torch.Tensor, block: int = SWIGLU_BLOCK) -> tuple[torch.Te
 
 def matmul_bias_rope(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
                      sin: torch.Tensor, *, rope_cols: int, head_dim: int,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, row_scale: torch.Tensor | None = None) -> torch.Tensor:
     """C = rope(a @ w + bias): a QKV projection with its bias and rotate-half rotary embedding in the epilogue.
 
     a [S, K], w [K, N] (16-bit, unit column stride), bias [N] or None, cos/sin [>=S, head_dim] contiguous tables
     (row r = position r).  Every column gets the bias; the heads of head_dim columns among the first rope_cols
     are rotated.  Equals `matmul(a, w)` followed by the bias add and `q*cos + rotate_half(q)*sin` in the
     16-bit type, bit for bit.  No counterpart in the reference (its model adds the bias and applies RoPE as
-    separate PyTorch ops).
+    separate PyTorch ops).  With `row_scale` (fp32 [S]) row r's product is scaled by row_scale[r] first: an
+    RMSNorm folded in (see `fold_rmsnorm_weight`).
     """
     for name, t in (("a", a), ("w", w), ("cos", cos), ("sin", sin)) + ((("bias", bias),) if bias is not None else ()):
         _require_cuda_tensor(name, t)
@@ -269,17 +277,18 @@ def matmul_bias_rope(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None
         out = torch.empty((M, N), device=a.device, dtype=a.dtype)
     _gemm(a, w, out, M, N, K, lda=a.stride(0), ldb=w.stride(0), ldc=out.stride(0), round_f16=False,
           epilogue=_native.FAB_GEMM_EPILOGUE_BIAS_ROPE, rope=(bias, cos, sin, rope_cols, head_dim),
-          what="matmul_bias_rope")
+          row_scale=row_scale, what="matmul_bias_rope")
     return out
 
 
-def matmul_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+def matmul_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, *, out: torch.Tensor | None = None,
+                  row_scale: torch.Tensor | None = None) -> torch.Tensor:
     """silu(a @ W_gate) * (a @ W_up) [M, m] in one kernel, for w_gate_up = interleave_gate_up(W_gate, W_up).
 
     No counterpart in the reference (its matmul has one epilogue).  The tcgen05 GEMM's epilogue warps read
     each 64-column gate block and its up block from the same accumulator tile and store only the product,
     rounding as the PyTorch expression does in a's 16-bit dtype: silu of the rounded gate product, rounded,
-    times the rounded up product, rounded."""
+    times the rounded up product, rounded.  `row_scale` as in `matmul_bias_rope`."""
     if a.ndim != 2 or w_gate_up.ndim != 2 or a.shape[1] != w_gate_up.shape[0]:
         raise ValueError(f"matmul_swiglu expects a [M, K] and w [K, 2m], got {tuple(a.shape)} and "
                          f"{tuple(w_gate_up.shape)}")
@@ -295,8 +304,20 @@ def matmul_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, *, out: torch.Tensor
         w_gate_up = w_gate_up.contiguous()
     c = torch.empty((M, N // 2), device=a.device, dtype=a.dtype) if out is None else out
     _gemm(a, w_gate_up, c, M, N, K, lda=a.stride(0), ldb=w_gate_up.stride(0), ldc=c.stride(0), round_f16=False,
-          epilogue=_native.FAB_GEMM_EPILOGUE_SWIGLU, what="matmul_swiglu")
+          epilogue=_native.FAB_GEMM_EPILOGUE_SWIGLU, row_scale=row_scale, what="matmul_swiglu")
     return c
+
+
+def fold_rmsnorm_weight(norm_weight: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """B' = diag(norm_weight) B: an RMSNorm's weight folded into the [K, N] weight of the GEMM after it.
+
+    With it, rmsnorm(x) @ B equals rstd * (x @ B') row by row, where rstd = rsqrt(mean(x^2) + eps), which
+    `fab_rmsnorm_rstd` computes and the GEMM applies through `row_scale`.  The folded weight is rounded to
+    B's dtype once, so results agree with the unfused PyTorch expression within rounding, not bit for bit."""
+    if norm_weight.ndim != 1 or w.ndim != 2 or norm_weight.numel() != w.shape[0]:
+        raise ValueError(f"fold_rmsnorm_weight expects weight [K] and B [K, N], got {tuple(norm_weight.shape)} "
+                         f"and {tuple(w.shape)}")
+    return (norm_weight.float()[:, None] * w.float()).to(w.dtype).contiguous()
 
 
 __all__ = [
@@ -306,6 +327,7 @@ __all__ = [
     "matmul",
     "matmul_swiglu",
     "matmul_bias_rope",
+    "fold_rmsnorm_weight",
     "kernel_plan",
     "interleave_gate_up",
     "split_gate_up",

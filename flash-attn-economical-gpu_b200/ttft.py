@@ -395,6 +395,15 @@ class LayerShard:
     ln_post: torch.Tensor
     w_gate_up: torch.Tensor      # [hidden, 2 * mlp_local]: 64 gate, 64 up columns alternating (mma.interleave_gate_up)
     w_down: torch.Tensor         # [mlp_local, hidden]
+    # ln_in / ln_post folded into w_qkv / w_gate_up (Backends.norm_fold), made on first use
+    folded: tuple | None = None
+
+    def folded_weights(self) -> tuple[torch.Tensor, torch.Tensor]:
+        if self.folded is None:
+            from mma import fold_rmsnorm_weight
+
+            self.folded = (fold_rmsnorm_weight(self.ln_in, self.w_qkv), fold_rmsnorm_weight(self.ln_post, self.w_gate_up))
+        return self.folded
 
 
 @dataclass
@@ -501,6 +510,13 @@ class Backends:
     # all-reduce; a tp_allreduce.FusedGemmAllReduce = one fused kernel over
     # NVLink peer memory (same group, rows >= the prompt, cols = hidden).
     fused_allreduce: object = None
+    # The input and post-attention RMSNorms folded into the QKV and gate/up
+    # GEMMs (native GEMM and elementwise only): a stats pass writes each row's
+    # 1/rms, the norm weight lives in the GEMM's B (mma.fold_rmsnorm_weight)
+    # and the GEMM scales its rows before the epilogue, so the normalised
+    # activations are never written.  Agrees with the unfused forward within
+    # rounding, not bit for bit.
+    norm_fold: bool = False
 
 
 def _matmul(a: torch.Tensor, b: torch.Tensor, how: str) -> torch.Tensor:
@@ -562,6 +578,24 @@ def _native_rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torc
     return h
 
 
+def _native_rmsnorm_rstd(x: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+                         rstd: torch.Tensor | None = None) -> torch.Tensor:
+    """rstd[r] = rsqrt(mean(x'[r]^2) + eps) (fp32) for x' = x [+ residual]; with a residual x is updated in place."""
+    import ctypes
+
+    import _native
+
+    rows, cols = x.shape
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if rstd is None else rstd
+    stream = ctypes.c_void_p(_native.current_stream_handle(x.device))
+    rc = _native.lib.fab_rmsnorm_rstd(x.data_ptr(), residual.data_ptr() if residual is not None else None,
+                                      x.data_ptr() if residual is not None else None, rstd.data_ptr(), rows, cols,
+                                      x.stride(0), residual.stride(0) if residual is not None else 0, x.stride(0),
+                                      float(eps), _native.dtype_code(x.dtype), stream)
+    _native.check(rc, "fab_rmsnorm_rstd")
+    return rstd
+
+
 def _native_bias_rope(qkv: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor, sin: torch.Tensor,
                       heads: int, rot_heads: int, head_dim: int) -> None:
     import ctypes
@@ -614,15 +648,24 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
     cos, sin = cos2[:, None, :], sin2[:, None, :]
     x = model.embed[input_ids[0]]                                  # [S, hidden]
     attn_out = torch.empty(S, nq, D, device=x.device, dtype=x.dtype)
-    h_buf = torch.empty_like(x) if native else None
+    fold = native and backends.gemm == "native" and backends.norm_fold
+    h_buf = torch.empty_like(x) if native and not fold else None
+    rstd = torch.empty(S, device=x.device, dtype=torch.float32) if fold else None
     pending = None  # the previous layer's down_proj output, not yet added to x
     for layer in model.layers:
-        if native:
+        if fold:
+            _native_rmsnorm_rstd(x, arch.rms_norm_eps, residual=pending, rstd=rstd)
+            w_qkv, w_gate_up = layer.folded_weights()
+        elif native:
             h = _native_rmsnorm(x, layer.ln_in, arch.rms_norm_eps, residual=pending, h=h_buf)
         else:
             h = _rms_norm(x, layer.ln_in, arch.rms_norm_eps)
         pending = None
-        if native and backends.gemm == "native":
+        if fold:
+            # QKV GEMM over the raw rows: 1/rms, bias add and RoPE in its epilogue
+            qkv = matmul_bias_rope(x, w_qkv, layer.b_qkv, cos2, sin2, rope_cols=(nq + nkv) * D, head_dim=D,
+                                   row_scale=rstd)
+        elif native and backends.gemm == "native":
             # QKV GEMM with the bias add and RoPE in its epilogue
             qkv = matmul_bias_rope(h, layer.w_qkv, layer.b_qkv, cos2, sin2, rope_cols=(nq + nkv) * D, head_dim=D)
         else:
@@ -650,12 +693,16 @@ def _decoder_forward(model: ModelShard, input_ids: torch.Tensor, backends: Backe
         else:
             o = _matmul(attn_out.view(S, nq * D), layer.w_o, backends.gemm)
             _all_reduce(o, group)
-        if native:
+        if fold:
+            _native_rmsnorm_rstd(x, arch.rms_norm_eps, residual=o, rstd=rstd)
+        elif native:
             h = _native_rmsnorm(x, layer.ln_post, arch.rms_norm_eps, residual=o, h=h_buf)
         else:
             x = x + o
             h = _rms_norm(x, layer.ln_post, arch.rms_norm_eps)
-        if native and backends.gemm == "native":
+        if fold:
+            a = matmul_swiglu(x, w_gate_up, row_scale=rstd)  # 1/rms and SwiGLU in the epilogue
+        elif native and backends.gemm == "native":
             a = matmul_swiglu(h, layer.w_gate_up)  # gate/up GEMM with SwiGLU in its epilogue
         else:
             gu = _matmul(h, layer.w_gate_up, backends.gemm)

@@ -223,6 +223,16 @@ typedef struct fab_gemm_params {
   const void* rope_sin;
   int rope_cols;        /* leading columns that get RoPE (whole heads) */
   int head_dim;         /* 64, 128 or 256 */
+  /*
+   * NULL, or [M] fp32 (4-byte aligned): row r's accumulator is multiplied by
+   * row_scale[r] before any epilogue step or rounding, with every epilogue.
+   * This folds an RMSNorm into the GEMM that consumes its rows: A holds the
+   * raw rows, B's row k is pre-multiplied by the norm weight w[k], and
+   * row_scale holds each row's rsqrt(mean(x^2) + eps) (fab_rmsnorm_rstd).
+   * Such GEMMs are never split over K.  No counterpart in the reference,
+   * which runs the norm as its own PyTorch op (ttft.py forward).
+   */
+  const float* row_scale;
 } fab_gemm_params;
 
 /*
@@ -331,6 +341,10 @@ int fab_ipc_close(void* base);
  * fab_rmsnorm: h = w * round(x' * rsqrt(mean(x'^2) + eps)) per row, where
  *   x' = x, or round(x + residual) (written to x_out, which may alias x) when
  *   residual is not NULL.  cols a multiple of 8, at most 8192.
+ * fab_rmsnorm_rstd: the first half of fab_rmsnorm for a GEMM with the norm
+ *   folded into it (fab_gemm_params.row_scale): x' as above (written to
+ *   x_out when residual is not NULL), and rstd[row] = rsqrt(mean(x'^2) + eps)
+ *   in fp32; h is not formed.
  * fab_bias_rope: in place on y [rows, heads, head_dim] (row stride ld): adds
  *   bias [heads * head_dim] (may be NULL) to every head, then applies
  *   rotate-half rotary embedding (cos/sin [rows, head_dim]) to the first
@@ -341,6 +355,8 @@ int fab_ipc_close(void* base);
  */
 int fab_rmsnorm(const void* x, const void* residual, const void* w, void* h, void* x_out, int rows, int cols,
                 int64_t ld_x, int64_t ld_res, int64_t ld_h, int64_t ld_xo, float eps, int dtype, void* stream);
+int fab_rmsnorm_rstd(const void* x, const void* residual, void* x_out, float* rstd, int rows, int cols, int64_t ld_x,
+                     int64_t ld_res, int64_t ld_xo, float eps, int dtype, void* stream);
 int fab_bias_rope(void* y, const void* bias, const void* cos, const void* sin, int rows, int heads, int rot_heads,
                   int head_dim, int64_t ld, int dtype, void* stream);
 int fab_silu_mul(const void* gu, void* a, int rows, int m, int64_t ld_gu, int64_t ld_a, int interleave, int dtype,

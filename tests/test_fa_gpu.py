@@ -379,9 +379,10 @@ def test_two_ctas_per_sm_kernel_matches_oracle(case, cuda_device):
 
 
 def test_measured_choice_takes_two_ctas_per_sm_for_short_causal(cuda_device):
-    """attention_forward's measured family choice for BASELINE config 2 causal S1024/S2048 and the TTFT
-    prefill is the two-CTAs-per-SM kernel, so the parity cases above cover what those calls run."""
-    for B, Hq, Hkv, S in ((4, 32, 32, 1024), (4, 32, 32, 2048), (1, 28, 4, 2048)):
+    """attention_forward's measured family choice for BASELINE config 2 causal S1024/S2048 is the
+    two-CTAs-per-SM kernel, so the parity cases above cover what those calls run.  (The TTFT prefill's
+    28 heads at 2048 take the two-tile kernel; the forced-variant case above covers the other.)"""
+    for B, Hq, Hkv, S in ((4, 32, 32, 1024), (4, 32, 32, 2048)):
         q = torch.empty(B, Hq, S, 128, device=cuda_device, dtype=torch.bfloat16)
         kv = torch.empty(B, Hkv, S, 128, device=cuda_device, dtype=torch.bfloat16)
         plan = flash_atten.attention_plan(q, kv, kv, causal=True)
