@@ -509,7 +509,7 @@ def run_decode(args, world, rank, local):
     v = torch.randn(B, Hkv, N, D, generator=g, device=dev, dtype=dtype)
     o = torch.empty_like(q)
     need, splits = splitkv_workspace_bytes(tuple(q.shape), tuple(k.shape), dtype)
-    ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+    ws = torch.zeros(max(need, 256), device=dev, dtype=torch.uint8)  # counters start at zero
     kv_bytes = 2 * k.numel() * k.element_size()
     algo_bytes = kv_bytes + 2 * q.numel() * q.element_size()  # K, V read once; q read, o written
     stream = torch.cuda.current_stream(dev)

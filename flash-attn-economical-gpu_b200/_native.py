@@ -30,6 +30,7 @@ FAB_GEMM_EPILOGUE_BIAS_ROPE = 2
 FAB_GEMM_KERNEL_SINGLE = 0
 FAB_GEMM_KERNEL_PAIR = 1
 FAB_GEMM_KERNEL_SPLITK = 2
+FAB_GEMM_KERNEL_PAIR_STREAMK = 3
 
 FAB_DTYPE_F16 = 0
 FAB_DTYPE_BF16 = 1
@@ -70,7 +71,7 @@ class FabGemmParams(ctypes.Structure):
         ("M", _i32), ("N", _i32), ("K", _i32),
         ("in_dtype", _i32), ("out_dtype", _i32), ("round_f16", _i32), ("group_m", _i32), ("epilogue", _i32),
         ("bias", _vp), ("rope_cos", _vp), ("rope_sin", _vp), ("rope_cols", _i32), ("head_dim", _i32),
-        ("row_scale", _vp),
+        ("row_scale", _vp), ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -145,6 +146,8 @@ PROTOTYPES = {
     "fab_gemm": (_i32, [ctypes.POINTER(FabGemmParams), _vp]),
     "fab_gemm_plan": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
                              ctypes.POINTER(_i32)]),
+    "fab_gemm_workspace_size": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(ctypes.c_size_t)]),
+    "fab_gemm_grid": (_i32, [ctypes.POINTER(FabGemmParams), ctypes.POINTER(ctypes.c_longlong)]),
     "fab_gemm_allreduce_layout": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_size_t),
                                          ctypes.POINTER(ctypes.c_size_t)]),
     "fab_gemm_allreduce": (_i32, [ctypes.POINTER(FabGemmAllreduceParams), _vp]),

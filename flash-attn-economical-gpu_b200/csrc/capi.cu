@@ -510,6 +510,7 @@ int fab_attention_fwd_splitkv(const fab_attention_params* p, int num_splits, voi
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     L.o_part = reinterpret_cast<float*>(ws);
     L.lse_part = reinterpret_cast<float*>(ws + plan.lse_offset);
+    L.split_cnt = reinterpret_cast<unsigned int*>(ws + plan.counter_offset);
   }
   return fa_forward_split(L, static_cast<cudaStream_t>(stream));
 }
@@ -524,11 +525,17 @@ int fab_attention_fwd_splitkv_static(const fab_attention_params* p, int num_spli
     if (plan.workspace_bytes > kStaticScratchBytes) return kErrWorkspace;
     uint8_t* ws = static_cast<uint8_t*>(static_scratch_address(current_device()));
     if (ws == nullptr) return kErrCuda;
-    // Nothing in the scratch has to start at zero: every split writes all of
-    // its partial rows (an empty split writes zeros and LSE -inf) before the
-    // merge kernel, launched after it on the same stream, reads them.
+    // Every split writes all of its partial rows (an empty split writes
+    // zeros and LSE -inf) before the group's last CTA merges them.  The row
+    // groups' arrival counters must start at zero: they are cleared here, on
+    // the call's stream, since an earlier call that gave up on a bounded wait
+    // may have left them counted.
     L.o_part = reinterpret_cast<float*>(ws);
     L.lse_part = reinterpret_cast<float*>(ws + plan.lse_offset);
+    L.split_cnt = reinterpret_cast<unsigned int*>(ws + plan.counter_offset);
+    if (cudaMemsetAsync(L.split_cnt, 0, sizeof(unsigned int) * plan.groups, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess)
+      return kErrCuda;
   }
   return fa_forward_split(L, static_cast<cudaStream_t>(stream));
 }
@@ -587,6 +594,8 @@ static int gemm_validate(const fab_gemm_params* p, GemmLaunch* out, bool* nothin
   L.group_m = p->group_m;
   L.swiglu = swiglu ? 1 : 0;
   L.row_scale = p->row_scale;
+  L.workspace = p->workspace;
+  L.workspace_bytes = p->workspace_bytes;
   if (rope) {
     L.bias_rope = 1;
     L.rope_cols = p->rope_cols;
@@ -617,6 +626,28 @@ int fab_gemm(const fab_gemm_params* p, void* stream) {
     return kOk;
   }
   return gemm_forward(L, static_cast<cudaStream_t>(stream));
+}
+
+int fab_gemm_workspace_size(const fab_gemm_params* p, size_t* bytes) {
+  if (bytes == nullptr) return kErrInvalidArg;
+  *bytes = 0;
+  GemmLaunch L;
+  bool nothing, empty_k;
+  const int rc = gemm_validate(p, &L, &nothing, &empty_k);
+  if (rc || nothing || empty_k) return rc;
+  *bytes = gemm_workspace_bytes(L);
+  return kOk;
+}
+
+int fab_gemm_grid(const fab_gemm_params* p, long long* ctas) {
+  if (ctas == nullptr) return kErrInvalidArg;
+  *ctas = 0;
+  GemmLaunch L;
+  bool nothing, empty_k;
+  const int rc = gemm_validate(p, &L, &nothing, &empty_k);
+  if (rc || nothing || empty_k) return rc;
+  *ctas = gemm_grid_ctas(L);
+  return kOk;
 }
 
 int fab_gemm_plan(const fab_gemm_params* p, int* kernel, int* k_split, int* tile_n) {

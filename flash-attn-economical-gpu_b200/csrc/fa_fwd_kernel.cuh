@@ -93,6 +93,7 @@ struct FaCfg {
   // The ring holds tiles in the order the MMA thread uses them, so at most
   // V_j and K_{j+2} (two S buffers) or V_j and K_{j+1} (one) are held at once.
   static_assert(kRing >= 2, "K/V ring too short");
+  // After the barriers: the TMEM address, the abort flag, the split-merge flag.
   static constexpr int kSmemBytes = 1024 + kDataBytes + kNumBars * 8 + 16;
   static_assert(kDP % kAtom == 0, "head dim must fill whole swizzle atoms");
   static_assert(kTmemUsed <= 512, "TMEM budget");
@@ -185,6 +186,75 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
         if (e < ncols) dst[e] = v[e];
     }
   }
+}
+
+// The key splits of one row group (the CTAs blockIdx.x of every blockIdx.y)
+// each leave their rows' normalised O and LSE in o_part / lse_part.  Every
+// CTA counts itself in split_cnt[blockIdx.x] once its 128 softmax threads
+// have stored; the last to arrive merges the group's rows:
+// O = sum_s w_s O_s / sum_s w_s and LSE = max + log(sum_s w_s), with
+// w_s = exp(LSE_s - max) (zero for an empty split), one warp per row and the
+// head dim across the lanes, and sets the counter back to zero for the next
+// call.  Called by the four softmax warps of a one-query-tile CTA on every
+// path (the named barrier has no time limit).
+template <typename T>
+__device__ __forceinline__ void split_merge(const FaKernelParams& p, int m0, int b, int h, int wq, int lane,
+                                            uint32_t* merge_flag) {
+  __threadfence();  // this thread's partial row, visible GPU-wide before the count
+  named_barrier_sync(1, 128);
+  if (wq == 0 && lane == 0) {
+    const unsigned int prev = atomicAdd(p.split_cnt + blockIdx.x, 1u);
+    *reinterpret_cast<volatile uint32_t*>(merge_flag) = prev + 1 == gridDim.y ? 1u : 0u;
+  }
+  named_barrier_sync(1, 128);
+  if (*reinterpret_cast<volatile uint32_t*>(merge_flag) == 0) return;
+  __threadfence();
+  constexpr int kMaxPerLane = 8;  // head dims up to 256
+  const int splits = static_cast<int>(gridDim.y);
+  const int64_t split_rows = static_cast<int64_t>(p.B) * p.Hq * p.Mq;
+  for (int rr = wq; rr < 128; rr += 4) {
+    const int row = m0 + rr;
+    if (row >= p.M) break;
+    const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
+    const int qpos = p.pack_gqa ? row % p.Mq : row;
+    const int64_t r0 = static_cast<int64_t>(b) * p.Hq * p.Mq + static_cast<int64_t>(oh) * p.Mq + qpos;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm;
+    float* lse = p.lse != nullptr ? p.lse + b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm : nullptr;
+    float mx = -INFINITY;
+    for (int sp = lane; sp < splits; sp += 32) mx = fmaxf(mx, __ldcg(p.lse_part + sp * split_rows + r0));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (mx == -INFINITY) {
+      // No split saw a key: 0/0 like the single-pass kernel.
+      for (int d = lane; d < p.D; d += 32) orow[d] = static_cast<T>(NAN);
+      if (lse != nullptr && lane == 0) *lse = -INFINITY;
+      continue;
+    }
+    float acc[kMaxPerLane];
+#pragma unroll
+    for (int e = 0; e < kMaxPerLane; ++e) acc[e] = 0.f;
+    float wsum = 0.f;
+#pragma unroll 4
+    for (int sp = 0; sp < splits; ++sp) {
+      const float ls = __ldcg(p.lse_part + sp * split_rows + r0);
+      const float w = ls == -INFINITY ? 0.f : expf(ls - mx);  // an empty split carries zeros
+      wsum += w;
+      const float* src = p.o_part + (sp * split_rows + r0) * p.D;
+#pragma unroll
+      for (int e = 0; e < kMaxPerLane; ++e) {
+        const int d = lane + 32 * e;
+        if (d < p.D) acc[e] = fmaf(w, __ldcg(src + d), acc[e]);
+      }
+    }
+    const float inv = 1.f / wsum;
+#pragma unroll
+    for (int e = 0; e < kMaxPerLane; ++e) {
+      const int d = lane + 32 * e;
+      if (d < p.D) orow[d] = static_cast<T>(acc[e] * inv);
+    }
+    if (lse != nullptr && lane == 0) *lse = mx + logf(wsum);
+  }
+  if (wq == 0 && lane == 0) p.split_cnt[blockIdx.x] = 0u;
 }
 
 template <typename T, int kDP, int kNQ, int kBN, int kRing, int kSB>
@@ -729,6 +799,9 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
       }
       if (lse_out != nullptr) *lse_out = kNegInf;
     }
+    if constexpr (kNQ == 1) {
+      if (p.split_cnt != nullptr) split_merge<T>(p, m0, b, h, wq, lane, tmem_slot + 2);
+    }
   }
   }
 
@@ -822,6 +895,7 @@ static int launch_fa(const FaLaunch& L, cudaStream_t stream) {
   kp.Mq = L.M;
   kp.o_part = L.o_part;
   kp.lse_part = L.lse_part;
+  kp.split_cnt = L.o_part != nullptr ? L.split_cnt : nullptr;
   kp.cu_q = L.cu_q;
   kp.cu_k = L.cu_k;
   // O through TMA tensor stores where the map allows it (dense, one query
@@ -1150,9 +1224,12 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
   plan->rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
   plan->workspace_bytes = 0;
   plan->lse_offset = 0;
+  plan->counter_offset = 0;
+  plan->groups = base_ctas;
   if (plan->num_splits > 1) {
     plan->lse_offset = align256(sizeof(float) * plan->num_splits * plan->rows * L.D);
-    plan->workspace_bytes = plan->lse_offset + align256(sizeof(float) * plan->num_splits * plan->rows);
+    plan->counter_offset = plan->lse_offset + align256(sizeof(float) * plan->num_splits * plan->rows);
+    plan->workspace_bytes = plan->counter_offset + align256(sizeof(unsigned int) * base_ctas);
   }
   return 0;
 }
@@ -1167,7 +1244,8 @@ int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
   if (elt == E && c.d_pad == DP) rc = launch_entry<E, DP, NQ, BN, ST, SB>(L, stream);
   FAB_FA_SPLIT_TABLE(FAB_FA_SLAUNCH)
 #undef FAB_FA_SLAUNCH
-  if (rc || L.num_splits <= 1 || L.o_part == nullptr) return rc;
+  // Merged inside the split kernel when the launch carries the counters.
+  if (rc || L.num_splits <= 1 || L.o_part == nullptr || L.split_cnt != nullptr) return rc;
   const int64_t rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
   const long long blocks = rows;  // one CTA per output row
   if (blocks > 0x7fffffffLL) return kErrInvalidArg;

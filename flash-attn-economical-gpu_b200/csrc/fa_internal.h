@@ -46,6 +46,10 @@ struct FaKernelParams {
   // [split][B][Hq][Mq][D]) and LSE ([split][B][Hq][Mq]) here instead of o/lse.
   float* o_part;
   float* lse_part;
+  // With key splits: one counter per row group (blockIdx.x), zero between
+  // calls.  The last split CTA of a group to finish merges the group's
+  // partials into o / lse and sets the counter back to zero.
+  unsigned int* split_cnt;
   // Packed variable-length batches: sequence b's query rows are
   // [cu_q[b], cu_q[b+1]) of a [total, heads, D] tensor (keys likewise with
   // cu_k); M and N are then the longest lengths.  NULL for dense batches.
@@ -78,6 +82,7 @@ struct FaLaunch {
   int pack_gqa;
   float* o_part;
   float* lse_part;
+  unsigned int* split_cnt;  // see FaKernelParams
   // Packed variable-length batches (see FaKernelParams); the tensor maps
   // then span total_q / total_k rows with batch extent 1.
   const int* cu_q;
@@ -92,8 +97,10 @@ struct FaSplitPlan {
   int split_len;
   int pack_gqa;
   int64_t rows;            // B * Hq * M output rows
-  size_t workspace_bytes;  // o_part then lse_part, each 256-byte aligned
+  size_t workspace_bytes;  // o_part, lse_part, then the row groups' counters, each 256-byte aligned
   size_t lse_offset;       // byte offset of lse_part in the workspace
+  size_t counter_offset;   // byte offset of the counters (which start at zero)
+  int64_t groups;          // row groups (CTAs per key split): one counter each
 };
 
 struct FaConfigInfo {
@@ -129,6 +136,15 @@ struct GemmKernelParams {
   // before any epilogue rounding (an RMSNorm's 1/rms folded into the GEMM
   // that consumes the normalised rows; its weight is folded into B).
   const float* row_scale;
+  // Stream-K schedule of the CTA-pair kernel (plain store epilogue only):
+  // tiles [0, sk_dp_tiles) run whole, round robin over the pairs; the K
+  // blocks of the remaining tiles are split evenly over all pairs, and each
+  // such tile is finished by the pair holding its last K block (its owner),
+  // which adds the partial sums the other pairs left in sk_part.
+  // sk_part == nullptr turns stream-K off.
+  int sk_dp_tiles;
+  float* sk_part;  // [pairs][2 CTAs][kBN / 4][128 rows] float4: one partial tile per pair and CTA
+  int* sk_flags;   // [pairs][2 CTAs][4 epilogue warps]; zero between calls
 };
 
 // Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output
@@ -163,6 +179,8 @@ struct GemmLaunch {
   const void* rope_cos;
   const void* rope_sin;
   const float* row_scale;  // see GemmKernelParams
+  void* workspace;         // stream-K partial tiles and flags, or null
+  size_t workspace_bytes;
 };
 
 // Epilogues that need whole 256-column tiles (gate/up block pairs, whole heads).
@@ -190,6 +208,10 @@ int fa_forward_split(const FaLaunch& L, cudaStream_t stream);
 int fa_kernel_attrs(int dtype, int D, int* regs, int* smem, int* threads, bool one_tile = false);
 int gemm_forward(const GemmLaunch& L, cudaStream_t stream);
 int gemm_plan(const GemmLaunch& L, int* kernel, int* split, int* tile_n);
+// Workspace the stream-K schedule would use for L (0 when it is not chosen).
+size_t gemm_workspace_bytes(const GemmLaunch& L);
+// CTAs in the grid gemm_forward would launch for L.
+long long gemm_grid_ctas(const GemmLaunch& L);
 // Output tiles of the fused GEMM + all-reduce: tile t belongs to rank t % world.
 int gemm_ar_tiles(int M, int N);
 int gemm_allreduce(const GemmLaunch& L, const GemmArParams& ar, cudaStream_t stream);

@@ -715,6 +715,9 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   kp.rope_cos = L.rope_cos;
   kp.rope_sin = L.rope_sin;
   kp.row_scale = L.row_scale;
+  kp.sk_dp_tiles = 0;  // stream-K is the CTA-pair kernel's
+  kp.sk_part = nullptr;
+  kp.sk_flags = nullptr;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   int sms = num_sms();
@@ -780,7 +783,8 @@ static int gemm_single_width(const GemmLaunch& L) {
 }
 
 // Which kernel gemm_forward runs for L: 0 single CTA per tile (*tile_n wide),
-// 1 CTA pairs, 2 split K over a cluster of *split CTAs per tile.
+// 1 CTA pairs (*tile_n wide tiles), 2 split K over a cluster of *split CTAs
+// per tile, 3 CTA pairs with the stream-K schedule (L carries a workspace).
 int gemm_plan(const GemmLaunch& L, int* kernel, int* split, int* tile_n) {
   *kernel = 0;
   *split = 1;
@@ -796,11 +800,33 @@ int gemm_plan(const GemmLaunch& L, int* kernel, int* split, int* tile_n) {
     }
   }
 #endif
-  if (gemm_use_pair(L))
-    *kernel = 1;
-  else
+  if (gemm_use_pair(L)) {
+    const PairChoice c = gemm_pair_layout_any(L);
+    *kernel = c.stream_k ? 3 : 1;
+    *tile_n = c.bn;
+  } else {
     *tile_n = gemm_single_width(L);
+  }
   return 0;
+}
+
+size_t gemm_workspace_bytes(const GemmLaunch& L) {
+  int kernel = 0, split = 1, tile_n = 256;
+  if (L.M <= 0 || L.N <= 0 || L.K <= 0) return 0;
+  gemm_plan(L, &kernel, &split, &tile_n);
+  if (kernel == 2 || !gemm_use_pair(L)) return 0;
+  return gemm_pair_workspace(L);
+}
+
+long long gemm_grid_ctas(const GemmLaunch& L) {
+  int kernel = 0, split = 1, tile_n = 256;
+  if (L.M <= 0 || L.N <= 0 || L.K <= 0) return 0;
+  gemm_plan(L, &kernel, &split, &tile_n);
+  const int sms = num_sms();
+  if (kernel == 2) return static_cast<long long>((L.M + 127) / 128) * ((L.N + 255) / 256) * split;
+  if (kernel == 1 || kernel == 3) return 2LL * gemm_pair_layout_any(L).pairs;
+  const long long tiles = static_cast<long long>((L.M + 127) / 128) * ((L.N + tile_n - 1) / tile_n);
+  return tiles < sms ? tiles : sms;
 }
 
 template <typename Tin, typename Tout>

@@ -59,6 +59,122 @@ struct GemmPairCfg {
   static_assert(kBN % 32 == 0 && kBN <= kAccStride && kBNc % 16 == 0, "tile width");
 };
 
+// ---------------------------------------------------------------- stream-K
+// With T tiles on P pairs, T % P tiles would leave most pairs idle in the
+// last wave.  Stream-K runs the first P * (T / P) tiles whole, round robin,
+// and cuts the K blocks of the remaining tiles into P equal ranges, one per
+// pair.  A tile cut this way is finished by its owner, the pair whose range
+// holds its last K block: the other pairs' pieces of it (partial fp32 sums)
+// wait in their workspace slots, and the owner adds them in pair order
+// (deterministic) before its epilogue.  A range is at most one tile long, so
+// a pair has at most one piece for another pair's tile; it computes that
+// piece first, so every owner finds its pieces computed at the start of the
+// stream-K phase.  No piece waits for anything, and all pairs are resident,
+// so an owner's wait always ends.
+enum PairItemKind : int { kItemFull = 0, kItemPart = 1, kItemOwner = 2 };
+
+struct PairItem {
+  int tile, kb0, kb1, kind;  // K blocks [kb0, kb1) of the tile
+};
+
+struct PairSched {
+  int num_pairs, nkb, dp_tiles;
+  long long sk_blocks;  // K blocks of the tiles after dp_tiles (0: stream-K off)
+  __host__ __device__ long long begin(int pair) const { return sk_blocks * pair / num_pairs; }
+};
+
+// Item i of a pair's work (false past the last): its whole tiles, then its
+// piece for another pair's tile, then its own (owned or whole) tile.
+__host__ __device__ inline bool pair_item(const PairSched& S, int pair, int i, PairItem* out) {
+  const int ndp = pair < S.dp_tiles ? (S.dp_tiles - 1 - pair) / S.num_pairs + 1 : 0;
+  if (i < ndp) {
+    *out = PairItem{pair + i * S.num_pairs, 0, S.nkb, kItemFull};
+    return true;
+  }
+  i -= ndp;
+  const long long s = S.begin(pair), e = S.begin(pair + 1);
+  if (s >= e || i > 1) return false;
+  const long long nkb = S.nkb;
+  const int ts = static_cast<int>(s / nkb), te = static_cast<int>((e - 1) / nkb);
+  PairItem a;
+  a.tile = S.dp_tiles + ts;
+  a.kb0 = static_cast<int>(s - ts * nkb);
+  a.kb1 = static_cast<int>((e < (ts + 1) * nkb ? e : (ts + 1) * nkb) - ts * nkb);
+  a.kind = a.kb1 < S.nkb ? kItemPart : (a.kb0 == 0 ? kItemFull : kItemOwner);
+  if (te == ts) {
+    if (i != 0) return false;
+    *out = a;
+    return true;
+  }
+  PairItem b;
+  b.tile = S.dp_tiles + te;
+  b.kb0 = 0;
+  b.kb1 = static_cast<int>(e - te * nkb);
+  b.kind = b.kb1 < S.nkb ? kItemPart : kItemFull;
+  *out = i == 0 ? b : a;
+  return true;
+}
+
+// The pairs whose pieces the owner of `tile` adds: [first, owner).
+__host__ __device__ inline int pair_first_piece(const PairSched& S, int owner, int tile) {
+  const long long start = static_cast<long long>(tile - S.dp_tiles) * S.nkb;
+  int q = owner;
+  while (q > 0 && S.begin(q) > start) --q;
+  return q;
+}
+
+// Float4 index of (16-byte column group g, row r) in one CTA's partial tile:
+// group-major, so a warp's 32 rows are 512 contiguous bytes.
+__device__ __forceinline__ int part_index(int g, int r) { return g * 128 + r; }
+
+// A piece's epilogue: the raw fp32 accumulator row into this pair's slot.
+template <int kWidth>
+__device__ __forceinline__ void store_partial_row(uint32_t acc, float4* slab, int r) {
+#pragma unroll 1
+  for (int cc = 0; cc < kWidth / 32; ++cc) {
+    uint32_t v[32];
+    tmem_ld32(acc + cc * 32, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      __stcg(slab + part_index(cc * 8 + q, r), make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                                           __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
+  }
+}
+
+// An owner's epilogue (plain store): accumulator + the pieces of pairs
+// [first, owner) in pair order, times the row scale, stored as C's type.
+template <typename Tout, int kWidth>
+__device__ __forceinline__ void store_owned_row(const GemmKernelParams& p, uint32_t acc, int row, int n0,
+                                                const float4* part0, int64_t part_stride, int npart, int r) {
+  const float rs = (p.row_scale != nullptr && row < p.M) ? p.row_scale[row] : 1.0f;
+  Tout* crow = reinterpret_cast<Tout*>(p.c) + static_cast<int64_t>(row) * p.ldc + n0;
+#pragma unroll 1
+  for (int cc = 0; cc < kWidth / 32; ++cc) {
+    uint32_t rr[32];
+    tmem_ld32(acc + cc * 32, rr);
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rr[e]);
+    for (int j = 0; j < npart; ++j) {
+      const float4* src = part0 + j * part_stride;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 x = __ldcg(src + part_index(cc * 8 + q, r));
+        v[4 * q] += x.x;
+        v[4 * q + 1] += x.y;
+        v[4 * q + 2] += x.z;
+        v[4 * q + 3] += x.w;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] *= rs;
+    const int ncols = min(32, p.N - n0 - cc * 32);
+    if (row < p.M && ncols > 0) gemm_store_chunk<Tout>(crow + cc * 32, v, ncols, p.round_f16 != 0);
+  }
+}
+
 template <typename Tin, typename Tout, int kBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_pair_kernel(const __grid_constant__ GemmKernelParams p, const __grid_constant__ CUtensorMap tm_a,
@@ -87,6 +203,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const int num_pid_n = (p.N + C::kBN - 1) / C::kBN;
   const int num_tiles = num_pid_m * num_pid_n;
   const int nkb = (p.K + C::kBK - 1) / C::kBK;
+  PairSched sched;
+  sched.num_pairs = num_pairs;
+  sched.nkb = nkb;
+  sched.dp_tiles = p.sk_part != nullptr ? p.sk_dp_tiles : num_tiles;
+  sched.sk_blocks = static_cast<long long>(num_tiles - sched.dp_tiles) * nkb;
+  if (sched.sk_blocks < num_pairs) {
+    // An empty range would leave a gap in an owner's run of pieces: whole tiles.
+    sched.dp_tiles = num_tiles;
+    sched.sk_blocks = 0;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -119,12 +245,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     tma_prefetch_desc(&tm_b);
     int it = 0;
     bool ok = true;
-    for (int t = pair; ok && t < num_tiles; t += num_pairs) {
+    PairItem w;
+    for (int i = 0; ok && pair_item(sched, pair, i, &w); ++i) {
       int pm, pn;
-      gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+      gemm_tile_coords(w.tile, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
       const int m0 = pm * C::kBM + static_cast<int>(rank) * C::kBMc;
       const int n0 = pn * C::kBN + static_cast<int>(rank) * C::kBNc;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!(ok = mbar_wait(bar_empty + s, ph ^ 1, abort_flag, kDevTimeoutEmpty))) break;
@@ -152,13 +279,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     constexpr uint16_t kBoth = 0x3;
     int it = 0, tcount = 0;
     bool ok = true;
-    for (int t = pair; ok && t < num_tiles; t += num_pairs, ++tcount) {
+    PairItem w;
+    for (int i = 0; ok && pair_item(sched, pair, i, &w); ++i, ++tcount) {
       const int buf = tcount & 1;
       const uint32_t use = tcount >> 1;
       if (!(ok = mbar_wait(bar_acc_empty + buf, (use & 1) ^ 1, abort_flag, kDevTimeoutAcc))) break;
       tc_fence_after();
       const uint32_t d = tmem + buf * C::kAccStride;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (!(ok = mbar_wait(bar_full + s, ph, abort_flag, kDevTimeoutKV))) break;
@@ -170,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         for (int kk = 0; kk < C::kBK / C::kKInstr; ++kk) {
           const uint64_t ad = umma_desc_join(a_lo + ((kk * 32) >> 4), kHiA);
           const uint64_t bd = umma_desc_join(b_lo + ((kk * C::kKInstr * 128) >> 4), kHiB);
-          mma_ss_f16_pair(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_ss_f16_pair(d, ad, bd, idesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
         }
         mma_commit_pair(bar_empty + s, kBoth);
       }
@@ -182,16 +310,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+    // One partial tile per pair and CTA: kBN / 4 16-byte groups x 128 rows.
+    constexpr int64_t kSlab = static_cast<int64_t>(C::kBN / 4) * 128;
     int tcount = 0;
-    for (int t = pair; t < num_tiles; t += num_pairs, ++tcount) {
+    PairItem w;
+    for (int i = 0; pair_item(sched, pair, i, &w); ++i, ++tcount) {
       const int buf = tcount & 1;
       const uint32_t use = tcount >> 1;
       if (!mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc)) break;
       tc_fence_after();
       int pm, pn;
-      gemm_tile_coords(t, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
-      gemm_store_tile_row<Tout, kBN>(p, tmem + lane_base + buf * C::kAccStride,
-                                     pm * C::kBM + static_cast<int>(rank) * C::kBMc + r, pn * C::kBN);
+      gemm_tile_coords(w.tile, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
+      const uint32_t acc = tmem + lane_base + buf * C::kAccStride;
+      const int row = pm * C::kBM + static_cast<int>(rank) * C::kBMc + r;
+      if (w.kind == kItemFull) {
+        gemm_store_tile_row<Tout, kBN>(p, acc, row, pn * C::kBN);
+      } else if (w.kind == kItemPart) {
+        // This pair's slot: every lane's row, then one flag per warp, set
+        // after all 32 rows are visible at GPU scope.
+        float4* slab = reinterpret_cast<float4*>(p.sk_part) + (static_cast<int64_t>(pair) * 2 + rank) * kSlab;
+        store_partial_row<kBN>(acc, slab, r);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(p.sk_flags + (pair * 2 + static_cast<int>(rank)) * 4 + wq, 1);
+      } else {
+        // Owner: wait (bounded) for every piece of this tile, add them in
+        // pair order, store, and clear the pieces' flags for the next call.
+        const int first = pair_first_piece(sched, pair, w.tile);
+        bool got = true;
+        if (lane == 0)
+          for (int q = first; got && q < pair; ++q)
+            got = wait_flag_set(p.sk_flags + (q * 2 + static_cast<int>(rank)) * 4 + wq, abort_flag,
+                                kDevTimeoutPartial);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (got) {
+          const float4* part0 =
+              reinterpret_cast<const float4*>(p.sk_part) + (static_cast<int64_t>(first) * 2 + rank) * kSlab;
+          store_owned_row<Tout, kBN>(p, acc, row, pn * C::kBN, part0, 2 * kSlab, pair - first, r);
+          __syncwarp();
+          if (lane == 0)
+            for (int q = first; q < pair; ++q) p.sk_flags[(q * 2 + static_cast<int>(rank)) * 4 + wq] = 0;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(bar_acc_empty + buf), 0));  // rank 0's
@@ -221,9 +381,111 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   }
 }
 
-// Pair tiles (256 x kBN) in a grid of up to one pair per two SMs.
+// Resident clusters (pairs) of one launch of the kBN-wide kernel: an owner
+// waits for other pairs' pieces, so a stream-K grid never exceeds this.
 template <typename Tin, typename Tout, int kBN>
-static int launch_gemm_pair_w(const GemmLaunch& L, cudaStream_t stream) {
+static int gemm_pair_capacity() {
+  using C = GemmPairCfg<kBN>;
+  static int cached = -1;
+  if (cached >= 0) return cached;
+  auto kern = gemm_pair_kernel<Tin, Tout, kBN>;
+  if (ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes)) return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * 64);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cached = n;
+  return n;
+}
+
+// How a CTA-pair GEMM is laid out: tile width, pairs in the grid and the
+// tiles run whole (all of them without stream-K).
+struct PairChoice {
+  int bn;
+  int pairs;
+  int dp_tiles;
+  int tiles;
+  bool stream_k;
+};
+
+static long long pair_tiles(const GemmLaunch& L, int bn) {
+  return static_cast<long long>((L.M + 255) / 256) * ((L.N + bn - 1) / bn);
+}
+
+// Stream-K workspace of a layout: one flag word per pair, CTA and epilogue
+// warp (a 256-byte aligned block), then one fp32 partial tile per pair and CTA.
+static size_t pair_sk_flag_bytes(int pairs) { return (static_cast<size_t>(pairs) * 8 * sizeof(int) + 255) / 256 * 256; }
+static size_t pair_sk_bytes(const PairChoice& c) {
+  return c.stream_k ? pair_sk_flag_bytes(c.pairs) + static_cast<size_t>(c.pairs) * 2 * 128 * c.bn * sizeof(float) : 0;
+}
+
+// Whole-tile layout with the fewest idle pair-slots: tiles 256 wide, or 224
+// where that leaves fewer pairs idle in the last wave and K is short (a
+// 224-wide tile's B halves start off the 128-byte line, which costs L2
+// traffic in long main loops; measured on B200: N = 3584 gains 7 % at
+// K = 3584, loses 2-7 % at K = 18944).  The SwiGLU and bias + RoPE
+// epilogues need 256-wide tiles.
+static PairChoice gemm_pair_whole(const GemmLaunch& L, int half_sms) {
+  PairChoice best{256, 0, 0, 0, false};
+  double best_cost = 1e300;
+  for (int bn : {256, 224}) {
+    if (bn == 224 && (gemm_fixed_width(L) || L.K > 8192)) continue;
+    const long long tiles = pair_tiles(L, bn);
+    if (tiles <= 0 || half_sms <= 0) continue;
+    const int pairs = static_cast<int>(tiles < half_sms ? tiles : half_sms);
+    const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * bn;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = PairChoice{bn, pairs, static_cast<int>(tiles), static_cast<int>(tiles), false};
+    }
+  }
+  return best;
+}
+
+// The chosen layout.  Stream-K (256-wide tiles, plain store epilogue) is
+// taken when the tiles leave part of the last wave idle and the estimate --
+// tiles / pairs waves plus ~4 % for writing and adding the pieces -- beats
+// the best whole-tile layout; it also needs at least two K blocks per pair
+// and ranges of at least a quarter tile (so an owner adds a handful of
+// pieces at most), and a workspace from the caller (with_workspace).
+template <typename Tin, typename Tout>
+static PairChoice gemm_pair_choice(const GemmLaunch& L, bool with_workspace) {
+  const int half_sms = num_sms() / 2;
+  PairChoice best = gemm_pair_whole(L, half_sms);
+#ifndef FAB_GEMM_NO_STREAMK
+  if (!with_workspace || gemm_fixed_width(L) || best.pairs <= 0) return best;
+  const double whole_cost = static_cast<double>((best.tiles + best.pairs - 1) / best.pairs) * best.bn;
+  const long long tiles = pair_tiles(L, 256);
+  const int cap = gemm_pair_capacity<Tin, Tout, 256>();
+  const int P = cap < half_sms ? cap : half_sms;
+  const long long nkb = (L.K + 63) / 64;
+  if (P >= 1 && tiles > P && tiles % P != 0) {
+    const long long dp = tiles / P * P;
+    const long long sk_blocks = (tiles - dp) * nkb;
+    const double sk_cost = static_cast<double>(tiles) / P * 256 * 1.04;
+    if (sk_blocks >= 2LL * P && 4 * sk_blocks >= P * nkb && sk_cost < whole_cost)
+      best = PairChoice{256, P, static_cast<int>(dp), static_cast<int>(tiles), true};
+  }
+#endif
+  return best;
+}
+
+template <typename Tin, typename Tout>
+static PairChoice gemm_pair_layout(const GemmLaunch& L) {
+  PairChoice c = gemm_pair_choice<Tin, Tout>(L, true);
+  if (c.stream_k && (L.workspace == nullptr || (reinterpret_cast<uintptr_t>(L.workspace) & 255u) != 0 ||
+                     L.workspace_bytes < pair_sk_bytes(c)))
+    c = gemm_pair_whole(L, num_sms() / 2);
+  return c;
+}
+
+template <typename Tin, typename Tout, int kBN>
+static int launch_gemm_pair_w(const GemmLaunch& L, const PairChoice& c, cudaStream_t stream) {
   using C = GemmPairCfg<kBN>;
   auto kern = gemm_pair_kernel<Tin, Tout, kBN>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
@@ -251,33 +513,41 @@ static int launch_gemm_pair_w(const GemmLaunch& L, cudaStream_t stream) {
   kp.rope_cos = L.rope_cos;
   kp.rope_sin = L.rope_sin;
   kp.row_scale = L.row_scale;
-  const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
-  if (tiles <= 0) return 0;
-  const int sms = num_sms();
-  if (sms < 2) return kErrLaunch;
-  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
-  kern<<<2 * pairs, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
+  kp.sk_dp_tiles = c.tiles;
+  kp.sk_part = nullptr;
+  kp.sk_flags = nullptr;
+  if (c.tiles <= 0) return 0;
+  if (c.pairs < 1) return kErrLaunch;
+  if (c.stream_k) {
+    uint8_t* ws = static_cast<uint8_t*>(L.workspace);
+    kp.sk_dp_tiles = c.dp_tiles;
+    kp.sk_flags = reinterpret_cast<int*>(ws);
+    kp.sk_part = reinterpret_cast<float*>(ws + pair_sk_flag_bytes(c.pairs));
+  }
+  kern<<<2 * c.pairs, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
-}
-
-// Relative time of a pair-tile width: full waves of pairs times the work of
-// one tile (proportional to its width).
-static long long gemm_pair_cost(const GemmLaunch& L, int bn, int pairs) {
-  const long long tiles = static_cast<long long>((L.M + 255) / 256) * ((L.N + bn - 1) / bn);
-  return (tiles + pairs - 1) / pairs * bn;
 }
 
 template <typename Tin, typename Tout>
 static int launch_gemm_pair(const GemmLaunch& L, cudaStream_t stream) {
-  const int pairs = num_sms() / 2;
-  // 224-wide tiles only where they leave less of the last wave idle and K is
-  // short: a 224-wide tile's B halves start off the 128-byte line, which
-  // costs L2 traffic in long main loops (measured on B200: N = 3584 gains 7 %
-  // at K = 3584, loses 2-7 % at K = 18944).  The SwiGLU epilogue pairs
-  // 64-column gate/up blocks within 256-wide tiles.
-  if (!gemm_fixed_width(L) && pairs > 0 && L.K <= 8192 && gemm_pair_cost(L, 224, pairs) < gemm_pair_cost(L, 256, pairs))
-    return launch_gemm_pair_w<Tin, Tout, 224>(L, stream);
-  return launch_gemm_pair_w<Tin, Tout, 256>(L, stream);
+  const PairChoice c = gemm_pair_layout<Tin, Tout>(L);
+  if (c.bn == 224) return launch_gemm_pair_w<Tin, Tout, 224>(L, c, stream);
+  return launch_gemm_pair_w<Tin, Tout, 256>(L, c, stream);
+}
+
+// The layout the launch for L takes (the capacity query is per tile width,
+// the same for every output type).
+static PairChoice gemm_pair_layout_any(const GemmLaunch& L) {
+  return L.in_dtype == kDtypeBF16 ? gemm_pair_layout<__nv_bfloat16, __nv_bfloat16>(L)
+                                  : gemm_pair_layout<__half, __half>(L);
+}
+
+// Stream-K workspace bytes the launch for L would use with a workspace.
+static size_t gemm_pair_workspace(const GemmLaunch& L) {
+  if (L.in_dtype != kDtypeBF16 && L.in_dtype != kDtypeF16) return 0;
+  const PairChoice c = L.in_dtype == kDtypeBF16 ? gemm_pair_choice<__nv_bfloat16, __nv_bfloat16>(L, true)
+                                                : gemm_pair_choice<__half, __half>(L, true);
+  return pair_sk_bytes(c);
 }
 
 // The pair kernel serves 16-bit inputs when the problem fills at least one

@@ -258,6 +258,9 @@ static int launch_gemm_splitk_k(const GemmLaunch& L, cudaStream_t stream) {
   kp.head_dim = 0;
   kp.bias = kp.rope_cos = kp.rope_sin = nullptr;
   kp.row_scale = nullptr;
+  kp.sk_dp_tiles = 0;
+  kp.sk_part = nullptr;
+  kp.sk_flags = nullptr;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   kern<<<static_cast<unsigned>(tiles * kSplit), C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;

@@ -26,6 +26,7 @@ enum DeviceError : int {
   kDevTimeoutTeardown = 8,
   kDevTimeoutPeerTile = 9,   // a tile's partial sums from every rank never all arrived
   kDevTimeoutPeerDone = 10,  // the reduced tiles from every owner never all arrived
+  kDevTimeoutPartial = 11,   // a stream-K partial tile from another CTA pair never arrived
 };
 
 // Device-global status word of the kernels of one translation unit (internal
@@ -166,6 +167,39 @@ __device__ __forceinline__ bool wait_counter_at_least(const unsigned long long* 
     if ((++spins & 63u) == 0u) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------- flags within one GPU ---
+// A word in global memory that one warp sets after writing data and another
+// waits for before reading it (GPU scope: both on this device).
+__device__ __forceinline__ void st_release_gpu(int* addr, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Bounded spin until *flag != 0.  Returns false (after recording `code`) when
+// the limit passes or another thread of the CTA gave up.
+__device__ __forceinline__ bool wait_flag_set(const int* flag, volatile int* abort, int code) {
+  if (ld_acquire_gpu(flag) != 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    __nanosleep(32);
+    if (ld_acquire_gpu(flag) != 0) return true;
+    if ((++spins & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > g_fab_wait_limit_ns) {
         record_device_error(code);
         *abort = 1;
         return false;

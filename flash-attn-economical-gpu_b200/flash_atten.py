@@ -106,10 +106,11 @@ def _launch_attention(
 
     `entry` picks the C entry point: "basic" / "optimize_shared_mem" /
     "nomask" for the reference-named kernels, "splitkv"
-    (`fab_attention_fwd_splitkv`, key splits merged by a second kernel;
-    `num_splits` 0 = one CTA per SM) or "general" (`fab_attention_fwd`,
-    grouped-query heads) otherwise.  `workspace` (uint8, CUDA) is used for the
-    split partials when it is large enough, else one is allocated.
+    (`fab_attention_fwd_splitkv`, key splits merged by the last split CTA of
+    each row group; `num_splits` 0 = one CTA per SM) or "general"
+    (`fab_attention_fwd`, grouped-query heads) otherwise.  `workspace` (uint8,
+    CUDA, zero-filled before its first use; calls leave it zeroed) is used for
+    the split partials when it is large enough, else a zeroed one is allocated.
     `variant` 1 runs the one-query-tile family (`fab_attention_fwd_variant`)
     instead of the default table, whatever `entry` names.
 
@@ -186,7 +187,7 @@ def _launch_attention(
                     ctypes.byref(p), int(num_splits), ctypes.byref(need), None), what)
                 ws = workspace
                 if need.value and (ws is None or ws.numel() < need.value or ws.data_ptr() % 256):
-                    ws = torch.empty(need.value, device=q.device, dtype=torch.uint8)
+                    ws = torch.zeros(need.value, device=q.device, dtype=torch.uint8)
                 rc = _native.lib.fab_attention_fwd_splitkv(
                     ctypes.byref(p), int(num_splits), ws.data_ptr() if need.value else None, need.value, stream)
             else:
@@ -412,8 +413,10 @@ def attention_forward_splitkv(
     """attention_forward with the keys cut into `num_splits` ranges (flash-decoding).
 
     For short query blocks (decode steps, speculative blocks) against long
-    key ranges: each range is attended to by its own CTAs and a second kernel
-    merges the ranges by their LSE.  `num_splits` 0 gives one CTA per SM.
+    key ranges: each range is attended to by its own CTAs, and the last CTA of
+    each row group to finish merges the ranges by their LSE.  `num_splits` 0
+    gives one CTA per SM.  A caller-supplied `workspace` must be zero-filled
+    before its first use (every call leaves its counters at zero again).
     Query heads that share a key/value head are packed into one query tile
     when q is laid out [batch, head, seq, dim] contiguously (or seq == 1).
     """

@@ -63,13 +63,16 @@ def _gemm(
     epilogue: int = _native.FAB_GEMM_EPILOGUE_STORE,
     rope: tuple | None = None,
     row_scale: torch.Tensor | None = None,
+    workspace: torch.Tensor | bool | None = None,
     what: str = "gemm",
 ) -> None:
     """C[M,N] = A[M,K] B[K,N] over row-major storage with leading dims (elements).
 
     With the SwiGLU epilogue C is [M, N/2] (see `matmul_swiglu`); with the bias + RoPE epilogue `rope` is
     (bias or None, cos, sin, rope_cols, head_dim) (see `matmul_bias_rope`).  `row_scale` (fp32 [M] or None)
-    multiplies row r's accumulator by row_scale[r] before the epilogue (an RMSNorm folded into the GEMM)."""
+    multiplies row r's accumulator by row_scale[r] before the epilogue (an RMSNorm folded into the GEMM).
+    `workspace`: None uses the device's shared stream-K workspace when the layout wants one (`gemm_workspace`),
+    False runs whole tiles, a zero-filled uint8 CUDA tensor is used as given."""
     for name, t in (("a", a), ("b", b), ("c", c)):
         _require_cuda_tensor(name, t)
     if a.dtype != b.dtype:
@@ -94,12 +97,34 @@ def _gemm(
             raise ValueError(f"{what}: row_scale must be a contiguous float32 tensor of at least {M} elements")
         p.row_scale = row_scale.data_ptr()
     with torch.cuda.device(a.device):
+        if workspace is not False:
+            need = ctypes.c_size_t(0)
+            _native.check(_native.lib.fab_gemm_workspace_size(ctypes.byref(p), ctypes.byref(need)), what)
+            if need.value:
+                ws = gemm_workspace(a.device, need.value) if workspace is None else workspace
+                p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
         rc = _native.lib.fab_gemm(ctypes.byref(p), ctypes.c_void_p(_native.current_stream_handle(a.device)))
     _native.check(rc, what)
 
 
 _KERNEL_NAMES = {_native.FAB_GEMM_KERNEL_SINGLE: "single", _native.FAB_GEMM_KERNEL_PAIR: "pair",
-                 _native.FAB_GEMM_KERNEL_SPLITK: "splitk"}
+                 _native.FAB_GEMM_KERNEL_SPLITK: "splitk", _native.FAB_GEMM_KERNEL_PAIR_STREAMK: "pair_streamk"}
+
+# Stream-K workspaces, one per device, grown on demand and zero-filled when made (the kernel leaves its flag
+# words zero again).  Calls on one device share it, so they must be ordered (one stream, or graph replays of
+# one stream); callers that overlap GEMMs pass their own `workspace`.
+_WORKSPACES: dict[int, torch.Tensor] = {}
+
+
+def gemm_workspace(device, nbytes: int) -> torch.Tensor:
+    """The device's shared stream-K workspace, at least `nbytes` long (uint8, 256-byte aligned, zeroed)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _WORKSPACES[idx] = ws
+    return ws
 
 
 def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
@@ -107,7 +132,8 @@ def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
     """(kernel, k_split, tile_n) that `matmul` runs for row-major contiguous operands of these shapes.
 
     kernel: "single" (one CTA per 128 x tile_n tile; tile_n 256, or 128 / 64 for small 16-bit problems), "pair"
-    (CTA pairs per 256x256 tile) or "splitk" (a cluster of k_split CTAs shares each 128x256 tile's K).  No
+    (CTA pairs per 256 x tile_n tile), "pair_streamk" (the same, with the K blocks of the tiles past the full
+    waves split evenly over all pairs) or "splitk" (a cluster of k_split CTAs shares each 128x256 tile's K).  No
     counterpart in the reference; it reads only the shapes.
     """
     out_dtype = in_dtype if out_dtype is None else out_dtype
@@ -117,12 +143,28 @@ def kernel_plan(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16,
     p.M, p.N, p.K = int(M), int(N), int(K)
     p.in_dtype = _native.dtype_code(in_dtype)
     p.out_dtype = _native.dtype_code(out_dtype)
+    p.workspace, p.workspace_bytes = 256, 1 << 40  # what `matmul` runs: its shared workspace is large enough
     kernel, split, tile_n = ctypes.c_int(0), ctypes.c_int(1), ctypes.c_int(256)
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
         _native.check(_native.lib.fab_gemm_plan(ctypes.byref(p), ctypes.byref(kernel), ctypes.byref(split),
                                                 ctypes.byref(tile_n)), "kernel_plan")
     return _KERNEL_NAMES[kernel.value], split.value, tile_n.value
+
+
+def kernel_grid(M: int, N: int, K: int, in_dtype: torch.dtype = torch.bfloat16, device=None) -> int:
+    """CTAs in the grid `matmul` launches for these shapes (two per pair for the CTA-pair kernels)."""
+    p = _native.FabGemmParams()
+    p.a = p.b = p.c = 256
+    p.lda, p.ldb, p.ldc = max(int(K), 1), max(int(N), 1), max(int(N), 1)
+    p.M, p.N, p.K = int(M), int(N), int(K)
+    p.in_dtype = p.out_dtype = _native.dtype_code(in_dtype)
+    p.workspace, p.workspace_bytes = 256, 1 << 40
+    ctas = ctypes.c_longlong(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _native.check(_native.lib.fab_gemm_grid(ctypes.byref(p), ctypes.byref(ctas)), "kernel_grid")
+    return int(ctas.value)
 
 
 class _MatmulKernel:
@@ -207,8 +249,14 @@ def _select_2d_contiguous_config(m: int, n: int, k: int) -> tuple[int, int, int,
     return SM100_BLOCK_M, SM100_BLOCK_N, _sm100_block_k(2), 8, SM100_NUM_WARPS, SM100_NUM_STAGES
 
 
-def matmul(a: torch.Tensor, b: torch.Tensor, *, out_dtype: torch.dtype | None = None, round_f16: bool = False) -> torch.Tensor:
-    """C = A B for 2-D row-major a [M, K], b [K, N] (any leading dims with unit column stride)."""
+def matmul(a: torch.Tensor, b: torch.Tensor, *, out_dtype: torch.dtype | None = None, round_f16: bool = False,
+           stream_k: bool = True) -> torch.Tensor:
+    """C = A B for 2-D row-major a [M, K], b [K, N] (any leading dims with unit column stride).
+
+    `stream_k` lets CTA-pair GEMMs whose tiles leave part of the last wave idle split the remaining tiles'
+    K over all pairs (through the device's shared workspace, `gemm_workspace`); False runs whole tiles,
+    which sum each output in the same order as the fused-epilogue GEMMs (`matmul_swiglu`,
+    `matmul_bias_rope`)."""
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0]:
         raise ValueError(f"matmul expects a [M, K] and b [K, N], got {tuple(a.shape)} and {tuple(b.shape)}")
     M, K = a.shape
@@ -218,7 +266,8 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, out_dtype: torch.dtype | None = 
     if b.stride(1) != 1:
         b = b.contiguous()
     c = torch.empty((M, N), device=a.device, dtype=out_dtype or a.dtype)
-    _gemm(a, b, c, M, N, K, lda=a.stride(0), ldb=b.stride(0), ldc=c.stride(0), round_f16=round_f16, what="matmul")
+    _gemm(a, b, c, M, N, K, lda=a.stride(0), ldb=b.stride(0), ldc=c.stride(0), round_f16=round_f16,
+          workspace=None if stream_k else False, what="matmul")
     return c
 
 
@@ -329,6 +378,8 @@ __all__ = [
     "matmul_bias_rope",
     "fold_rmsnorm_weight",
     "kernel_plan",
+    "kernel_grid",
+    "gemm_workspace",
     "interleave_gate_up",
     "split_gate_up",
     "get_architecture",

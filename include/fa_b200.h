@@ -163,8 +163,9 @@ int fab_attention_fwd_varlen(const fab_attention_varlen_params* params, void* st
  *
  * The keys are cut into num_splits ranges (num_splits <= 0: enough ranges for
  * one CTA per SM).  Each range's attention (normalised O in fp32 and its LSE)
- * goes to the workspace; a second kernel merges the ranges into o (and lse,
- * when not NULL) with weights exp(LSE_split - LSE).  When the query heads of a
+ * goes to the workspace; the last range of each row group to finish merges
+ * the group into o (and lse, when not NULL) with weights exp(LSE_split - LSE),
+ * inside the same kernel, found through one arrival counter per row group.  When the query heads of a
  * key/value head are evenly spaced in memory (q_stride_h == seqlen_q *
  * q_stride_s, or seqlen_q == 1) they share one query tile, so every K/V tile
  * is read once per key/value head.
@@ -172,7 +173,9 @@ int fab_attention_fwd_varlen(const fab_attention_varlen_params* params, void* st
  * fab_attention_fwd_splitkv_workspace writes the workspace size the call
  * needs (0 when a single range suffices) and, if splits_used is not NULL, the
  * number of ranges it will use.  The workspace is caller-owned device memory,
- * 256-byte aligned; calls that share a workspace must be ordered on one
+ * 256-byte aligned and zero-filled before its first use (its counters must
+ * start at zero; each call leaves them zero again, so refill it only after a
+ * FAB_ERR_DEVICE_TIMEOUT); calls that share a workspace must be ordered on one
  * stream.  FAB_ERR_WORKSPACE when it is missing, misaligned or too small.
  */
 int fab_attention_fwd_splitkv_workspace(const fab_attention_params* params, int num_splits, size_t* bytes,
@@ -233,6 +236,21 @@ typedef struct fab_gemm_params {
    * which runs the norm as its own PyTorch op (ttft.py forward).
    */
   const float* row_scale;
+  /*
+   * NULL, or device memory (256-byte aligned, zero-filled before its first
+   * use) for the stream-K schedule of the CTA-pair kernel: when the output
+   * tiles leave part of the last wave of SM pairs idle, the K blocks of the
+   * tiles past the full waves are split evenly over all pairs, and each such
+   * tile's pieces are added through this memory (plain store epilogue only).
+   * fab_gemm_workspace_size gives the size; without a workspace (or with a
+   * smaller one) the call runs whole tiles.  The kernel leaves the memory's
+   * flag words zero again when it completes, so one workspace serves calls
+   * ordered on one stream, CUDA graph replays included; calls that overlap
+   * in time must not share it.  After a FAB_ERR_DEVICE_TIMEOUT, zero it again.
+   * No counterpart in the reference.
+   */
+  void* workspace;
+  size_t workspace_bytes;
 } fab_gemm_params;
 
 /*
@@ -265,8 +283,9 @@ int fab_gemm(const fab_gemm_params* params, void* stream);
  * reference; like the launch facts of `_select_2d_contiguous_config`,
  * mma.py:22-81, it only reads the shapes): one CTA per 128 x *tile_n output
  * tile (*tile_n 256, or 128 / 64 for 16-bit problems whose 256-wide tiles
- * would leave over a quarter of the SMs idle), CTA pairs per 256x256 tile
- * (16-bit inputs, at least one wave of pairs), or split K, where the
+ * would leave over a quarter of the SMs idle), CTA pairs per 256 x *tile_n
+ * tile (*tile_n 256 or 224; 16-bit inputs, at least one wave of pairs; with
+ * a large enough workspace, the stream-K schedule), or split K, where the
  * *k_split CTAs of a cluster share each 128x256 tile's K and add their
  * partial sums in distributed shared memory (16-bit inputs, few tiles, deep
  * K).  Validates like fab_gemm; pointers are not dereferenced.  Nothing to
@@ -275,8 +294,13 @@ int fab_gemm(const fab_gemm_params* params, void* stream);
 #define FAB_GEMM_KERNEL_SINGLE 0
 #define FAB_GEMM_KERNEL_PAIR 1
 #define FAB_GEMM_KERNEL_SPLITK 2
+#define FAB_GEMM_KERNEL_PAIR_STREAMK 3 /* CTA pairs, stream-K schedule through the caller's workspace */
 
 int fab_gemm_plan(const fab_gemm_params* params, int* kernel, int* k_split, int* tile_n);
+/* Stream-K workspace bytes a fab_gemm call with these parameters would use if given one (0: none). */
+int fab_gemm_workspace_size(const fab_gemm_params* params, size_t* bytes);
+/* CTAs in the grid a fab_gemm call with these parameters launches (0 when nothing is computed). */
+int fab_gemm_grid(const fab_gemm_params* params, long long* ctas);
 
 /*
  * GEMM + all-reduce over the ranks of a tensor-parallel group in one kernel,

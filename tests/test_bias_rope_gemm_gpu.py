@@ -45,7 +45,7 @@ def _case(S, K, heads, rot_heads, D, dtype, with_bias, device, seed):
 
 
 def _two_pass(a, w, bias, cos, sin, heads, rot_heads, D):
-    y = matmul(a, w)
+    y = matmul(a, w, stream_k=False)  # whole tiles: the fused kernel's summation order
     ttft._native_bias_rope(y, bias, cos, sin, heads, rot_heads, D)
     return y
 
@@ -72,7 +72,7 @@ def test_fused_equals_two_pass(case, cuda_device):
 def test_fused_equals_pytorch_expression(cuda_device):
     S, K, nq, nkv, D = 257, 640, 6, 2, 128
     a, w, bias, cos, sin = _case(S, K, nq + 2 * nkv, nq + nkv, D, torch.bfloat16, True, cuda_device, seed=3)
-    ref = matmul(a, w) + bias
+    ref = matmul(a, w, stream_k=False) + bias
     q = ref[:, : nq * D].view(S, nq, D)
     k = ref[:, nq * D:(nq + nkv) * D].view(S, nkv, D)
     q_ref = q * cos[:, None, :] + ttft._rotate_half(q) * sin[:, None, :]

@@ -191,15 +191,18 @@ def _round256(x):
 
 @pytest.mark.parametrize("splits, expect_used", [(8, 8), (1, 1), (1000, 256), (300, 256)])
 def test_splitkv_workspace_size(splits, expect_used):
-    """Workspace = fp32 partial O of every split and row, then the partial LSEs, each 256-byte aligned; the
-    split count is capped by the number of 128-key tiles."""
+    """Workspace = fp32 partial O of every split and row, the partial LSEs, then one arrival counter per row
+    group (4 key/value heads, whose 7 query heads share one 128-row tile), each 256-byte aligned; the split
+    count is capped by the number of 128-key tiles."""
     lib = _native.lib
     a = _decode_params()
     need, used = ctypes.c_size_t(0), ctypes.c_int(0)
     assert lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(a), splits, ctypes.byref(need), ctypes.byref(used)) == 0
     assert used.value == expect_used
     rows = 1 * 28 * 1
-    want = 0 if expect_used == 1 else _round256(4 * expect_used * rows * 128) + _round256(4 * expect_used * rows)
+    groups = 4
+    want = 0 if expect_used == 1 else (_round256(4 * expect_used * rows * 128) + _round256(4 * expect_used * rows)
+                                       + _round256(4 * groups))
     assert need.value == want
 
 

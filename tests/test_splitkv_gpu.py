@@ -101,10 +101,17 @@ def test_caller_workspace_reused_across_calls(cuda_device):
     shape = (1, 28, 4, 1, 8192, 128)
     q, k, v = (t.to(cuda_device) for t in _inputs(shape, torch.bfloat16, seed=32))
     need, _ = splitkv_workspace_bytes(tuple(q.shape), tuple(k.shape), torch.bfloat16, num_splits=16)
-    ws = torch.empty(need, device=cuda_device, dtype=torch.uint8)
+    ws = torch.zeros(need, device=cuda_device, dtype=torch.uint8)
     a = attention_forward_splitkv(q, k, v, num_splits=16, workspace=ws)
-    ws.fill_(0xFF)  # stale contents must not matter: every split rewrites its partials
+    # The workspace ends with one arrival counter per row group (4 key/value heads here: one 256-byte
+    # block), which every call leaves at zero; stale partials before it must not matter, since every
+    # split rewrites its own.
+    torch.cuda.synchronize()
+    assert bool((ws[-256:] == 0).all())
+    ws[:-256].fill_(0xFF)
     b = attention_forward_splitkv(q, k, v, num_splits=16, workspace=ws)
+    torch.cuda.synchronize()
+    assert bool((ws[-256:] == 0).all())
     assert torch.equal(a, b)
 
 

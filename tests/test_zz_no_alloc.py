@@ -53,7 +53,7 @@ def test_static_scratch_matches_workspace_entry(shape, splits, cuda_device):
     _native.check(lib.fab_attention_fwd_splitkv_workspace(ctypes.byref(p_ref), splits, ctypes.byref(need),
                                                           ctypes.byref(used)), "workspace")
     assert used.value > 1 and 0 < need.value <= STATIC_SCRATCH_BYTES
-    ws = torch.empty(need.value, device=cuda_device, dtype=torch.uint8)
+    ws = torch.zeros(need.value, device=cuda_device, dtype=torch.uint8)
     _native.check(lib.fab_attention_fwd_splitkv(ctypes.byref(p_ref), splits, ws.data_ptr(), need.value, stream),
                   "workspace entry")
 
