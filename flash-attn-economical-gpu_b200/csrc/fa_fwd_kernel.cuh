@@ -43,10 +43,19 @@
 #include "fa_internal.h"
 #include "ptx.cuh"
 
+// 1: the MMA issuer is a converged warp whose elected lane issues (descriptor
+// arithmetic stays warp-uniform); 0: a single thread.  Measured on B200
+// together with 4 of 16 polynomial pairs below: +2.7 % at B4 H32 S8192 D128,
+// +4 % causal, +6.5 % S4096 causal; within +-2 % on the short shapes.
+#ifndef FAB_FA_WARP_MMA
+#define FAB_FA_WARP_MMA 1
+#endif
+constexpr bool kWarpMma = FAB_FA_WARP_MMA != 0;
+
 // Of every 16 pairs of scores, this many are exponentiated by exp2_poly2 on
 // the FMA pipe and the rest by ex2.approx on the MUFU unit.
 #ifndef FAB_FA_POLY_PAIRS_PER_16
-#define FAB_FA_POLY_PAIRS_PER_16 0
+#define FAB_FA_POLY_PAIRS_PER_16 4
 #endif
 
 namespace fab {
@@ -441,8 +450,19 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
     for (int i = 0; i < q_loaded; ++i) mbar_wait(bar_q_full + i, 0, &no_abort, kDevTimeoutTeardown);
     for (int x = max(0, issued - kRing); x < issued; ++x)
       mbar_wait(bar_kv_full + (x % kRing), (x / kRing) & 1, &no_abort, kDevTimeoutTeardown);
-  } else if (!skip && warp == 1 && lane == 0) {
+  } else if (!skip && warp == 1 && (kWarpMma || lane == 0)) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread issues every tcgen05.mma and commit (the commits track that
+    // thread's products).  With kWarpMma the whole warp runs this code and
+    // waits together, and its elected lane issues.
+    const bool leader = kWarpMma ? elect_one() : true;
+    auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+      if constexpr (kWarpMma) {
+        return mbar_wait_warp(bar, parity, abort_flag, code);
+      } else {
+        return mbar_wait(bar, parity, abort_flag, code);
+      }
+    };
     constexpr uint32_t kFmt = ElemOps<T>::kFmt;
     constexpr uint32_t idesc_qk = umma_idesc(kFmt, C::kBM, kBN, 0, 0);
     constexpr uint32_t idesc_pv = umma_idesc(kFmt, C::kBM, kDP, 0, 1);
@@ -474,10 +494,13 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
         const uint32_t off = (kk & 3) * 32;
         const uint64_t ad = umma_desc_join(qa + ((a * C::kQAtomBytes + off) >> 4), kHiK);
         const uint64_t bd = umma_desc_join(kb + ((a * C::kKVAtomBytes + off) >> 4), kHiK);
-        if constexpr (sizeof(T) == 4)
-          mma_ss_tf32(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-        else
-          mma_ss_f16(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        if (leader) {
+          if constexpr (sizeof(T) == 4) {
+            mma_ss_tf32(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          } else {
+            mma_ss_f16(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+        }
       }
     };
     auto issue_pv = [&](int i, int slot, int s, bool acc) {
@@ -490,54 +513,57 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
         const uint64_t bd = umma_desc_join(vb + ((kk * C::kKInstr * 128) >> 4), kHiV);
         const uint32_t a_t = pa + kk * (C::kKInstr * static_cast<int>(sizeof(T)) / 4);
         const uint32_t accum = (acc || kk > 0) ? 1u : 0u;
-        if constexpr (sizeof(T) == 4)
-          mma_ts_tf32(d, a_t, bd, idesc_pv, accum);
-        else
-          mma_ts_f16(d, a_t, bd, idesc_pv, accum);
+        if (leader) {
+          if constexpr (sizeof(T) == 4) {
+            mma_ts_tf32(d, a_t, bd, idesc_pv, accum);
+          } else {
+            mma_ts_f16(d, a_t, bd, idesc_pv, accum);
+          }
+        }
       }
     };
 
-    bool ok = mbar_wait(bar_q_full, 0, abort_flag, kDevTimeoutQ);  // Q tile 0
+    bool ok = wait(bar_q_full, 0, kDevTimeoutQ);  // Q tile 0
     bool any_issued = false;
     // Prologue: S for the first kSB KV tiles of every Q tile.  Q tiles after
     // the first land behind K_0, so tile 0's product starts without them.
     for (int j = 0; ok && j < min(kSB, nt); ++j) {
-      if (!(ok = mbar_wait(bar_kv_full + kslot(j), kpar(j), abort_flag, kDevTimeoutKV))) break;
+      if (!(ok = wait(bar_kv_full + kslot(j), kpar(j), kDevTimeoutKV))) break;
       tc_fence_after();
       for (int i = 0; i < kNQ; ++i) {
         if (j == 0 && i > 0) {
-          if (!(ok = mbar_wait(bar_q_full + i, 0, abort_flag, kDevTimeoutQ))) break;
+          if (!(ok = wait(bar_q_full + i, 0, kDevTimeoutQ))) break;
           tc_fence_after();
         }
         issue_qk(i, i * kSB + j, kslot(j));
         any_issued = true;
-        mma_commit(bar_s_full + i * kSB + j);
+        { if (leader) mma_commit(bar_s_full + i * kSB + j); }
       }
       if (!ok) break;
-      mma_commit(bar_kv_empty + kslot(j));
+      { if (leader) mma_commit(bar_kv_empty + kslot(j)); }
     }
     for (int j = 0; ok && j < nt; ++j) {
       const int s = vslot(j);
       const int jn = j + kSB;  // the KV tile whose S product reuses this S buffer
       const int sn = kslot(jn);
-      if (!(ok = mbar_wait(bar_kv_full + s, vpar(j), abort_flag, kDevTimeoutKV))) break;
+      if (!(ok = wait(bar_kv_full + s, vpar(j), kDevTimeoutKV))) break;
       if constexpr (kSB == 1) {
         // Two Q tiles.  Each MMA burst is followed by a stall of a few hundred
         // cycles before the issuing thread's next instruction, so P_i*V(j)
         // and S_i(j+1) go out back to back: K(j+1) (loaded an iteration ago)
         // is waited for up front and the K/V release commits come last.
-        if (jn < nt && !(ok = mbar_wait(bar_kv_full + sn, kpar(jn), abort_flag, kDevTimeoutKV))) break;
+        if (jn < nt && !(ok = wait(bar_kv_full + sn, kpar(jn), kDevTimeoutKV))) break;
         for (int i = 0; i < kNQ; ++i) {
           const int slot = i;
-          if (!(ok = mbar_wait(bar_p_full + slot, j & 1, abort_flag, kDevTimeoutP))) break;
+          if (!(ok = wait(bar_p_full + slot, j & 1, kDevTimeoutP))) break;
           tc_fence_after();
           issue_pv(i, slot, s, j > 0);
           if (jn < nt) issue_qk(i, slot, sn);
-          if (j == nt - 1) mma_commit(bar_o_done + i);  // nobody reads O before the end
-          if (jn < nt) mma_commit(bar_s_full + slot);
+          if (j == nt - 1) { if (leader) mma_commit(bar_o_done + i); }  // nobody reads O before the end
+          if (jn < nt) { if (leader) mma_commit(bar_s_full + slot); }
         }
         if (!ok) break;
-        mma_commit(bar_kv_empty + (j + 1) % kRing);  // release group j+1: V_j and K_{j+1}
+        { if (leader) mma_commit(bar_kv_empty + (j + 1) % kRing); }  // release group j+1: V_j and K_{j+1}
       } else {
         // Two S buffers per Q tile: S_i(j+1) is already in TMEM while the
         // softmax works on tile j.  The softmax of tile j+1 waits for
@@ -547,29 +573,29 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
         // afterwards.
         for (int i = 0; i < kNQ; ++i) {
           const int slot = i * kSB + j % kSB;
-          if (!(ok = mbar_wait(bar_p_full + slot, (j / kSB) & 1, abort_flag, kDevTimeoutP))) break;
+          if (!(ok = wait(bar_p_full + slot, (j / kSB) & 1, kDevTimeoutP))) break;
           tc_fence_after();
           issue_pv(i, slot, s, j > 0);
-          mma_commit(bar_o_done + i);
+          { if (leader) mma_commit(bar_o_done + i); }
         }
         if (!ok) break;
-        mma_commit(bar_kv_empty + s);
+        { if (leader) mma_commit(bar_kv_empty + s); }
         if (jn < nt) {
-          if (!(ok = mbar_wait(bar_kv_full + sn, kpar(jn), abort_flag, kDevTimeoutKV))) break;
+          if (!(ok = wait(bar_kv_full + sn, kpar(jn), kDevTimeoutKV))) break;
           tc_fence_after();
           for (int i = 0; i < kNQ; ++i) {
             const int slot = i * kSB + j % kSB;
             issue_qk(i, slot, sn);
-            mma_commit(bar_s_full + slot);
+            { if (leader) mma_commit(bar_s_full + slot); }
           }
-          mma_commit(bar_kv_empty + sn);
+          { if (leader) mma_commit(bar_kv_empty + sn); }
         }
       }
     }
     if (any_issued) {
       // Drain the tensor pipe before TMEM is released.
       volatile int no_abort = 0;
-      mma_commit(bar_teardown);
+      { if (leader) mma_commit(bar_teardown); }
       mbar_wait(bar_teardown, 0, &no_abort, kDevTimeoutTeardown);
     }
   }
