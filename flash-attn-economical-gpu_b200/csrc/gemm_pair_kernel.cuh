@@ -447,8 +447,8 @@ static PairChoice gemm_pair_whole(const GemmLaunch& L, int half_sms) {
   return best;
 }
 
-// The chosen layout.  Stream-K (256-wide tiles, plain store epilogue) is
-// taken when the tiles leave part of the last wave idle and the estimate --
+// The chosen layout.  Stream-K (256-wide tiles, plain store epilogue, deep
+// K) is taken when the tiles leave part of the last wave idle and the estimate --
 // tiles / pairs waves plus ~4 % for writing and adding the pieces -- beats
 // the best whole-tile layout; it also needs at least two K blocks per pair
 // and ranges of at least a quarter tile (so an owner adds a handful of
@@ -464,7 +464,12 @@ static PairChoice gemm_pair_choice(const GemmLaunch& L, bool with_workspace) {
   const int cap = gemm_pair_capacity<Tin, Tout, 256>();
   const int P = cap < half_sms ? cap : half_sms;
   const long long nkb = (L.K + 63) / 64;
-  if (P >= 1 && tiles > P && tiles % P != 0) {
+  // K >= 8192 only: measured on B200, stream-K beat whole tiles at the TTFT
+  // down_proj (K = 18944: 1386 -> 1512 TF/s) but lost 3-5 % at K = 3584 and
+  // 4096, where its fixed costs (writing and adding the pieces, the owners'
+  // tails) weigh more, and where whole tiles' part-idle last wave runs the
+  // busy SMs at a higher clock under the power cap.
+  if (P >= 1 && tiles > P && tiles % P != 0 && L.K >= 8192) {
     const long long dp = tiles / P * P;
     const long long sk_blocks = (tiles - dp) * nkb;
     const double sk_cost = static_cast<double>(tiles) / P * 256 * 1.04;

@@ -58,16 +58,16 @@ def _flags_zero(device):
 
 
 SHAPES = [
-    # M, K, N, dtype
-    (2048, 18944, 3584, torch.bfloat16),  # TTFT down_proj at 2048 tokens
-    (2048, 3584, 3584, torch.bfloat16),   # TTFT o_proj
-    (4096, 4096, 4096, torch.bfloat16),   # BASELINE config 4 at 4096
-    (2381, 1000, 2376, torch.float16),    # ragged in every dimension, K not a multiple of 64
+    # M, K, N, dtype -- all take the stream-K schedule (asserted)
+    (2048, 18944, 3584, torch.bfloat16),  # TTFT down_proj at 2048 tokens: 112 tiles on 74 pairs
+    (2381, 9000, 2376, torch.float16),    # ragged in every dimension, K not a multiple of 64
+    (1800, 12000, 4000, torch.bfloat16),  # ragged, 8 x 16 tiles
 ]
 
 
 @pytest.mark.parametrize("M, K, N, dtype", SHAPES, ids=lambda x: NAME[x] if isinstance(x, torch.dtype) else str(x))
 def test_matches_oracle_and_is_deterministic(M, K, N, dtype, cuda_device):
+    assert mma.kernel_plan(M, N, K, dtype)[0] == "pair_streamk"
     a, b = _inputs(M, N, K, dtype, cuda_device, seed=M + N + K)
     c1 = mma.matmul(a, b)
     c2 = mma.matmul(a, b)
@@ -78,10 +78,11 @@ def test_matches_oracle_and_is_deterministic(M, K, N, dtype, cuda_device):
 
 
 def test_down_proj_takes_stream_k(cuda_device):
-    """112 tiles on 74 pairs with K = 18944: the schedule is chosen, and the pairs that cannot all be resident
-    are never more than the device reports."""
+    """112 tiles on 74 pairs with K = 18944: the schedule is chosen, and never with more pairs than can be
+    resident.  Short K (the o_proj, K = 3584) keeps whole tiles."""
     plan = mma.kernel_plan(2048, 3584, 18944, torch.bfloat16)
     assert plan[0] == "pair_streamk", plan
+    assert mma.kernel_plan(2048, 3584, 3584, torch.bfloat16)[0] == "pair"
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
     assert 0 < mma.kernel_grid(2048, 3584, 18944) <= sms
 
