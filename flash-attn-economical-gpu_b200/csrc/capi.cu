@@ -216,6 +216,7 @@ static int splitkv_prepare(const fab_attention_params* p, int num_splits, FaLaun
   L->num_splits = plan->num_splits;
   L->split_len = plan->split_len;
   L->pack_gqa = plan->pack_gqa;
+  L->split_dual = plan->dual;
   return kOk;
 }
 

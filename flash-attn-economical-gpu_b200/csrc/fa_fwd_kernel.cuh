@@ -1223,10 +1223,27 @@ int fa_select_split_config(int dtype, int D, FaConfigInfo* out) {
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
+// Key splits on the two-CTAs-per-SM one-tile kernel (one S buffer per CTA,
+// two CTAs sharing each SM) instead of the two-S-buffer tile, with twice the
+// CTAs.
+#ifndef FAB_SPLIT_DUAL
+#define FAB_SPLIT_DUAL 0
+#endif
+
 int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
   FaConfigInfo cfg;
   int rc = fa_select_split_config(L.dtype, L.D, &cfg);
   if (rc) return rc;
+  int per_sm = 1;
+  plan->dual = 0;
+  if (FAB_SPLIT_DUAL) {
+    FaConfigInfo one;
+    if (fa_select_one_tile_config(L.dtype, L.D, &one) == 0 && one.s_bufs == 1) {
+      cfg = one;
+      per_sm = 2;
+      plan->dual = 1;
+    }
+  }
   const int group = L.Hq / L.Hkv;
   // Pack a key/value head's query heads into one tile when their rows are
   // evenly spaced: every query position of a head, then the next head.
@@ -1241,12 +1258,13 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
     // Enough CTAs for one per SM.
     const int sms = num_sms();
     if (sms <= 0) return kErrCuda;
-    splits = static_cast<int>((sms + base_ctas - 1) / (base_ctas > 0 ? base_ctas : 1));
+    splits = static_cast<int>((static_cast<long long>(per_sm) * sms + base_ctas - 1) / (base_ctas > 0 ? base_ctas : 1));
   }
   splits = std::max(1, std::min({splits, std::max(tiles, 1), 65535}));
   const int tiles_per_split = tiles > 0 ? (tiles + splits - 1) / splits : 1;
   plan->split_len = tiles_per_split * cfg.bn;
   plan->num_splits = L.N > 0 ? (L.N + plan->split_len - 1) / plan->split_len : 1;
+  if (plan->num_splits <= 1) plan->dual = 0;  // a single pass keeps the two-S-buffer tile
   plan->rows = static_cast<int64_t>(L.B) * L.Hq * L.M;
   plan->workspace_bytes = 0;
   plan->lse_offset = 0;
@@ -1262,13 +1280,17 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
 
 int fa_forward_split(const FaLaunch& L, cudaStream_t stream) {
   FaConfigInfo c;
-  int rc = fa_select_split_config(L.dtype, L.D, &c);
+  int rc = L.split_dual ? fa_select_one_tile_config(L.dtype, L.D, &c) : fa_select_split_config(L.dtype, L.D, &c);
   if (rc) return rc;
   const int elt = L.dtype == kDtypeF32 ? 4 : 2;
   rc = kErrUnsupported;
 #define FAB_FA_SLAUNCH(E, DP, NQ, BN, ST, SB) \
   if (elt == E && c.d_pad == DP) rc = launch_entry<E, DP, NQ, BN, ST, SB>(L, stream);
-  FAB_FA_SPLIT_TABLE(FAB_FA_SLAUNCH)
+  if (L.split_dual) {
+    FAB_FA_ONE_TILE_TABLE(FAB_FA_SLAUNCH)
+  } else {
+    FAB_FA_SPLIT_TABLE(FAB_FA_SLAUNCH)
+  }
 #undef FAB_FA_SLAUNCH
   // Merged inside the split kernel when the launch carries the counters.
   if (rc || L.num_splits <= 1 || L.o_part == nullptr || L.split_cnt != nullptr) return rc;

@@ -83,6 +83,7 @@ struct FaLaunch {
   float* o_part;
   float* lse_part;
   unsigned int* split_cnt;  // see FaKernelParams
+  int split_dual;           // key splits on the two-CTAs-per-SM one-tile kernel (see FaSplitPlan)
   // Packed variable-length batches (see FaKernelParams); the tensor maps
   // then span total_q / total_k rows with batch extent 1.
   const int* cu_q;
@@ -101,6 +102,7 @@ struct FaSplitPlan {
   size_t lse_offset;       // byte offset of lse_part in the workspace
   size_t counter_offset;   // byte offset of the counters (which start at zero)
   int64_t groups;          // row groups (CTAs per key split): one counter each
+  int dual;                // 1: the splits run on the two-CTAs-per-SM one-tile kernel, two CTAs per SM
 };
 
 struct FaConfigInfo {
