@@ -147,6 +147,11 @@ struct GemmKernelParams {
   int sk_dp_tiles;
   float* sk_part;  // [pairs][2 CTAs][kBN / 4][128 rows] float4: one partial tile per pair and CTA
   int* sk_flags;   // [pairs][2 CTAs][4 epilogue warps]; zero between calls
+  // CTA-pair kernel, whole tiles: 1 launches one cluster per tile, and a
+  // running cluster takes the tile of the next cluster that has not started
+  // (cluster launch control) instead of a fixed round robin; 0 launches one
+  // cluster per resident pair.
+  int dyn_sched;
 };
 
 // Fused GEMM + all-reduce over NVLink peer memory (tensor-parallel output

@@ -718,6 +718,7 @@ static int launch_gemm(const GemmLaunch& L, cudaStream_t stream, const GemmArPar
   kp.sk_dp_tiles = 0;  // stream-K is the CTA-pair kernel's
   kp.sk_part = nullptr;
   kp.sk_flags = nullptr;
+  kp.dyn_sched = 0;
   const int tiles = ((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   if (tiles <= 0) return 0;
   int sms = num_sms();
@@ -824,7 +825,10 @@ long long gemm_grid_ctas(const GemmLaunch& L) {
   gemm_plan(L, &kernel, &split, &tile_n);
   const int sms = num_sms();
   if (kernel == 2) return static_cast<long long>((L.M + 127) / 128) * ((L.N + 255) / 256) * split;
-  if (kernel == 1 || kernel == 3) return 2LL * gemm_pair_layout_any(L).pairs;
+  if (kernel == 1 || kernel == 3) {
+    const PairChoice c = gemm_pair_layout_any(L);
+    return 2LL * (pair_dynamic(c) ? c.tiles : c.pairs);
+  }
   const long long tiles = static_cast<long long>((L.M + 127) / 128) * ((L.N + tile_n - 1) / tile_n);
   return tiles < sms ? tiles : sms;
 }

@@ -30,6 +30,13 @@
 #include "fa_internal.h"
 #include "ptx.cuh"
 
+// 1: whole-tile launches of the pair kernel start one cluster per tile and
+// hand out tiles dynamically (cluster launch control); 0: one cluster per
+// resident pair, tiles round robin.
+#ifndef FAB_GEMM_DYNAMIC
+#define FAB_GEMM_DYNAMIC 0
+#endif
+
 namespace fab {
 
 // kBN: 256, or 224 where that width leaves fewer idle pairs in the last wave
@@ -53,8 +60,13 @@ struct GemmPairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kThreads = 256;
   static constexpr int kTmemCols = 512;               // 2 accumulators, kAccStride apart
-  static constexpr int kNumBars = 2 * kStages + 4 + 1;
+  // full/empty per stage, acc full/empty x 2, dealloc, then the dynamic
+  // schedule's ring (full/empty x 2) and its cluster-launch-control barrier.
+  static constexpr int kNumBars = 2 * kStages + 4 + 1 + 5;
+  // After the barriers: TMEM address, abort flag, (unused), the ring's two
+  // tile words at +8, the 16-byte scheduler response at +12.
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kNumBars * 8 + 64;
+  static_assert(kNumBars % 2 == 0 && kStageBytes % 16 == 0, "scheduler response 16-byte aligned");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kBN % 32 == 0 && kBN <= kAccStride && kBNc % 16 == 0, "tile width");
 };
@@ -190,8 +202,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   uint64_t* bar_acc_full = bar_empty + C::kStages;
   uint64_t* bar_acc_empty = bar_acc_full + 2;
   uint64_t* bar_dealloc = bar_acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_dealloc + 1);
+  uint64_t* bar_sched_full = bar_dealloc + 1;    // [2]
+  uint64_t* bar_sched_empty = bar_sched_full + 2;  // [2], rank 0's is the one used
+  uint64_t* bar_clc = bar_sched_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_clc + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* sched_tile = reinterpret_cast<volatile int*>(tmem_slot + 8);  // [2]
+  const uint32_t clc_resp = smem_u32(tmem_slot + 12);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -213,6 +230,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     sched.dp_tiles = num_tiles;
     sched.sk_blocks = 0;
   }
+  // Item i of this pair.  Static schedule: pair_item.  Dynamic (whole tiles,
+  // one cluster launched per tile): item 0 is the cluster's own tile, item
+  // i >= 1 the tile rank 0's scheduler thread took from a cluster that had
+  // not started, published in both CTAs' two-slot ring (slot (i-1) % 2); -1
+  // ends the run.  Epilogue warps read last, so they free the slot (`epi`,
+  // called by whole warps).
+  const bool dyn = p.dyn_sched != 0;
+  auto next_item = [&](int i, PairItem* out, bool epi) -> bool {
+    if (!dyn) return pair_item(sched, pair, i, out);
+    int tile = pair;
+    if (i > 0) {
+      const int q = i - 1, s = q & 1;
+      bool got = mbar_wait_cluster(bar_sched_full + s, (q >> 1) & 1, abort_flag, kDevTimeoutSched);
+      if (epi) got = __all_sync(0xffffffffu, got) != 0;
+      if (!got) return false;
+      tile = sched_tile[s];
+      if (epi) {
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(mapa_shared(smem_u32(bar_sched_empty + s), 0));
+      }
+    }
+    if (tile < 0 || tile >= num_tiles) return false;
+    *out = PairItem{tile, 0, nkb, kItemFull};
+    return true;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -224,6 +266,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       mbar_init(bar_acc_empty + b, 8);  // 4 epilogue warps x 2 CTAs (rank 0's is the one used)
     }
     mbar_init(bar_dealloc, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_sched_full + b, 1);
+      mbar_init(bar_sched_empty + b, 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(bar_clc, 1);
     *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
     mbar_fence_init();
   }
@@ -246,7 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     int it = 0;
     bool ok = true;
     PairItem w;
-    for (int i = 0; ok && pair_item(sched, pair, i, &w); ++i) {
+    for (int i = 0; ok && next_item(i, &w, false); ++i) {
       int pm, pn;
       gemm_tile_coords(w.tile, num_pid_m, num_pid_n, p.group_m, &pm, &pn);
       const int m0 = pm * C::kBM + static_cast<int>(rank) * C::kBMc;
@@ -280,7 +327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     int it = 0, tcount = 0;
     bool ok = true;
     PairItem w;
-    for (int i = 0; ok && pair_item(sched, pair, i, &w); ++i, ++tcount) {
+    for (int i = 0; ok && next_item(i, &w, false); ++i, ++tcount) {
       const int buf = tcount & 1;
       const uint32_t use = tcount >> 1;
       if (!(ok = mbar_wait(bar_acc_empty + buf, (use & 1) ^ 1, abort_flag, kDevTimeoutAcc))) break;
@@ -305,6 +352,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       if (!ok) break;
       mma_commit_pair(bar_acc_full + buf, kBoth);
     }
+  } else if (!skip && dyn && warp == 2 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ tile scheduler (rank 0, dynamic)
+    // Takes the pair's next tile from a cluster of this grid that has not
+    // started (cluster launch control: the hardware hands out clusters in
+    // launch order, so the tiles in flight stay a window of consecutive
+    // raster positions) while the current one runs, and publishes it in
+    // both CTAs' ring.  A slot is reused once all eight epilogue warps read
+    // it.  Every request's response lands before this thread moves on.
+    volatile int no_abort = 0;
+    for (int q = 0;; ++q) {
+      const int s = q & 1;
+      if (q >= 2 && !mbar_wait_cluster(bar_sched_empty + s, ((q - 2) >> 1) & 1, abort_flag, kDevTimeoutSched)) break;
+      mbar_arrive_expect_tx(bar_clc, 16);
+      clc_try_cancel(clc_resp, bar_clc);
+      if (!mbar_wait(bar_clc, q & 1, &no_abort, kDevTimeoutSched)) break;
+      const int x = clc_first_cta_x(clc_resp);
+      const int tile = x < 0 ? -1 : (x >> 1);
+      sched_tile[s] = tile;
+      st_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(sched_tile + s)), 1), static_cast<uint32_t>(tile));
+      mbar_arrive(bar_sched_full + s);
+      mbar_arrive_cluster(mapa_shared(smem_u32(bar_sched_full + s), 1));
+      if (tile < 0) break;
+    }
   } else if (!skip && warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int wq = warp & 3;
@@ -314,7 +384,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     constexpr int64_t kSlab = static_cast<int64_t>(C::kBN / 4) * 128;
     int tcount = 0;
     PairItem w;
-    for (int i = 0; pair_item(sched, pair, i, &w); ++i, ++tcount) {
+    for (int i = 0; next_item(i, &w, true); ++i, ++tcount) {
       const int buf = tcount & 1;
       const uint32_t use = tcount >> 1;
       if (!mbar_wait_warp(bar_acc_full + buf, use & 1, abort_flag, kDevTimeoutAcc)) break;
@@ -412,6 +482,9 @@ struct PairChoice {
   int tiles;
   bool stream_k;
 };
+
+// Whole tiles with more tiles than resident pairs take the dynamic schedule.
+static bool pair_dynamic(const PairChoice& c) { return FAB_GEMM_DYNAMIC != 0 && !c.stream_k && c.tiles > c.pairs; }
 
 static long long pair_tiles(const GemmLaunch& L, int bn) {
   return static_cast<long long>((L.M + 255) / 256) * ((L.N + bn - 1) / bn);
@@ -521,15 +594,20 @@ static int launch_gemm_pair_w(const GemmLaunch& L, const PairChoice& c, cudaStre
   kp.sk_dp_tiles = c.tiles;
   kp.sk_part = nullptr;
   kp.sk_flags = nullptr;
+  kp.dyn_sched = 0;
   if (c.tiles <= 0) return 0;
   if (c.pairs < 1) return kErrLaunch;
+  int clusters = c.pairs;
   if (c.stream_k) {
     uint8_t* ws = static_cast<uint8_t*>(L.workspace);
     kp.sk_dp_tiles = c.dp_tiles;
     kp.sk_flags = reinterpret_cast<int*>(ws);
     kp.sk_part = reinterpret_cast<float*>(ws + pair_sk_flag_bytes(c.pairs));
+  } else if (pair_dynamic(c)) {
+    kp.dyn_sched = 1;
+    clusters = c.tiles;
   }
-  kern<<<2 * c.pairs, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
+  kern<<<2 * clusters, C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }
 

@@ -261,6 +261,7 @@ static int launch_gemm_splitk_k(const GemmLaunch& L, cudaStream_t stream) {
   kp.sk_dp_tiles = 0;
   kp.sk_part = nullptr;
   kp.sk_flags = nullptr;
+  kp.dyn_sched = 0;
   const long long tiles = static_cast<long long>((L.M + C::kBM - 1) / C::kBM) * ((L.N + C::kBN - 1) / C::kBN);
   kern<<<static_cast<unsigned>(tiles * kSplit), C::kThreads, C::kSmemBytes, stream>>>(kp, ta, tb);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;

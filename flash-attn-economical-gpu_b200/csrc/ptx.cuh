@@ -27,6 +27,7 @@ enum DeviceError : int {
   kDevTimeoutPeerTile = 9,   // a tile's partial sums from every rank never all arrived
   kDevTimeoutPeerDone = 10,  // the reduced tiles from every owner never all arrived
   kDevTimeoutPartial = 11,   // a stream-K partial tile from another CTA pair never arrived
+  kDevTimeoutSched = 12,     // the next tile from the cluster scheduler, or its slot's release, never came
 };
 
 // Device-global status word of the kernels of one translation unit (internal
@@ -359,6 +360,75 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, fl
 // Arrive on an mbarrier of any CTA of the cluster (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 4-byte store into the shared memory of any CTA of the cluster; published to
+// that CTA by a later mbar_arrive_cluster (release at cluster scope) on a
+// barrier it waits on with mbar_wait_cluster.
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// mbar_wait with acquire at cluster scope: for phases completed by arrivals
+// (and stores before them) from the other CTA of the cluster.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 63u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > g_fab_wait_limit_ns) {
+        record_device_error(code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------ cluster launch control ---
+// Ask the hardware scheduler to cancel one cluster of this grid that has not
+// started yet and hand its work to the caller.  The 16-byte response lands in
+// `resp` (shared::cta, 16-byte aligned) and completes 16 transaction bytes on
+// `bar`, whose phase the caller armed with mbar_arrive_expect_tx(bar, 16).
+// One thread per cluster issues it; the response must land before the CTA
+// exits.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint64_t* bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(resp),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+// The x index of the first CTA of the cancelled cluster, or -1 when the
+// request failed (no cluster was left to cancel).
+__device__ __forceinline__ int clc_first_cta_x(uint32_t resp) {
+  uint32_t ok, x;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 h;\n\t"
+      "ld.shared.b128 h, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, h;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "mov.u32 %1, 0;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, h;\n\t}"
+      : "=r"(ok), "=r"(x)
+      : "r"(resp)
+      : "memory");
+  return ok ? static_cast<int>(x) : -1;
 }
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
