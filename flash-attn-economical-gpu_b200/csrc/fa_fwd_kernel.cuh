@@ -213,13 +213,17 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 // CTA counts itself in split_cnt[blockIdx.x] once its 128 softmax threads
 // have stored; the last to arrive merges the group's rows:
 // O = sum_s w_s O_s / sum_s w_s and LSE = max + log(sum_s w_s), with
-// w_s = exp(LSE_s - max) (zero for an empty split), one warp per row and the
-// head dim across the lanes, and sets the counter back to zero for the next
-// call.  Called by the four softmax warps of a one-query-tile CTA on every
-// path (the named barrier has no time limit).
+// w_s = exp(LSE_s - max) (zero for an empty split), and sets the counter back
+// to zero for the next call.  The group's rows are consecutive in o_part, so
+// the merge runs over all 128 threads in row chunks: the chunk's LSEs into
+// `scratch` (the idle K/V ring), per-row max and weights there, then each
+// thread sums 4-column pieces of O (single columns for head dims that are
+// not a multiple of 4) over the splits in split order, eight splits' loads in
+// flight at a time.  Called by the four softmax warps of a
+// one-query-tile CTA on every path (the named barriers have no time limit).
 template <typename T>
 __device__ __forceinline__ void split_merge(const FaKernelParams& p, int m0, int b, int h, int wq, int lane,
-                                            uint32_t* merge_flag) {
+                                            uint32_t* merge_flag, float* scratch, int scratch_floats) {
   __threadfence();  // this thread's partial row, visible GPU-wide before the count
   named_barrier_sync(1, 128);
   if (wq == 0 && lane == 0) {
@@ -229,50 +233,90 @@ __device__ __forceinline__ void split_merge(const FaKernelParams& p, int m0, int
   named_barrier_sync(1, 128);
   if (*reinterpret_cast<volatile uint32_t*>(merge_flag) == 0) return;
   __threadfence();
-  constexpr int kMaxPerLane = 8;  // head dims up to 256
+  const int tid = wq * 32 + lane;
   const int splits = static_cast<int>(gridDim.y);
   const int64_t split_rows = static_cast<int64_t>(p.B) * p.Hq * p.Mq;
-  for (int rr = wq; rr < 128; rr += 4) {
-    const int row = m0 + rr;
-    if (row >= p.M) break;
-    const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
-    const int qpos = p.pack_gqa ? row % p.Mq : row;
-    const int64_t r0 = static_cast<int64_t>(b) * p.Hq * p.Mq + static_cast<int64_t>(oh) * p.Mq + qpos;
-    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm;
-    float* lse = p.lse != nullptr ? p.lse + b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm : nullptr;
-    float mx = -INFINITY;
-    for (int sp = lane; sp < splits; sp += 32) mx = fmaxf(mx, __ldcg(p.lse_part + sp * split_rows + r0));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (mx == -INFINITY) {
-      // No split saw a key: 0/0 like the single-pass kernel.
-      for (int d = lane; d < p.D; d += 32) orow[d] = static_cast<T>(NAN);
-      if (lse != nullptr && lane == 0) *lse = -INFINITY;
-      continue;
+  // o_part / lse_part row of group row 0: rows m0.. of one (batch, head) or,
+  // packed, of the query heads sharing key/value head h -- consecutive.
+  const int64_t row_base = static_cast<int64_t>(b) * p.Hq * p.Mq +
+                           (p.pack_gqa ? static_cast<int64_t>(h) * p.group * p.Mq : static_cast<int64_t>(h) * p.Mq) + m0;
+  const int nrows = min(128, p.M - m0);
+  const bool vec4 = (p.D & 3) == 0;  // o_part rows are then 16-byte aligned
+  // Per chunk row: splits weights, then max and 1/sum.
+  const int chunk = min(nrows, scratch_floats / (splits + 2));
+  float* wsc = scratch;
+  for (int r0 = 0; r0 < nrows; r0 += chunk) {
+    const int nr = min(chunk, nrows - r0);
+    float* rmax = wsc + splits * nr;
+    float* rinv = rmax + nr;
+    for (int idx = tid; idx < splits * nr; idx += 128) {
+      const int sp = idx / nr, rr = idx - sp * nr;
+      wsc[idx] = __ldcg(p.lse_part + sp * split_rows + row_base + r0 + rr);
     }
-    float acc[kMaxPerLane];
-#pragma unroll
-    for (int e = 0; e < kMaxPerLane; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
-#pragma unroll 4
-    for (int sp = 0; sp < splits; ++sp) {
-      const float ls = __ldcg(p.lse_part + sp * split_rows + r0);
-      const float w = ls == -INFINITY ? 0.f : expf(ls - mx);  // an empty split carries zeros
-      wsum += w;
-      const float* src = p.o_part + (sp * split_rows + r0) * p.D;
-#pragma unroll
-      for (int e = 0; e < kMaxPerLane; ++e) {
-        const int d = lane + 32 * e;
-        if (d < p.D) acc[e] = fmaf(w, __ldcg(src + d), acc[e]);
+    named_barrier_sync(1, 128);
+    for (int rr = tid; rr < nr; rr += 128) {
+      float mx = -INFINITY;
+      for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, wsc[sp * nr + rr]);
+      float wsum = 0.f;
+      if (mx != -INFINITY) {
+        for (int sp = 0; sp < splits; ++sp) {
+          const float ls = wsc[sp * nr + rr];
+          const float w = ls == -INFINITY ? 0.f : expf(ls - mx);  // an empty split carries zeros
+          wsc[sp * nr + rr] = w;
+          wsum += w;
+        }
       }
+      rmax[rr] = mx;
+      rinv[rr] = 1.f / wsum;
+      const int row = m0 + r0 + rr;
+      const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
+      const int qpos = p.pack_gqa ? row % p.Mq : row;
+      if (p.lse != nullptr)
+        p.lse[b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm] =
+            mx == -INFINITY ? -INFINITY : mx + logf(wsum);
     }
-    const float inv = 1.f / wsum;
+    named_barrier_sync(1, 128);
+    // Units of 4 columns (float4) when the head dim allows, else single columns.
+    const int uw = vec4 ? 4 : 1;
+    const int upr = p.D / uw;  // units per row
+    for (int u = tid; u < nr * upr; u += 128) {
+      const int rr = u / upr, c0 = (u - rr * upr) * uw;
+      const int row = m0 + r0 + rr;
+      const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
+      const int qpos = p.pack_gqa ? row % p.Mq : row;
+      T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm + c0;
+      if (rmax[rr] == -INFINITY) {
+        // No split saw a key: 0/0 like the single-pass kernel.
+        for (int e = 0; e < uw; ++e) orow[e] = static_cast<T>(NAN);
+        continue;
+      }
+      const float* src = p.o_part + (row_base + r0 + rr) * p.D + c0;
+      const int64_t sstride = split_rows * p.D;  // floats between splits
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int sp0 = 0; sp0 < splits; sp0 += 8) {
+        float4 x[8];
 #pragma unroll
-    for (int e = 0; e < kMaxPerLane; ++e) {
-      const int d = lane + 32 * e;
-      if (d < p.D) orow[d] = static_cast<T>(acc[e] * inv);
+        for (int k = 0; k < 8; ++k) {
+          if (sp0 + k < splits) {
+            const float* q = src + (sp0 + k) * sstride;
+            x[k] = vec4 ? __ldcg(reinterpret_cast<const float4*>(q)) : make_float4(__ldcg(q), 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (sp0 + k < splits) {
+            const float w = wsc[(sp0 + k) * nr + rr];
+            acc[0] = fmaf(w, x[k].x, acc[0]);
+            acc[1] = fmaf(w, x[k].y, acc[1]);
+            acc[2] = fmaf(w, x[k].z, acc[2]);
+            acc[3] = fmaf(w, x[k].w, acc[3]);
+          }
+        }
+      }
+      const float inv = rinv[rr];
+      for (int e = 0; e < uw; ++e) orow[e] = static_cast<T>(acc[e] * inv);
     }
-    if (lse != nullptr && lane == 0) *lse = mx + logf(wsum);
+    named_barrier_sync(1, 128);  // the next chunk reuses the scratch
   }
   if (wq == 0 && lane == 0) p.split_cnt[blockIdx.x] = 0u;
 }
@@ -879,7 +923,11 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
       if (lse_out != nullptr) *lse_out = kNegInf;
     }
     if constexpr (kNQ == 1) {
-      if (p.split_cnt != nullptr) split_merge<T>(p, m0, b, h, wq, lane, tmem_slot + 2);
+      // The K/V ring is idle here: every tile it held was consumed by
+      // products that completed before O was final.
+      if (p.split_cnt != nullptr)
+        split_merge<T>(p, m0, b, h, wq, lane, tmem_slot + 2, reinterpret_cast<float*>(sKV),
+                       kRing * C::kKVTileBytes / 4);
     }
   }
   }
