@@ -762,8 +762,12 @@ def run_gemm(args, world, rank, local):
         for _ in range(3):
             cublas()
         torch.cuda.synchronize(dev)
-        ms = timed_steps(cublas, 10)
-        comparators["torch_matmul_cublas_tflops"] = round(flops * 10 / (ms / 1e3) / 1e12, 1)
+        # As many calls as the timed region (at least 10), so a long run compares both under the power cap.
+        n_cmp = max(10, args.steps)
+        with ClockSampler(local) as cmp_clocks:
+            ms = timed_steps(cublas, n_cmp)
+        comparators["torch_matmul_cublas_tflops"] = round(flops * n_cmp / (ms / 1e3) / 1e12, 1)
+        comparators["torch_matmul_cublas_clocks"] = cmp_clocks.summary()
     return {
         "metric": METRIC,
         "value": round(value, 1),
