@@ -106,7 +106,7 @@ struct FaCfg {
   static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                     : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kNumBars = kNQ + 2 * kRing + 3 * kSlots + kNQ + 1;
+  static constexpr int kNumBars = kNQ + 2 * kRing + 3 * kSlots + kNQ + 2;
   static constexpr int kDataBytes = kNQ * kQTileBytes + kRing * kKVTileBytes;
   // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
   // ring tiles 2j+1 .. 2j+4 are resident together.
@@ -223,7 +223,8 @@ __device__ __forceinline__ void store_o_chunk(T* dst, const float (&v)[32], int 
 // one-query-tile CTA on every path (the named barriers have no time limit).
 template <typename T>
 __device__ __forceinline__ void split_merge(const FaKernelParams& p, int m0, int b, int h, int wq, int lane,
-                                            uint32_t* merge_flag, float* scratch, int scratch_floats) {
+                                            uint32_t* merge_flag, float* scratch, int scratch_floats,
+                                            uint64_t* bar, volatile int* abort_flag) {
   __threadfence();  // this thread's partial row, visible GPU-wide before the count
   named_barrier_sync(1, 128);
   if (wq == 0 && lane == 0) {
@@ -242,6 +243,85 @@ __device__ __forceinline__ void split_merge(const FaKernelParams& p, int m0, int
                            (p.pack_gqa ? static_cast<int64_t>(h) * p.group * p.Mq : static_cast<int64_t>(h) * p.Mq) + m0;
   const int nrows = min(128, p.M - m0);
   const bool vec4 = (p.D & 3) == 0;  // o_part rows are then 16-byte aligned
+  // Staged: per chunk of rows, every split's partial rows are bulk-copied
+  // into the scratch at once (one round trip instead of one per eight
+  // splits), then summed from shared memory.  Per chunk row: splits x D
+  // partial values, splits weights, its max and 1/sum.
+  const int staged_rows = vec4 ? min(nrows, scratch_floats / (splits * (p.D + 1) + 2)) : 0;
+  if (staged_rows > 0) {
+    uint32_t phase = 0;
+    for (int r0 = 0; r0 < nrows; r0 += staged_rows, phase ^= 1u) {
+      const int nr = min(staged_rows, nrows - r0);
+      float* part = scratch;                    // [splits][nr][D]
+      float* wsc = part + splits * nr * p.D;    // [splits][nr]
+      float* rmax = wsc + splits * nr;
+      float* rinv = rmax + nr;
+      if (tid == 0) {
+        fence_proxy_async_global();  // the other CTAs' rows, seen through the counter, before the copies
+        fence_proxy_async_smem();    // this CTA's earlier reads of the scratch, before the copies overwrite it
+        const uint32_t bytes = static_cast<uint32_t>(nr * p.D * 4);
+        mbar_arrive_expect_tx(bar, bytes * static_cast<uint32_t>(splits));
+        for (int sp = 0; sp < splits; ++sp)
+          bulk_load_g2s(part + sp * nr * p.D, p.o_part + (sp * split_rows + row_base + r0) * p.D, bytes, bar);
+      }
+      for (int idx = tid; idx < splits * nr; idx += 128) {
+        const int sp = idx / nr, rr = idx - sp * nr;
+        wsc[idx] = __ldcg(p.lse_part + sp * split_rows + row_base + r0 + rr);
+      }
+      named_barrier_sync(1, 128);
+      for (int rr = tid; rr < nr; rr += 128) {
+        float mx = -INFINITY;
+        for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, wsc[sp * nr + rr]);
+        float wsum = 0.f;
+        if (mx != -INFINITY) {
+          for (int sp = 0; sp < splits; ++sp) {
+            const float ls = wsc[sp * nr + rr];
+            const float w = ls == -INFINITY ? 0.f : expf(ls - mx);  // an empty split carries zeros
+            wsc[sp * nr + rr] = w;
+            wsum += w;
+          }
+        }
+        rmax[rr] = mx;
+        rinv[rr] = 1.f / wsum;
+        const int row = m0 + r0 + rr;
+        const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
+        const int qpos = p.pack_gqa ? row % p.Mq : row;
+        if (p.lse != nullptr)
+          p.lse[b * p.l_sb + oh * p.l_sh + static_cast<int64_t>(qpos) * p.l_sm] =
+              mx == -INFINITY ? -INFINITY : mx + logf(wsum);
+      }
+      named_barrier_sync(1, 128);
+      const bool got = mbar_wait(bar, phase, abort_flag, kDevTimeoutMerge);
+      const int upr = p.D / 4;
+      for (int u = tid; got && u < nr * upr; u += 128) {
+        const int rr = u / upr, c0 = (u - rr * upr) * 4;
+        const int row = m0 + r0 + rr;
+        const int oh = p.pack_gqa ? h * p.group + row / p.Mq : h;
+        const int qpos = p.pack_gqa ? row % p.Mq : row;
+        T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + oh * p.o_sh + static_cast<int64_t>(qpos) * p.o_sm + c0;
+        if (rmax[rr] == -INFINITY) {
+          for (int e = 0; e < 4; ++e) orow[e] = static_cast<T>(NAN);  // no split saw a key: 0/0
+          continue;
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int sp = 0; sp < splits; ++sp) {
+          const float w = wsc[sp * nr + rr];
+          const float4 x = *reinterpret_cast<const float4*>(part + (sp * nr + rr) * p.D + c0);
+          acc[0] = fmaf(w, x.x, acc[0]);
+          acc[1] = fmaf(w, x.y, acc[1]);
+          acc[2] = fmaf(w, x.z, acc[2]);
+          acc[3] = fmaf(w, x.w, acc[3]);
+        }
+        const float inv = rinv[rr];
+        for (int e = 0; e < 4; ++e) orow[e] = static_cast<T>(acc[e] * inv);
+      }
+      named_barrier_sync(1, 128);  // the next chunk's copies overwrite the scratch
+    }
+    if (wq == 0 && lane == 0) p.split_cnt[blockIdx.x] = 0u;
+    return;
+  }
+  // Otherwise (head dims not a multiple of 4, or too many splits for one row
+  // in the scratch): plain loads, eight splits in flight at a time.
   // Per chunk row: splits weights, then max and 1/sum.
   const int chunk = min(nrows, scratch_floats / (splits + 2));
   float* wsc = scratch;
@@ -344,7 +424,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
   uint64_t* bar_o_done = bar_p_full + C::kSlots; // [kNQ]
   uint64_t* bar_teardown = bar_o_done + kNQ;
   uint64_t* bar_p_half = bar_teardown + 1;        // [kSlots], P of the first half of the keys
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_p_half + C::kSlots);
+  uint64_t* bar_merge = bar_p_half + C::kSlots;   // split-KV merge: partial rows copied in
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_merge + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -407,6 +488,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
     }
     for (int i = 0; i < kNQ; ++i) mbar_init(bar_o_done + i, 1);
     mbar_init(bar_teardown, 1);
+    mbar_init(bar_merge, 1);
     *abort_flag = *reinterpret_cast<volatile int*>(&g_fab_device_error) != 0 ? 1 : 0;
     mbar_fence_init();
   }
@@ -927,7 +1009,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
       // products that completed before O was final.
       if (p.split_cnt != nullptr)
         split_merge<T>(p, m0, b, h, wq, lane, tmem_slot + 2, reinterpret_cast<float*>(sKV),
-                       kRing * C::kKVTileBytes / 4);
+                       kRing * C::kKVTileBytes / 4, bar_merge, abort_flag);
     }
   }
   }
@@ -1356,10 +1438,11 @@ int fa_split_plan(const FaLaunch& L, int num_splits, FaSplitPlan* plan) {
   const int tiles = L.N > 0 ? (L.N + cfg.bn - 1) / cfg.bn : 0;
   int splits = num_splits;
   if (splits <= 0) {
-    // Enough CTAs for one per SM.
+    // As many splits as keep every CTA in one wave (at most one per SM): a
+    // few CTAs past the wave would run their whole range after it.
     const int sms = num_sms();
     if (sms <= 0) return kErrCuda;
-    splits = static_cast<int>((static_cast<long long>(per_sm) * sms + base_ctas - 1) / (base_ctas > 0 ? base_ctas : 1));
+    splits = static_cast<int>(static_cast<long long>(per_sm) * sms / (base_ctas > 0 ? base_ctas : 1));
   }
   splits = std::max(1, std::min({splits, std::max(tiles, 1), 65535}));
   const int tiles_per_split = tiles > 0 ? (tiles + splits - 1) / splits : 1;

@@ -28,6 +28,7 @@ enum DeviceError : int {
   kDevTimeoutPeerDone = 10,  // the reduced tiles from every owner never all arrived
   kDevTimeoutPartial = 11,   // a stream-K partial tile from another CTA pair never arrived
   kDevTimeoutSched = 12,     // the next tile from the cluster scheduler, or its slot's release, never came
+  kDevTimeoutMerge = 13,     // the split-KV merge's copies of the partial rows never landed
 };
 
 // Device-global status word of the kernels of one translation unit (internal
@@ -138,6 +139,20 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Orders this thread's view of global memory (generic proxy: e.g. data other
+// CTAs published before an atomic this thread observed) before its later
+// bulk copies (async proxy) read it.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Contiguous bulk copy global -> this CTA's shared memory (no tensor map):
+// both addresses 16-byte aligned, bytes a multiple of 16; completes `bytes`
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // ------------------------------------------------- cross-GPU signalling ---
 // Counters in (possibly peer) global memory, ordered at system scope so that

@@ -161,8 +161,8 @@ int fab_attention_fwd_varlen(const fab_attention_varlen_params* params, void* st
  * replacement to decode-shaped calls).  Same parameters, same results within
  * fp32 rounding of the merge.
  *
- * The keys are cut into num_splits ranges (num_splits <= 0: enough ranges for
- * one CTA per SM).  Each range's attention (normalised O in fp32 and its LSE)
+ * The keys are cut into num_splits ranges (num_splits <= 0: as many ranges as
+ * keep the CTAs in one wave, at most one per SM).  Each range's attention (normalised O in fp32 and its LSE)
  * goes to the workspace; the last range of each row group to finish merges
  * the group into o (and lse, when not NULL) with weights exp(LSE_split - LSE),
  * inside the same kernel, found through one arrival counter per row group.  When the query heads of a

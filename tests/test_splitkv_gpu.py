@@ -76,7 +76,7 @@ def test_splitkv_matches_oracle(shape, dtype, causal, splits, cuda_device):
 def test_split_count_reported_and_respected(cuda_device):
     need, used = splitkv_workspace_bytes((1, 28, 1, 128), (1, 4, 32768, 128), torch.bfloat16, num_splits=0)
     sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
-    assert used == -(-sms // 4)  # four packed key/value heads, one CTA per SM
+    assert used == sms // 4  # four packed key/value heads, at most one CTA per SM, one wave
     assert need > 0
     need1, used1 = splitkv_workspace_bytes((1, 28, 1, 128), (1, 4, 32768, 128), torch.bfloat16, num_splits=1)
     assert (need1, used1) == (0, 1)
