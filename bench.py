@@ -244,6 +244,11 @@ def setup_dist(args):
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
+            # NCCL's communicator set-up lines (ranks, devices, transports) on stderr, so the run records which
+            # ranks joined; stdout keeps rank 0's one JSON line.
+            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
@@ -871,6 +876,7 @@ def main():
             print(json.dumps(result), flush=True)
         return
     world, rank, local = setup_dist(args)
+    result = None
     try:
         if gemm_shape(args.workload) is not None:
             result = run_gemm(args, world, rank, local)
@@ -883,14 +889,15 @@ def main():
                 ttft_result = run_ttft(args, world, rank, local)
                 if result is not None:
                     result["ttft"] = ttft_result
-        if rank == 0 and result is not None:
-            print(json.dumps(result), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist
 
             if dist.is_initialized():
                 dist.destroy_process_group()
+    # After the process group is gone, so the JSON line is the last thing rank 0 writes.
+    if rank == 0 and result is not None:
+        print(json.dumps(result), flush=True)
 
 
 if __name__ == "__main__":
