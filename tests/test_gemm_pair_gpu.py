@@ -97,3 +97,48 @@ def test_pair_leading_dimensions(cuda_device):
 def test_pair_deterministic(cuda_device):
     a, b = _inputs(3000, 3072, 704, torch.bfloat16, cuda_device, seed=21)
     assert torch.equal(matmul(a, b), matmul(a, b))
+
+
+# ------------------------------------------------ dynamic tile order (cluster launch control)
+def test_dynamic_order_launches_one_cluster_per_tile(cuda_device):
+    """Whole-tile launches with more tiles than resident pairs start one two-CTA cluster per tile; running
+    clusters take the tiles of clusters that have not started.  Every tile is computed exactly once."""
+    import mma
+
+    M, N, K = 4096, 4096, 1024
+    assert mma.kernel_plan(M, N, K, torch.bfloat16)[0] == "pair"
+    assert mma.kernel_grid(M, N, K) == 2 * _pair_tiles(M, N)
+    a, b = _inputs(M, N, K, torch.bfloat16, cuda_device, seed=41)
+    c = matmul(a, b)
+    torch.testing.assert_close(c.float(), (a.float() @ b.float()).to(torch.bfloat16).float(), rtol=RTOL, atol=ATOL)
+    assert torch.equal(c, matmul(a, b))  # the tile order never changes a tile's sums
+
+
+def test_dynamic_order_on_two_streams_and_in_a_graph(cuda_device):
+    """Two launches in flight at once on different streams, and graph replays: the scheduler keeps no state
+    outside the launch, so neither interferes with the other."""
+    shapes = [(3000, 2800, 700), (2048, 5120, 512)]
+    ins = [_inputs(M, N, K, torch.bfloat16, cuda_device, seed=50 + i) for i, (M, N, K) in enumerate(shapes)]
+    want = [matmul(a, b) for a, b in ins]
+    streams = [torch.cuda.Stream(cuda_device) for _ in shapes]
+    outs = [None, None]
+    torch.cuda.synchronize()
+    for _ in range(3):
+        for i, st in enumerate(streams):
+            with torch.cuda.stream(st):
+                outs[i] = matmul(*ins[i])
+        torch.cuda.synchronize()
+        for o, w in zip(outs, want):
+            assert torch.equal(o, w)
+    side = torch.cuda.Stream(cuda_device)
+    side.wait_stream(torch.cuda.current_stream(cuda_device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph):
+            g_out = matmul(*ins[0])
+    torch.cuda.current_stream(cuda_device).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(g_out, want[0])
+    graph.reset()
