@@ -267,6 +267,21 @@ def host_lead(ms=3.0):
         sleep(int(ms * 1e-3 * 1.965e9))
 
 
+def warm_up(fn, count: int, min_s: float = 0.02) -> None:
+    """`count` untimed calls, then more until `min_s` of wall time has passed (synchronised), so that a short
+    kernel's timed calls do not follow a fraction of a millisecond of work; every timed leg, ours and each
+    comparator, warms this way.  Warming much longer (0.1-0.3 s back to back) runs the timed calls under the
+    power cap instead (1.5-1.9 GHz on B200)."""
+    for _ in range(count):
+        fn()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < min_s:
+        for _ in range(4):
+            fn()
+        torch.cuda.synchronize()
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -377,9 +392,13 @@ def run_attention(args, world, rank, local):
     flops = attention_flops(B, Hq, S, D, causal)
     stream = torch.cuda.current_stream(dev)
 
-    for i in range(args.warmup):
-        attention_forward(*sets[i % len(sets)], causal=causal, out=o)
-    torch.cuda.synchronize(dev)
+    warm_step = [0]
+
+    def warm_call():
+        attention_forward(*sets[warm_step[0] % len(sets)], causal=causal, out=o)
+        warm_step[0] += 1
+
+    warm_up(warm_call, args.warmup)
     if _native.device_error():
         raise RuntimeError("device error during warm-up")
 
@@ -446,9 +465,7 @@ def run_attention(args, world, rank, local):
                 csets = [(qq, kk if rep == 1 else kk.repeat_interleave(rep, dim=1),
                           vv if rep == 1 else vv.repeat_interleave(rep, dim=1)) for qq, kk, vv in sets]
                 with sdpa_kernel([be]):
-                    for i in range(3):
-                        F.scaled_dot_product_attention(*csets[i % len(csets)], is_causal=causal)
-                    torch.cuda.synchronize(dev)
+                    warm_up(lambda: F.scaled_dot_product_attention(*csets[0], is_causal=causal), 3)
                     c0 = torch.cuda.Event(enable_timing=True)
                     c1 = torch.cuda.Event(enable_timing=True)
                     host_lead()
@@ -522,9 +539,7 @@ def run_decode(args, world, rank, local):
     def step(qq):
         return attention_forward_splitkv(qq, k, v, out=o, workspace=ws)
 
-    for _ in range(args.warmup):
-        step(q)
-    torch.cuda.synchronize(dev)
+    warm_up(lambda: step(q), args.warmup)
 
     def graph_of(fn, n):
         """n calls of fn captured as one CUDA graph, the way a decode loop runs them: a step is ~50 us of
@@ -580,9 +595,7 @@ def run_decode(args, world, rank, local):
         for name, be in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
             try:
                 with sdpa_kernel([be]):
-                    for _ in range(3):
-                        F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
-                    torch.cuda.synchronize(dev)
+                    warm_up(lambda: F.scaled_dot_product_attention(q, k, v, enable_gqa=True), 3)
                     cgraph = graph_of(lambda: F.scaled_dot_product_attention(q, k, v, enable_gqa=True), 20)
                     cgraph.replay()
                     torch.cuda.synchronize(dev)
@@ -746,9 +759,16 @@ def run_gemm(args, world, rank, local):
     def ours():
         matmul(a, b)
 
-    for _ in range(args.warmup):
-        ours()
-    torch.cuda.synchronize(dev)
+    def flushed(fn):
+        """A warm-up call the way timed_steps makes it, flush first: on B200 a 2048 x 3584 x 4608 matmul timed
+        in the first loop to follow the flush measured 24 % slower than in later ones."""
+        def call():
+            if flush is not None:
+                flush.zero_()
+            fn()
+        return call
+
+    warm_up(flushed(ours), args.warmup)
     barrier(world)
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clocks:
@@ -764,9 +784,7 @@ def run_gemm(args, world, rank, local):
         def cublas():
             torch.matmul(a, b, out=c)
 
-        for _ in range(3):
-            cublas()
-        torch.cuda.synchronize(dev)
+        warm_up(flushed(cublas), 3)
         # As many calls as the timed region (at least 10), so a long run compares both under the power cap.
         n_cmp = max(10, args.steps)
         with ClockSampler(local) as cmp_clocks:
