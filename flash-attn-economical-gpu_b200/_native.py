@@ -216,10 +216,19 @@ def device_error() -> int:
     return int(code.value)
 
 
+# What each device error code's wait was waiting for (fab_get_device_error, include/fa_b200.h).
+DEVICE_WAITS = {1: "a Q tile's load", 2: "a K/V tile's load", 3: "an S product", 4: "a softmax's P",
+                5: "O's last product", 6: "a free K/V or stage slot", 7: "a GEMM accumulator",
+                8: "the drain at teardown", 9: "a peer rank's partial tile", 10: "a peer owner's reduced tile",
+                11: "a stream-K piece from another CTA pair", 12: "the CTA-pair GEMM's next tile from its scheduler",
+                13: "the split-KV merge's copies"}
+
+
 def raise_on_device_error() -> None:
     code = device_error()
     if code:
-        raise DeviceTimeoutError(f"a kernel gave up on a bounded wait (device error code {code})")
+        what = DEVICE_WAITS.get(code, "unknown wait")
+        raise DeviceTimeoutError(f"a kernel gave up on a bounded wait (device error code {code}: {what})")
 
 
 def dtype_code(dtype) -> int:

@@ -472,7 +472,13 @@ int fab_device_limits_query(int device, fab_device_limits* out);
 /*
  * Reads and clears the device error word of the current device.  *code is 0
  * when no kernel has given up on a bounded wait, else a positive code naming
- * the wait.  Synchronises with the device (call it between launches).
+ * the wait (the first to give up):
+ *    1 a Q tile's load            2 a K/V tile's load       3 an S product
+ *    4 a softmax's P              5 O's last product        6 a free K/V or stage slot
+ *    7 a GEMM accumulator         8 the drain at teardown   9 a peer rank's partial tile
+ *   10 a peer owner's reduced tile                          11 a stream-K piece from another pair
+ *   12 the CTA-pair GEMM's next tile from its scheduler     13 the split-KV merge's copies
+ * Synchronises with the device (call it between launches).
  */
 int fab_get_device_error(int* code);
 
