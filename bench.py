@@ -42,6 +42,18 @@ for _p in (str(PKG), str(ROOT)):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+NCCL_LOG = None
+if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
+    # NCCL reads these when torch first calls into it.  Its communicator set-up lines (ranks, devices,
+    # transports) go to a per-process file that setup_dist copies to stderr once the communicator exists,
+    # so a multi-rank run records which ranks joined while stdout keeps rank 0's one JSON line.
+    import tempfile
+
+    NCCL_LOG = os.path.join(tempfile.gettempdir(), f"bench_nccl_{os.getpid()}.log")
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ["NCCL_DEBUG_FILE"] = NCCL_LOG
+
 import torch  # noqa: E402
 
 METRIC = "FA fwd TFLOPS (% of B200 bf16 peak) vs torch SDPA; Qwen2.5-7B-arch TTFT ms"
@@ -242,14 +254,19 @@ def setup_dist(args):
         import torch.distributed as dist
 
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kwargs = {}
         if backend == "nccl":
             torch.cuda.set_device(local)
-            # NCCL's communicator set-up lines (ranks, devices, transports) on stderr, so the run records which
-            # ranks joined; stdout keeps rank 0's one JSON line.
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            kwargs["device_id"] = torch.device("cuda", local)  # one communicator per rank, made here
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300), **kwargs)
+        dist.barrier()
+        nccl = ".".join(str(x) for x in torch.cuda.nccl.version()) if backend == "nccl" else "-"
+        print(f"[bench] rank {rank} of {world}: {backend} (NCCL {nccl}), device cuda:{local}", file=sys.stderr,
+              flush=True)
+        if NCCL_LOG is not None and os.path.isfile(NCCL_LOG):
+            with open(NCCL_LOG) as f:
+                sys.stderr.write(f.read())
+            sys.stderr.flush()
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return world, rank, local
