@@ -107,7 +107,7 @@ def _launch_attention(
     `entry` picks the C entry point: "basic" / "optimize_shared_mem" /
     "nomask" for the reference-named kernels, "splitkv"
     (`fab_attention_fwd_splitkv`, key splits merged by the last split CTA of
-    each row group; `num_splits` 0 = one CTA per SM) or "general"
+    each row group; `num_splits` 0 = as many splits as keep the grid in one wave) or "general"
     (`fab_attention_fwd`, grouped-query heads) otherwise.  `workspace` (uint8,
     CUDA, zero-filled before its first use; calls leave it zeroed) is used for
     the split partials when it is large enough, else a zeroed one is allocated.
@@ -415,8 +415,8 @@ def attention_forward_splitkv(
     For short query blocks (decode steps, speculative blocks) against long
     key ranges: each range is attended to by its own CTAs, and the last CTA of
     each row group to finish merges the ranges by their LSE.  `num_splits` 0
-    gives one CTA per SM.  A caller-supplied `workspace` must be zero-filled
-    before its first use (every call leaves its counters at zero again).
+    gives as many splits as keep the grid in one wave (at most one CTA per
+    SM).  A caller-supplied `workspace` must be zero-filled before its first use (every call leaves its counters at zero again).
     Query heads that share a key/value head are packed into one query tile
     when q is laid out [batch, head, seq, dim] contiguously (or seq == 1).
     """

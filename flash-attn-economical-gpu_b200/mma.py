@@ -5,10 +5,10 @@ BLOCK_K=..., GROUP_M=..., USE_CACHE_EVICTION_HINTS=..., num_warps=...,
 num_stages=...)` keeps the Triton kernel's call form (mma.py:8-21) and
 result: C = A B over row-major contiguous storage with fp32 accumulation,
 rounded to fp16 and then stored in C's dtype (mma.py:51-52).  It runs the
-persistent sm_100a tcgen05 GEMM through the C ABI (`fab_matmul_contiguous`),
-which picks the kernel: 16-bit problems of at least one wave of 256x256 tiles
-run on CTA pairs (tcgen05 cta_group::2, one tile per two SMs), the rest on one
-CTA per 128x256 tile;
+sm_100a tcgen05 GEMM through the C ABI (`fab_matmul_contiguous`), which picks
+the kernel: 16-bit problems of at least one wave of 256x256 tiles run on CTA
+pairs (tcgen05 cta_group::2, one tile per two SMs, tiles handed out in raster
+order by cluster launch control), the rest on one CTA per 128x256 tile;
 the Triton tiling keywords (BLOCK_*, GROUP_M, cache hints, num_warps,
 num_stages) are accepted and not needed.  `_select_2d_contiguous_config` accepts and
 rejects exactly the shapes the reference accepts and rejects (mma.py:63-81)
