@@ -416,7 +416,8 @@ def attention_forward_splitkv(
     key ranges: each range is attended to by its own CTAs, and the last CTA of
     each row group to finish merges the ranges by their LSE.  `num_splits` 0
     gives as many splits as keep the grid in one wave (at most one CTA per
-    SM).  A caller-supplied `workspace` must be zero-filled before its first use (every call leaves its counters at zero again).
+    SM).  A caller-supplied `workspace` must be zero-filled before its first
+    use (every call leaves its counters at zero again).
     Query heads that share a key/value head are packed into one query tile
     when q is laid out [batch, head, seq, dim] contiguously (or seq == 1).
     """
