@@ -43,10 +43,11 @@ for _p in (str(PKG), str(ROOT)):
         sys.path.insert(0, _p)
 
 NCCL_LOG = None
-if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
-    # NCCL reads these when torch first calls into it.  Its communicator set-up lines (ranks, devices,
-    # transports) go to a per-process file that setup_dist copies to stderr once the communicator exists,
-    # so a multi-rank run records which ranks joined while stdout keeps rank 0's one JSON line.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1 and os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+    # NCCL reads these when torch first calls into it (the GPU boxes preset NCCL_DEBUG=VERSION, which prints
+    # only the version).  Its communicator set-up lines (ranks, devices, transports) go to a per-process file
+    # that setup_dist copies to stderr once the communicator exists, so a multi-rank run records which ranks
+    # joined while stdout keeps rank 0's one JSON line.
     import tempfile
 
     NCCL_LOG = os.path.join(tempfile.gettempdir(), f"bench_nccl_{os.getpid()}.log")
