@@ -69,6 +69,13 @@ constexpr bool kWarpMma = FAB_FA_WARP_MMA != 0;
 #endif
 constexpr bool kPHalves = FAB_FA_P_HALVES != 0;
 
+// 1 (with P halves): a third release after three quarters of the keys, so the
+// P*V left after the last release covers a quarter of the tile.
+#ifndef FAB_FA_P_3Q
+#define FAB_FA_P_3Q 0
+#endif
+constexpr bool kP3Q = kPHalves && FAB_FA_P_3Q != 0;
+
 namespace fab {
 
 // Test hook (fab_debug_starve_kv_load): the producer of every CTA skips the
@@ -106,7 +113,7 @@ struct FaCfg {
   static constexpr int kTmemUsed = kSlots * kBN + kNQ * kDP;
   static constexpr int kTmemAlloc = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
                                     : kTmemUsed <= 256 ? 256 : 512;
-  static constexpr int kNumBars = kNQ + 2 * kRing + 3 * kSlots + kNQ + 2;
+  static constexpr int kNumBars = kNQ + 2 * kRing + 4 * kSlots + kNQ + 2;
   static constexpr int kDataBytes = kNQ * kQTileBytes + kRing * kKVTileBytes;
   // With two S buffers the MMA thread holds V_j while it waits for K_{j+2}:
   // ring tiles 2j+1 .. 2j+4 are resident together.
@@ -424,7 +431,8 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
   uint64_t* bar_o_done = bar_p_full + C::kSlots; // [kNQ]
   uint64_t* bar_teardown = bar_o_done + kNQ;
   uint64_t* bar_p_half = bar_teardown + 1;        // [kSlots], P of the first half of the keys
-  uint64_t* bar_merge = bar_p_half + C::kSlots;   // split-KV merge: partial rows copied in
+  uint64_t* bar_p_3q = bar_p_half + C::kSlots;    // [kSlots], P of three quarters of the keys
+  uint64_t* bar_merge = bar_p_3q + C::kSlots;     // split-KV merge: partial rows copied in
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_merge + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -485,6 +493,7 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
       mbar_init(bar_s_full + x, 1);
       mbar_init(bar_p_full + x, 4);  // one arrival per softmax warp
       mbar_init(bar_p_half + x, 4);
+      mbar_init(bar_p_3q + x, 4);
     }
     for (int i = 0; i < kNQ; ++i) mbar_init(bar_o_done + i, 1);
     mbar_init(bar_teardown, 1);
@@ -701,9 +710,19 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
             if (!(ok = wait(bar_p_half + slot, j & 1, kDevTimeoutP))) break;
             tc_fence_after();
             issue_pv(i, slot, s, j > 0, 0, kHalf);
-            if (!(ok = wait(bar_p_full + slot, j & 1, kDevTimeoutP))) break;
-            tc_fence_after();
-            issue_pv(i, slot, s, true, kHalf, 2 * kHalf);
+            if constexpr (kP3Q) {
+              constexpr int k3q = 3 * kBN / C::kKInstr / 4;
+              if (!(ok = wait(bar_p_3q + slot, j & 1, kDevTimeoutP))) break;
+              tc_fence_after();
+              issue_pv(i, slot, s, true, kHalf, k3q);
+              if (!(ok = wait(bar_p_full + slot, j & 1, kDevTimeoutP))) break;
+              tc_fence_after();
+              issue_pv(i, slot, s, true, k3q, 2 * kHalf);
+            } else {
+              if (!(ok = wait(bar_p_full + slot, j & 1, kDevTimeoutP))) break;
+              tc_fence_after();
+              issue_pv(i, slot, s, true, kHalf, 2 * kHalf);
+            }
           } else {
             if (!(ok = wait(bar_p_full + slot, j & 1, kDevTimeoutP))) break;
             tc_fence_after();
@@ -860,6 +879,14 @@ __global__ void __launch_bounds__(128 + kNQ * 128, (kNQ == 1 && kSB == 1) ? 2 : 
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_p_half + slot);
+          }
+          if constexpr (kP3Q) {
+            if (cc == 3 * kBN / 128) {
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar_p_3q + slot);
+            }
           }
         }
         if constexpr (sizeof(T) == 2) {
