@@ -70,9 +70,13 @@ constexpr bool kWarpMma = FAB_FA_WARP_MMA != 0;
 constexpr bool kPHalves = FAB_FA_P_HALVES != 0;
 
 // 1 (with P halves): a third release after three quarters of the keys, so the
-// P*V left after the last release covers a quarter of the tile.
+// P*V left after the last release covers a quarter of the tile.  Measured on
+// B200 in two sets of three interleaved rounds against halves only: +0.7 and
+// +3.9 % at B4 H32 S8192 D128, +1.0 / +2.1 % at S4096, +3.4 / +2.0 % at
+// S2048, +3.6 / +3.1 % at D64; short causal shapes and Qwen2.5-7B's GQA
+// prefill within +-2.5 % either way.
 #ifndef FAB_FA_P_3Q
-#define FAB_FA_P_3Q 0
+#define FAB_FA_P_3Q 1
 #endif
 constexpr bool kP3Q = kPHalves && FAB_FA_P_3Q != 0;
 
